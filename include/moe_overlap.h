@@ -1,0 +1,140 @@
+/*
+ * moe_overlap.h - C ABI of the B200 (sm_100a) MoE expert hot path.
+ *
+ * Every entry point takes plain device pointers, element counts/strides and a
+ * CUDA stream handle (cudaStream_t passed as void*; NULL = legacy default
+ * stream).  Nothing here allocates device memory except where stated; all
+ * work is enqueued asynchronously on `stream` and the functions return as soon
+ * as it is queued.
+ *
+ * Return value: MOE_OK (0) or one of the MOE_ERR_* codes below for argument
+ * or launch errors found on the host.  Errors found on the device while a
+ * kernel runs (bounded wait expired, offsets out of range) are written to the
+ * optional `status` word (int32, device memory or mapped pinned host memory,
+ * zero-initialised by the caller); a nonzero value there is one of the same
+ * codes.
+ */
+#ifndef MOE_OVERLAP_H_
+#define MOE_OVERLAP_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status -- */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARG 1  /* bad shape / dtype / pointer / alignment   */
+#define MOE_ERR_CUDA 2         /* a CUDA runtime/driver call failed         */
+#define MOE_ERR_TIMEOUT 3      /* a bounded device-side wait ran out        */
+#define MOE_ERR_OFFSETS 4      /* expert_offsets point outside [0, m_total] */
+#define MOE_ERR_UNSUPPORTED 5  /* device is not sm_100 / feature missing    */
+#define MOE_ERR_CAPACITY 6     /* a fixed-capacity buffer would overflow    */
+
+/* ----------------------------------------------------------------- dtypes -- */
+#define MOE_DTYPE_BF16 0
+#define MOE_DTYPE_F16 1
+
+/* ------------------------------------------------------------ activations -- */
+#define MOE_ACT_NONE 0
+#define MOE_ACT_GELU 1 /* exact GELU, 0.5*x*(1+erf(x/sqrt(2))), on the fp32 accumulator */
+
+/* Human-readable text for a status code (static storage). */
+MOE_API const char* moe_status_string(int32_t code);
+
+/* ABI version of this library, MOE_ABI_VERSION. */
+#define MOE_ABI_VERSION 1
+MOE_API int32_t moe_abi_version(void);
+
+/*
+ * Grouped GEMM over ragged expert segments.
+ *
+ * Replaces persistent_grouped_gemm (src/triton_grouped_gemm.py:326-443) and
+ * the two Triton kernels it launches (_persistent_grouped_gemm_kernel_striped,
+ * :101-154, and _persistent_grouped_gemm_kernel_atomic, :157-233), including
+ * the work list that _build_work_queue (:240-297) builds on the host side:
+ * here the tile list is derived on the device from expert_offsets.
+ *
+ * For every expert e in [0, num_experts):
+ *   C[off[e]:off[e+1], :] = act( A[off[e]:off[e+1], :] @ B[e] )
+ * with fp32 accumulation and the result rounded to `dtype`.  Rows outside
+ * every expert segment are left untouched, except that when no expert has a
+ * row at all, the whole of C is zero-filled (src/triton_grouped_gemm.py:369-371).
+ *
+ *   a               A, m_total x k, row stride lda elements, unit column stride
+ *   b               B, num_experts x k x n; element (e,kk,nn) at
+ *                   b + e*b_stride_e + kk*b_stride_k + nn*b_stride_n.
+ *                   Either b_stride_n == 1 (N-major, the reference layout) or
+ *                   b_stride_k == 1 (K-major, i.e. a transposed weight view).
+ *   c               C, m_total x n, row stride ldc elements
+ *   expert_offsets  num_experts+1 ints (int32, or int64 if offsets_int64)
+ *   dtype           MOE_DTYPE_BF16 or MOE_DTYPE_F16 (A, B and C share it)
+ *   activation      MOE_ACT_NONE or MOE_ACT_GELU
+ *   num_sms         persistent grid size (clamped to the device's SM count)
+ *   use_atomic_queue 0: tiles striped over the grid; 1: dynamic tile queue
+ *   work_counter    int32 device scratch word for the dynamic queue; required
+ *                   when use_atomic_queue != 0, zeroed on `stream` by this call
+ *   status          optional device-visible int32 error word (may be NULL)
+ *   stream          cudaStream_t
+ *
+ * Alignment: a, b, c 16-byte aligned; lda, ldc and the non-unit B strides
+ * multiples of 8 elements; k and n multiples of 8.
+ */
+MOE_API int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int64_t b_stride_e,
+                         int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                         const void* expert_offsets, int32_t offsets_int64, int64_t m_total,
+                         int64_t k, int64_t n, int32_t num_experts, int32_t dtype,
+                         int32_t activation, int32_t num_sms, int32_t use_atomic_queue,
+                         int32_t* work_counter, int32_t* status, void* stream);
+
+/*
+ * Decodes the grouped-GEMM tile list on the device, exactly as the GEMM
+ * kernel's scheduler does, for inspection and testing.
+ *
+ * Replaces _build_work_queue (src/triton_grouped_gemm.py:240-297).  With
+ * order == 0 the list is expert-major, then tile_m, then tile_n (the
+ * reference's order, :277-286); order == 1 is the GEMM kernel's own order
+ * (expert-major, then tile_n, then tile_m) that keeps CTAs sharing a weight
+ * column block adjacent.  Writes up to max_items entries to out_expert /
+ * out_tile_m / out_tile_n (int32 device arrays) and the total count to
+ * *out_count (int32 device word).
+ */
+MOE_API int32_t moe_tile_list(const void* expert_offsets, int32_t offsets_int64, int32_t num_experts,
+                      int64_t m_total, int64_t n, int32_t block_m, int32_t block_n, int32_t order,
+                      int32_t* out_expert, int32_t* out_tile_m, int32_t* out_tile_n,
+                      int32_t max_items, int32_t* out_count, int32_t* status, void* stream);
+
+/*
+ * offsets[0] = 0, offsets[i+1] = offsets[i] + counts[i], accumulated in 64-bit
+ * and stored as int32 (offsets_int64 == 0, wrapping like a two's-complement
+ * cast) or int64.
+ *
+ * Replaces expert_offsets_from_recv_counts (src/triton_grouped_gemm.py:300-323)
+ * for device-resident counts.  counts is int32 (counts_int64 == 0) or int64;
+ * an int64 count is narrowed to int32 before it is added, as the reference's
+ * .to(torch.int32) does.
+ */
+MOE_API int32_t moe_expert_offsets(const void* counts, int32_t counts_int64, int32_t num_experts,
+                           void* offsets, int32_t offsets_int64, void* stream);
+
+/*
+ * Same as moe_expert_offsets for host-resident counts and offsets; runs on the
+ * calling thread.  Serves expert_offsets_from_recv_counts
+ * (src/triton_grouped_gemm.py:300-323) when the counts are a Python list or a
+ * CPU tensor and no device is requested, where the reference returns a CPU tensor.
+ */
+MOE_API int32_t moe_expert_offsets_host(const void* counts, int32_t counts_int64, int32_t num_experts,
+                                void* offsets, int32_t offsets_int64);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_OVERLAP_H_ */

@@ -1,0 +1,25 @@
+"""B200-native (sm_100a) MoE expert hot path: persistent grouped GEMM and
+NVLink token dispatch/combine, behind the call surface of moe-overlap's
+``triton_grouped_gemm`` and ``deep_ep_comm`` modules.
+
+The compute runs in ``libmoe_overlap_b200.so`` (built in-tree by
+``python -m moe_overlap_b200.build``) through its C ABI (``include/moe_overlap.h``).
+"""
+from .grouped_gemm import (
+    expert_offsets_from_recv_counts,
+    grouped_gemm,
+    persistent_grouped_gemm,
+    reference_grouped_gemm,
+    tile_list,
+)
+from ._lib import MoeError, check_status
+
+__all__ = [
+    "persistent_grouped_gemm",
+    "grouped_gemm",
+    "expert_offsets_from_recv_counts",
+    "reference_grouped_gemm",
+    "tile_list",
+    "MoeError",
+    "check_status",
+]

@@ -1,0 +1,144 @@
+"""ctypes binding of the in-tree C-ABI library ``libmoe_overlap_b200.so``.
+
+The library is the only compute path: if it is missing or fails to load, every
+entry point raises ``RuntimeError``; there is no Python or CPU fallback.
+
+Device-side errors (an expired bounded wait, offsets out of range) are written
+by the kernels into a per-device status word that lives in pinned, mapped host
+memory.  ``check_status()`` reads it without synchronising; the public entry
+points call it before every launch, so an error from an earlier kernel is
+raised at the next call (like CUDA's own asynchronous error reporting), and
+``check_status(sync=True)`` synchronises first.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libmoe_overlap_b200.so"
+LIB_PATH = Path(__file__).resolve().with_name(LIB_NAME)
+
+MOE_OK = 0
+MOE_ERR_INVALID_ARG = 1
+MOE_ERR_CUDA = 2
+MOE_ERR_TIMEOUT = 3
+MOE_ERR_OFFSETS = 4
+MOE_ERR_UNSUPPORTED = 5
+MOE_ERR_CAPACITY = 6
+
+MOE_DTYPE_BF16 = 0
+MOE_DTYPE_F16 = 1
+MOE_ACT_NONE = 0
+MOE_ACT_GELU = 1
+
+_c_void_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+
+# name -> (restype, argtypes); mirrors include/moe_overlap.h
+SIGNATURES: dict[str, tuple] = {
+    "moe_status_string": (ctypes.c_char_p, [_i32]),
+    "moe_abi_version": (_i32, []),
+    "moe_grouped_gemm": (
+        _i32,
+        [
+            _c_void_p, _i64,  # a, lda
+            _c_void_p, _i64, _i64, _i64,  # b, strides e/k/n
+            _c_void_p, _i64,  # c, ldc
+            _c_void_p, _i32,  # offsets, offsets_int64
+            _i64, _i64, _i64, _i32,  # m_total, k, n, num_experts
+            _i32, _i32, _i32, _i32,  # dtype, activation, num_sms, use_atomic_queue
+            _c_void_p, _c_void_p, _c_void_p,  # work_counter, status, stream
+        ],
+    ),
+    "moe_tile_list": (
+        _i32,
+        [
+            _c_void_p, _i32, _i32, _i64, _i64, _i32, _i32, _i32,
+            _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p,
+        ],
+    ),
+    "moe_expert_offsets": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _i32, _c_void_p]),
+    "moe_expert_offsets_host": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _i32]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+_status_words: dict[int, torch.Tensor] = {}
+
+
+class MoeError(RuntimeError):
+    """A status code returned by the library or recorded by one of its kernels."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: {status_string(code)} (status {code})")
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once and declares every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_NAME} is not built (expected at {LIB_PATH}); "
+                    "run `python -m moe_overlap_b200.build`"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = lib
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return load().moe_status_string(int(code)).decode()
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Pinned host int32 the kernels on ``device`` write their error code into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _status_words.get(idx)
+    if w is None:
+        with _lock:
+            w = _status_words.get(idx)
+            if w is None:
+                w = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+                _status_words[idx] = w
+    return w
+
+
+def check_status(device: torch.device | None = None, sync: bool = False) -> None:
+    """Raises MoeError if a kernel on ``device`` recorded an error (and clears it)."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    if sync:
+        torch.cuda.synchronize(device)
+    w = status_word(device)
+    code = int(w[0])
+    if code != 0:
+        w.zero_()
+        raise MoeError(code, "device-side error from an earlier moe_overlap_b200 kernel")
+
+
+def check_call(code: int, where: str) -> None:
+    if code != MOE_OK:
+        raise MoeError(code, where)
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def sync_check_enabled() -> bool:
+    """MOE_B200_SYNC_CHECK=1 synchronises and checks the status after every call."""
+    return os.environ.get("MOE_B200_SYNC_CHECK", "0") not in ("", "0")
