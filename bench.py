@@ -1,0 +1,472 @@
+#!/usr/bin/env python
+"""Benchmark of the moe_overlap_b200 hot path (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gemm_cfg2|gemm_cfg3|gemm_cfg1]
+
+Default workload: BASELINE config 2 -- grouped GEMM forward, 16 experts x 512
+rows, H=2048, F=4096, bf16, striped persistent schedule over every SM.  One
+"step" is one grouped-GEMM launch over the whole batch; ``value`` is the
+TFLOP/s of all ranks together (2*M*K*N algorithmic flops, real rows only)
+divided by the device time of the K timed launches (CUDA events on the
+launching stream, max over ranks).  L2 is flushed (a 256 MiB write) between
+timed launches, outside the events.  ``e2e`` times the same step through the
+public ``persistent_grouped_gemm`` call with the activations and offsets
+copied from pinned host memory and the result copied back inside the timed
+region (expert weights stay resident, as model parameters do).
+
+With N > 1 (torchrun) every rank runs its own copy of the workload: the
+grouped GEMM has no cross-rank exchange, so scaling is weak and there is no
+collective on the data path.
+
+``--impl reference`` times the reference's CPU implementation of the path on
+this host's cores: the numpy restatement of the per-expert loop in
+``oracle/`` (the reference's Python cannot travel to the GPU box), on a
+bounded sample of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "grouped-GEMM TFLOP/s vs bf16 peak"
+UNIT = "TFLOP/s"
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+WORKLOADS = {
+    # name: (counts builder, k, n, dtype, atomic, description)
+    "gemm_cfg2": dict(k=2048, n=4096, dtype="bf16", atomic=False, experts=16,
+                      desc="BASELINE config 2: E=16, 512 rows/expert (8192 rows), H=2048, F=4096, bf16, striped"),
+    "gemm_cfg3": dict(k=2048, n=4096, dtype="bf16", atomic=True, experts=16,
+                      desc="BASELINE config 3: E=16, 16384 Zipf(1.2) rows (one expert empty), H=2048, F=4096, bf16, atomic queue"),
+    "gemm_cfg1": dict(k=512, n=1024, dtype="f16", atomic=False, experts=8,
+                      desc="BASELINE config 1: E=8, 128 rows/expert, H=512, F=1024, fp16, striped"),
+}
+
+
+def workload_counts(name: str) -> list[int]:
+    from tests._inputs import zipf_counts
+
+    if name == "gemm_cfg2":
+        return [512] * 16
+    if name == "gemm_cfg3":
+        return zipf_counts(16384, 16, 1.2, seed=0)
+    if name == "gemm_cfg1":
+        return [128] * 8
+    raise ValueError(name)
+
+
+def parse_args() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm_cfg2")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    return ap.parse_args()
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def load_peaks() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        peaks = json.loads(path.read_text())
+        return float(peaks["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, "fallback (no MEASURED_PEAKS.json)"
+
+
+def profiled_traffic(workload: str) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary of this workload."""
+    path = REPO / "profiles" / f"grouped_gemm_{workload.split('_')[-1]}.ncu.txt"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        return None
+    return None
+
+
+# ---------------------------------------------------------------- CPU side --
+class CpuGemm:
+    """The oracle's per-expert loop with the expert weights kept resident in fp32.
+
+    Weights are model parameters, so they are converted once, outside the
+    timed region; each sample converts its activation rows, multiplies in fp32
+    (numpy BLAS) and rounds the result to the storage dtype, as
+    oracle/grouped_gemm.py does.
+    """
+
+    def __init__(self, a_np, b_np, offsets, dtype):
+        from oracle.numerics import to_f32
+
+        self.a_np, self.dtype = a_np, dtype
+        self.off = [int(v) for v in offsets]
+        self.b32 = [to_f32(b_np[e], dtype) for e in range(b_np.shape[0])]
+        self.experts = [e for e in range(len(self.off) - 1) if self.off[e + 1] > self.off[e]]
+
+    def run(self, experts, rows_cap=None) -> int:
+        from oracle.numerics import from_f32, to_f32
+
+        flops = 0
+        for e in experts:
+            s, t = self.off[e], self.off[e + 1]
+            if rows_cap is not None:
+                t = min(t, s + rows_cap)
+            if t <= s:
+                continue
+            acc = to_f32(self.a_np[s:t], self.dtype) @ self.b32[e]
+            from_f32(acc, self.dtype)
+            flops += 2 * (t - s) * self.a_np.shape[1] * self.b32[e].shape[1]
+        return flops
+
+
+def set_blas_threads(n: int) -> int:
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(n)
+    except Exception:
+        pass
+    return n
+
+
+def cpu_baseline(a, b, offsets, dtype, budget_s: float = 20.0) -> dict:
+    """Oracle (numpy restatement of the per-expert torch loop) on this host."""
+    from tests._inputs import to_storage
+
+    cores = set_blas_threads(cpu_cores())
+    g = CpuGemm(to_storage(a), to_storage(b), offsets.tolist(), dtype)
+    g.run(g.experts[:1], rows_cap=64)  # warm BLAS threads
+    done_flops, done_experts = 0, 0
+    t0 = time.perf_counter()
+    for e in g.experts:
+        done_flops += g.run([e])
+        done_experts += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {
+        "value": round(done_flops / dt / 1e12, 4),
+        "unit": UNIT,
+        "cores": cores,
+        "kind": "port",
+        "sample": f"{done_experts} of {len(g.experts)} non-empty experts of the same workload "
+                  f"({done_flops / 1e9:.1f} GFLOP in {dt:.2f} s): numpy fp32 matmul with resident "
+                  f"fp32 weights + activation conversion + output rounding (oracle/)",
+    }
+
+
+def run_reference(args, rank: int) -> None:
+    """The reference arm: CPU implementation of the path, rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+
+    from tests._inputs import gemm_inputs, to_storage
+
+    wl = WORKLOADS[args.workload]
+    counts = workload_counts(args.workload)
+    a, b, offsets = gemm_inputs(counts, wl["k"], wl["n"], wl["dtype"], seed=0)
+    g = CpuGemm(to_storage(a), to_storage(b), offsets.tolist(), wl["dtype"])
+    cores = set_blas_threads(cpu_cores())
+    # Size each step's sample (rows of one expert) so the whole run stays near a minute.
+    g.run(g.experts[:1], rows_cap=64)
+    probe_t = time.perf_counter()
+    g.run(g.experts[:1], rows_cap=128)
+    per_row_s = max((time.perf_counter() - probe_t) / 128, 1e-7)
+    budget_per_step = 60.0 / max(1, args.steps + args.warmup)
+    rows_cap = int(max(16, min(max(counts), budget_per_step / per_row_s)))
+    for i in range(args.warmup):
+        g.run([g.experts[i % len(g.experts)]], rows_cap)
+    flops, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        flops += g.run([g.experts[i % len(g.experts)]], rows_cap)
+    dt = time.perf_counter() - t0
+    value = flops / dt / 1e12
+    sample = (f"per step: up to {rows_cap} rows of one expert (cycling over {len(g.experts)} experts) "
+              f"of {args.workload}; numpy fp32 matmul with resident fp32 weights, activation "
+              f"conversion and output rounding (oracle/)")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt / max(1, args.steps) * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": wl["dtype"],
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": args.workload, "description": wl["desc"]},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    del torch
+
+
+# ---------------------------------------------------------------- clocks --
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler(threading.Thread):
+    """Samples SM clock, power and clock-event reasons through NVML."""
+
+    def __init__(self, torch_device, interval_s: float = 0.002):
+        super().__init__(daemon=True)
+        self.interval = interval_s
+        self.samples: list[tuple[int, int, float]] = []
+        self.max_mhz = None
+        self._stop_evt = threading.Event()
+        self.handle = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(torch_device)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{props.uuid}")
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(torch_device.index or 0)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+        except Exception:
+            self.handle = None
+
+    def run(self) -> None:
+        if self.handle is None:
+            return
+        nv = self.nvml
+        while not self._stop_evt.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                try:
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                except Exception:
+                    reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                power = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((sm, reasons, power))
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def stop(self) -> dict:
+        self._stop_evt.set()
+        self.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        mask = 0
+        for s in busy:
+            mask |= s[1]
+        return {
+            "sm_mhz": int(statistics.median(s[0] for s in busy)),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": [name for bit, name in _REASONS.items() if mask & bit and bit != 0x1],
+            "samples": len(busy),
+            "power_w_max": round(max(s[2] for s in busy), 1),
+        }
+
+
+# ---------------------------------------------------------------- GPU side --
+def main() -> None:
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import moe_overlap_b200 as mo
+    from tests._inputs import gemm_inputs
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("bench.py needs a CUDA device")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
+
+    wl = WORKLOADS[args.workload]
+    counts = workload_counts(args.workload)
+    a_cpu, b_cpu, off_cpu = gemm_inputs(counts, wl["k"], wl["n"], wl["dtype"], seed=0)
+    m_rows = int(sum(counts))
+    flops = 2.0 * m_rows * wl["k"] * wl["n"]
+    sm_count = torch.cuda.get_device_properties(device).multi_processor_count
+    a = a_cpu.to(device)
+    b = b_cpu.to(device)
+    off = off_cpu.to(device)
+    counter = torch.zeros(1, dtype=torch.int32, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return mo.persistent_grouped_gemm(a, b, off, num_sms=sm_count,
+                                          use_atomic_queue=wl["atomic"], work_counter=counter)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+        flush.fill_(1)
+    torch.cuda.synchronize(device)
+    mo.check_status(device, sync=True)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(device)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)  # evict L2 between launches (outside the events)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    mo.check_status(device, sync=True)
+    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(launch_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * flops * args.steps / (total_ms / 1e3) / 1e12
+    avg_launch_s = statistics.mean(launch_ms) / 1e3
+    achieved = flops / avg_launch_s / 1e12
+    peak, peak_src = load_peaks()
+
+    # ---- end to end through the public API, host buffers in and out ----
+    e2e = None
+    if not args.no_e2e:
+        a_host = a_cpu.pin_memory()
+        off_host = off_cpu.pin_memory()
+        c_host = torch.empty((m_rows, wl["n"]), dtype=a_cpu.dtype).pin_memory()
+        a_dev = torch.empty_like(a)
+        off_dev = torch.empty_like(off)
+
+        def e2e_step():
+            a_dev.copy_(a_host, non_blocking=True)
+            off_dev.copy_(off_host, non_blocking=True)
+            c = mo.persistent_grouped_gemm(a_dev, b, off_dev, num_sms=sm_count,
+                                           use_atomic_queue=wl["atomic"], work_counter=counter)
+            c_host.copy_(c, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e_end.record(stream)
+        torch.cuda.synchronize(device)
+        e2e_ms = e_start.elapsed_time(e_end)
+        if world > 1:
+            t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        mo.check_status(device, sync=True)
+        e2e = {
+            "value": round(world * flops * args.steps / (e2e_ms / 1e3) / 1e12, 3),
+            "unit": UNIT,
+            "h2d_bytes_per_step": a_host.numel() * a_host.element_size()
+            + off_host.numel() * off_host.element_size(),
+            "d2h_bytes_per_step": c_host.numel() * c_host.element_size(),
+            "ms_per_step": round(e2e_ms / args.steps, 4),
+        }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(a_cpu, b_cpu, off_cpu, wl["dtype"])
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": wl["dtype"],
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; generated on CPU)",
+            "config": {
+                "workload": args.workload,
+                "description": wl["desc"],
+                "rows": m_rows,
+                "counts": counts,
+                "num_sms": sm_count,
+                "schedule": "atomic" if wl["atomic"] else "striped",
+                "l2": "flushed between timed launches (256 MiB write, outside the events); "
+                      "inputs also exceed L2 (A+B = "
+                      f"{(a.numel() * a.element_size() + b.numel() * b.element_size()) >> 20} MiB)",
+                "parallelism": f"replica x{world} (no data-path collective)",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "achieved": round(achieved, 2),
+                "peak": peak,
+                "unit": UNIT,
+                "frac": round(achieved / peak, 4),
+                "peak_source": peak_src,
+                "traffic": profiled_traffic(args.workload),
+                "kernel": "moe::gg::grouped_gemm_kernel",
+                "algorithmic_work": f"2*M*K*N = {flops / 1e9:.2f} GFLOP per launch (M={m_rows} real rows)",
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

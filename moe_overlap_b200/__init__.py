@@ -5,7 +5,7 @@ NVLink token dispatch/combine, behind the call surface of moe-overlap's
 The compute runs in ``libmoe_overlap_b200.so`` (built in-tree by
 ``python -m moe_overlap_b200.build``) through its C ABI (``include/moe_overlap.h``).
 """
-from .grouped_gemm import (
+from .gemm import (
     expert_offsets_from_recv_counts,
     grouped_gemm,
     persistent_grouped_gemm,

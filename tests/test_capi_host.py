@@ -1,0 +1,154 @@
+"""CPU-only checks of the C-ABI library and the host-side mirror of the reference API.
+
+No kernel is launched here: the library must load without a GPU, export every
+entry point that include/*.h declares, reject bad arguments on the host with
+the documented status codes, and the Python layer must raise the reference's
+exceptions (src/triton_grouped_gemm.py:347-360, 383-384).
+"""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import moe_overlap_b200 as mo
+from moe_overlap_b200 import _lib
+
+HEADERS = sorted((Path(__file__).resolve().parents[1] / "include").glob("*.h"))
+
+
+def declared_symbols() -> list[str]:
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        names += re.findall(r"^MOE_API\s+[\w\s\*]+?\b(moe_\w+)\s*\(", text, flags=re.M)
+    return names
+
+
+def test_headers_declare_entry_points():
+    names = declared_symbols()
+    assert "moe_grouped_gemm" in names and "moe_expert_offsets" in names
+    assert len(names) == len(set(names))
+
+
+@pytest.mark.parametrize("name", declared_symbols())
+def test_library_exports_every_declared_symbol(name):
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    assert name in _lib.SIGNATURES, f"{name} has no ctypes signature in _lib.SIGNATURES"
+
+
+def test_abi_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.moe_abi_version() == 1
+    for code in range(7):
+        assert _lib.status_string(code)
+    assert _lib.status_string(99) == "unknown status"
+
+
+def _gemm_call(**kw):
+    args = dict(a=16, lda=64, b=16, se=64 * 64, sk=64, sn=1, c=16, ldc=64, off=16, off64=0,
+                m=10, k=64, n=64, e=1, dtype=0, act=0, sms=148, atomic=0, counter=None,
+                status=None, stream=None)
+    args.update(kw)
+    return _lib.load().moe_grouped_gemm(*args.values())
+
+
+@pytest.mark.parametrize(
+    "kw",
+    [
+        dict(dtype=7),                 # unknown dtype
+        dict(act=9),                   # unknown activation
+        dict(m=-1),                    # negative size
+        dict(e=2000),                  # more experts than the scheduler's smem table
+        dict(n=12, ldc=16),            # n not a multiple of 8
+        dict(k=12, lda=16),            # k not a multiple of 8
+        dict(c=18),                    # misaligned output
+        dict(a=24),                    # misaligned A
+        dict(sn=2, sk=2),              # B neither N-major nor K-major
+        dict(atomic=1, counter=None),  # atomic queue without a counter
+        dict(off=None),                # no offsets
+    ],
+)
+def test_grouped_gemm_rejects_bad_arguments_on_host(kw):
+    code = _gemm_call(**kw)
+    assert code in (_lib.MOE_ERR_INVALID_ARG, _lib.MOE_ERR_UNSUPPORTED), code
+
+
+def test_grouped_gemm_empty_output_is_a_no_op():
+    assert _gemm_call(m=0) == _lib.MOE_OK
+    assert _gemm_call(n=0) == _lib.MOE_OK
+
+
+def test_tile_list_and_offsets_reject_bad_arguments():
+    lib = _lib.load()
+    assert lib.moe_tile_list(None, 0, 4, 10, 10, 128, 128, 0, None, None, None, 0, 16, None,
+                             None) == _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_tile_list(16, 0, 4, 10, 10, 128, 128, 2, None, None, None, 0, 16, None,
+                             None) == _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_expert_offsets(None, 0, 4, 16, 0, None) == _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_expert_offsets_host(None, 0, 3, None, 0) == _lib.MOE_ERR_INVALID_ARG
+
+
+def _cpu_args():
+    a = torch.zeros(8, 16, dtype=torch.bfloat16)
+    b = torch.zeros(2, 16, 8, dtype=torch.bfloat16)
+    off = torch.tensor([0, 4, 8], dtype=torch.int32)
+    return a, b, off
+
+
+def test_persistent_grouped_gemm_requires_cuda_tensors():
+    a, b, off = _cpu_args()
+    with pytest.raises(ValueError, match="requires CUDA tensors"):
+        mo.persistent_grouped_gemm(a, b, off)
+
+
+def test_host_mirror_error_messages_match_reference(monkeypatch):
+    """Validation order and messages of src/triton_grouped_gemm.py:347-360."""
+    from moe_overlap_b200 import gemm as gg
+
+    class FakeCuda:
+        type = "cuda"
+
+        def __eq__(self, other):
+            return isinstance(other, FakeCuda)
+
+    class T:
+        def __init__(self, shape, dtype=torch.bfloat16, device=None):
+            self.shape, self.dtype = shape, dtype
+            self.device = device or FakeCuda()
+
+        def dim(self):
+            return len(self.shape)
+
+        def size(self, i):
+            return self.shape[i]
+
+        def numel(self):
+            n = 1
+            for s in self.shape:
+                n *= s
+            return n
+
+    a, b, off = T((8, 16)), T((2, 16, 8)), T((3,), torch.int32)
+    cases = [
+        ((T((8,)), b, off), "Shapes must be"),
+        ((T((8, 12)), b, off), "K dimension mismatch"),
+        ((a, b, T((4,), torch.int32)), r"expert_offsets must have shape \[num_experts \+ 1\]"),
+        ((a, b, T((3,), torch.int32, device=torch.device("cpu"))), "same device"),
+        ((T((8, 16), torch.float32), T((2, 16, 8), torch.float32), off), "bf16/fp16"),
+        ((a, T((2, 16, 8), torch.float16), off), "should match a_cat dtype"),
+    ]
+    for args, msg in cases:
+        with pytest.raises(ValueError, match=msg):
+            gg.persistent_grouped_gemm(*args)
+    with pytest.raises(ValueError, match="work_counter must be int32"):
+        gg.persistent_grouped_gemm(a, b, off, work_counter=T((2,), torch.int32))
+
+
+def test_library_missing_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "missing.so")
+    with pytest.raises(RuntimeError, match="is not built"):
+        _lib.load()
