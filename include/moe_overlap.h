@@ -95,6 +95,38 @@ MOE_API int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int6
                          int32_t* work_counter, int32_t* status, void* stream);
 
 /*
+ * Allocation-free variant of moe_grouped_gemm with the dynamic (atomic) tile
+ * queue.  It has no counterpart in the reference; it exists for callers that
+ * cannot allocate device memory: code running under a host framework whose
+ * memory pool owns the GPU and forbids raw cudaMalloc/cudaFree beside it, and
+ * latency-critical loops where an allocation could synchronise the device.
+ *
+ * Same arguments and result as moe_grouped_gemm with use_atomic_queue = 1,
+ * minus work_counter: the queue counter lives in a 256-byte device array inside
+ * this library (one per GPU, kept until the process exits).  The caller still
+ * passes every input and output.  The call allocates nothing and calls no
+ * allocating routine.
+ *
+ * Limit: the tile count of one call, bounded above by
+ * (ceil(m_total/128) + num_experts) * ceil(n/256), must stay below about
+ * 2^31 - 4096; larger problems are refused with MOE_ERR_CAPACITY.
+ * Set-up: the first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.
+ * Sharing: every call on a device uses the same counter, which keeps what the
+ * last call left and is re-zeroed on `stream` at the start of each call.  Calls
+ * that overlap on the GPU (e.g. on two streams at once) race on it and must be
+ * serialised by the caller.
+ */
+MOE_API int32_t moe_grouped_gemm_noalloc(const void* a, int64_t lda, const void* b,
+                                         int64_t b_stride_e, int64_t b_stride_k,
+                                         int64_t b_stride_n, void* c, int64_t ldc,
+                                         const void* expert_offsets, int32_t offsets_int64,
+                                         int64_t m_total, int64_t k, int64_t n,
+                                         int32_t num_experts, int32_t dtype, int32_t activation,
+                                         int32_t num_sms, int32_t* status, void* stream);
+
+/*
  * Decodes the grouped-GEMM tile list on the device, exactly as the GEMM
  * kernel's scheduler does, for inspection and testing.
  *

@@ -55,6 +55,18 @@ SIGNATURES: dict[str, tuple] = {
             _c_void_p, _c_void_p, _c_void_p,  # work_counter, status, stream
         ],
     ),
+    "moe_grouped_gemm_noalloc": (
+        _i32,
+        [
+            _c_void_p, _i64,  # a, lda
+            _c_void_p, _i64, _i64, _i64,  # b, strides e/k/n
+            _c_void_p, _i64,  # c, ldc
+            _c_void_p, _i32,  # offsets, offsets_int64
+            _i64, _i64, _i64, _i32,  # m_total, k, n, num_experts
+            _i32, _i32, _i32,  # dtype, activation, num_sms
+            _c_void_p, _c_void_p,  # status, stream
+        ],
+    ),
     "moe_tile_list": (
         _i32,
         [
