@@ -17,6 +17,7 @@
 #ifndef MOE_OVERLAP_H_
 #define MOE_OVERLAP_H_
 
+#include <stdbool.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -164,6 +165,128 @@ MOE_API int32_t moe_expert_offsets(const void* counts, int32_t counts_int64, int
  */
 MOE_API int32_t moe_expert_offsets_host(const void* counts, int32_t counts_int64, int32_t num_experts,
                                 void* offsets, int32_t offsets_int64);
+
+/* ================================================ expert-parallel exchange == */
+/*
+ * Token dispatch/combine between the GPUs of one NVLink/NVSwitch domain.
+ * Replaces DeepEPDispatcher (src/deep_ep_comm.py:21-115) and the DeepEP
+ * intranode runtime under it (thirdParty/DeepEP/csrc/deep_ep.cpp:131-914,
+ * kernels/layout.cu, kernels/intranode.cu, kernels/runtime.cu).
+ *
+ * Each rank owns an endpoint with one symmetric device buffer (allocated by
+ * moe_ep_create).  The host exchanges the buffers between ranks (e.g. CUDA IPC
+ * handles gathered over the process group, as deep_ep.cpp:185-199 and
+ * buffer.py:96-101 do) and hands every rank's base pointer, as mapped on this
+ * GPU, to moe_ep_connect.  Experts are sharded contiguously, num_experts/world
+ * per rank (src/train_moe_baseline.py:136-137).
+ *
+ * Receive layout: one row per (token, selected expert) on the expert's owner,
+ * ordered by local expert, then source rank, then (token, slot); the owner gets
+ * expert_offsets on the device.  Two slots alternate between consecutive
+ * dispatches; at most two dispatches may be outstanding (not yet combined).
+ * Every call takes an `epoch` (1, 2, 3, ... in call order, the same on every
+ * rank) and a `slot` (the epoch's parity, by convention).
+ */
+#define MOE_EP_MAX_RANKS 64
+
+typedef struct moe_ep_s* moe_ep_t;
+
+/* Device pointers into this rank's endpoint for one slot. */
+typedef struct {
+  void* recv_x;               /* [cap_rows][hidden] bf16, expert-ordered rows      */
+  void* expert_out;           /* [cap_rows][hidden] bf16, rows read by combine     */
+  int64_t* recv_topk_idx;     /* [cap_rows][max_topk]: local expert in the row's slot, else -1 */
+  float* recv_topk_weights;   /* [cap_rows][max_topk]: weight in the row's slot, else 0 */
+  int32_t* recv_src;          /* [cap_rows][2]: {source rank, source token}        */
+  int32_t* expert_offsets;    /* [num_experts/world + 1] int32, on the device      */
+  int32_t* send_pos;          /* [max_tokens][topk] row of each sent (token, slot) on its owner, -1 none */
+  int64_t* host_info;         /* mapped host [2]: {epoch, rows received} after scatter */
+  int64_t cap_rows;
+  int32_t max_topk;
+} moe_ep_views_t;
+
+/* Allocates this rank's endpoint: a symmetric buffer holding two slots of
+ * max_recv_rows received rows (plus expert outputs, metadata, counts, flags),
+ * and local scratch for max_tokens tokens of up to max_topk experts each. */
+MOE_API int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden,
+                              int32_t max_tokens, int32_t max_topk, int64_t max_recv_rows,
+                              moe_ep_t* out);
+MOE_API int32_t moe_ep_destroy(moe_ep_t ep);
+/* Base pointer and size of this rank's symmetric buffer (to export to peers). */
+MOE_API int32_t moe_ep_buffer(moe_ep_t ep, void** base, uint64_t* bytes);
+/* peer_bases[r] = rank r's symmetric buffer as addressable from this GPU
+ * (peer_bases[rank] must be this endpoint's own buffer). */
+MOE_API int32_t moe_ep_connect(moe_ep_t ep, void* const* peer_bases);
+MOE_API int32_t moe_ep_views(moe_ep_t ep, int32_t slot, moe_ep_views_t* views);
+
+/*
+ * Dispatch, in three phases enqueued on `stream` (moe_ep_dispatch runs all three):
+ *   begin    per-expert counts of this rank's (token, slot) pairs, pushed into every
+ *            rank (no waiting);                         ~ layout.cu + notify_dispatch
+ *   scatter  waits (bounded by wait_ns) for every rank's counts, then pushes each
+ *            selected token's bf16 row and its metadata into the owner's receive
+ *            slot and raises this rank's data flag everywhere; pad_rows != 0 also
+ *            sets recv_topk_idx = -1 for this rank's unused receive rows;
+ *                                                       ~ intranode.cu dispatch
+ *   end      waits (bounded) until every rank's rows have landed here.
+ * x: [num_tokens][hidden] bf16; topk_idx: [num_tokens][topk] int64 global expert ids
+ * (-1 = none); topk_weights: [num_tokens][topk] float.  num_blocks is the grid of
+ * the scatter (the SM budget of the exchange).  Device errors go to `status`.
+ */
+MOE_API int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                      const float* topk_weights, int32_t num_tokens,
+                                      int32_t topk, int32_t slot, uint64_t epoch,
+                                      int32_t* status, void* stream);
+MOE_API int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                        const float* topk_weights, int32_t num_tokens,
+                                        int32_t topk, int32_t slot, uint64_t epoch,
+                                        int32_t num_blocks, int32_t pad_rows, uint64_t wait_ns,
+                                        int32_t* status, void* stream);
+MOE_API int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch, uint64_t wait_ns,
+                                    int32_t* status, void* stream);
+MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                int32_t slot, uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
+                                uint64_t wait_ns, int32_t* status, void* stream);
+
+/*
+ * Combine, in two phases (moe_ep_combine runs both):
+ *   begin  raises "this rank's expert_out rows for `slot` are complete" in every
+ *          rank (no waiting);
+ *   end    waits (bounded) for every rank's flag, then for each of this rank's
+ *          num_tokens tokens writes out[t] = bf16( sum_j s_j * owner_j.expert_out[
+ *          send_pos[t][j]] ), summed in fp32 in slot order, with s_j = 1
+ *          (weighted == 0: the reference's unweighted combine, intranode.cu:961-1030)
+ *          or s_j = topk_weights[t][j] (the fused weighted top-k reduction).
+ * topk_idx / topk_weights / num_tokens / topk are those of the matching dispatch.
+ */
+MOE_API int32_t moe_ep_combine_begin(moe_ep_t ep, int32_t slot, uint64_t epoch, void* stream);
+MOE_API int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx, const float* topk_weights,
+                                   int32_t num_tokens, int32_t topk, int32_t slot,
+                                   uint64_t epoch, int32_t weighted, void* out,
+                                   int32_t num_blocks, uint64_t wait_ns, int32_t* status,
+                                   void* stream);
+MOE_API int32_t moe_ep_combine(moe_ep_t ep, const int64_t* topk_idx, const float* topk_weights,
+                               int32_t num_tokens, int32_t topk, int32_t slot, uint64_t epoch,
+                               int32_t weighted, void* out, int32_t num_blocks, uint64_t wait_ns,
+                               int32_t* status, void* stream);
+
+/*
+ * DeepEP's get_dispatch_layout (thirdParty/DeepEP/deep_ep/buffer.py:293-319,
+ * kernels/layout.cu:10-121): tokens per rank (each token counted once per rank),
+ * tokens per expert and is_token_in_rank [num_tokens][world] (bool, 1 byte).
+ * Any output may be NULL.
+ */
+MOE_API int32_t moe_ep_dispatch_layout(const int64_t* topk_idx, int32_t num_tokens, int32_t topk,
+                                       int32_t num_experts, int32_t world,
+                                       int32_t* tokens_per_rank, int32_t* tokens_per_expert,
+                                       bool* is_token_in_rank, void* stream);
+
+/* CUDA IPC helpers for sharing symmetric buffers between processes. */
+#define MOE_IPC_HANDLE_BYTES 64
+MOE_API int32_t moe_ipc_export(void* dev_ptr, void* handle_out);
+MOE_API int32_t moe_ipc_import(const void* handle, void** dev_ptr_out);
+MOE_API int32_t moe_ipc_close(void* dev_ptr);
 
 #ifdef __cplusplus
 }

@@ -38,6 +38,7 @@ MOE_ACT_GELU = 1
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
 
 # name -> (restype, argtypes); mirrors include/moe_overlap.h
 SIGNATURES: dict[str, tuple] = {
@@ -76,6 +77,34 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "moe_expert_offsets": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _i32, _c_void_p]),
     "moe_expert_offsets_host": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _i32]),
+    # expert-parallel exchange
+    "moe_ep_create": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i64, _c_void_p]),
+    "moe_ep_destroy": (_i32, [_c_void_p]),
+    "moe_ep_buffer": (_i32, [_c_void_p, _c_void_p, _c_void_p]),
+    "moe_ep_connect": (_i32, [_c_void_p, _c_void_p]),
+    "moe_ep_views": (_i32, [_c_void_p, _i32, _c_void_p]),
+    "moe_ep_dispatch_begin": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _c_void_p,
+               _c_void_p]),
+    "moe_ep_dispatch_scatter": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
+               _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch_end": (_i32, [_c_void_p, _i32, _u64, _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
+               _u64, _c_void_p, _c_void_p]),
+    "moe_ep_combine_begin": (_i32, [_c_void_p, _i32, _u64, _c_void_p]),
+    "moe_ep_combine_end": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _c_void_p, _i32,
+               _u64, _c_void_p, _c_void_p]),
+    "moe_ep_combine": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _c_void_p, _i32,
+               _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch_layout": (
+        _i32, [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "moe_ipc_export": (_i32, [_c_void_p, _c_void_p]),
+    "moe_ipc_import": (_i32, [_c_void_p, _c_void_p]),
+    "moe_ipc_close": (_i32, [_c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,871 @@
+// Expert-parallel token exchange over NVLink peer memory (sm_100a).
+//
+// Replaces the intranode dispatch/combine that src/deep_ep_comm.py:69-115 drives
+// through DeepEP (thirdParty/DeepEP/csrc/kernels/layout.cu, intranode.cu,
+// deep_ep.cpp:397-914), with a layout built for the grouped GEMM that follows:
+//
+//   dispatch  every (token, selected expert) pair becomes one bf16 row pushed
+//             straight into the owning rank's receive buffer, at its place in
+//             that rank's expert-ordered layout (local expert, then source rank,
+//             then token/slot order).  The receiver gets expert_offsets on the
+//             device, so recv_x feeds the grouped GEMM with no permutation and no
+//             host synchronisation.
+//   combine   the source rank pulls, for each of its tokens, the rows the owners
+//             produced (plain loads through peer pointers) and reduces them in
+//             fp32, optionally weighted by its own top-k weights, into one bf16 row.
+//
+// Phases (separate launches, all on one stream):
+//   dispatch_begin   layout (stable per-expert ranks) + push this rank's per-expert
+//                    counts into every peer + count flag            (no waiting)
+//   dispatch_scatter wait for every peer's counts, derive row bases, push rows and
+//                    metadata, last block raises the data flag in every peer
+//   dispatch_end     wait until every peer's rows have landed here
+//   combine_begin    raise "my expert outputs are ready" in every peer (no waiting)
+//   combine_end      wait for every peer's ready flag, pull + reduce
+// Waits are bounded (globaltimer); on expiry a kernel records MOE_ERR_TIMEOUT in the
+// status word and returns.  Flags carry a monotonically increasing epoch, so they
+// are never reset.  Two slots alternate between consecutive dispatches, which lets
+// the next chunk's dispatch run while the previous chunk is being computed.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <new>
+
+#include "../../include/moe_overlap.h"
+#include "host_common.h"
+
+namespace moe {
+namespace ep {
+
+constexpr int kMaxRanks = MOE_EP_MAX_RANKS;
+constexpr int kMaxExperts = 1024;
+constexpr int kAssignPerLayoutBlock = 2048;  // 8 warps x 8 chunks x 32 lanes
+constexpr int kLayoutThreads = 256;
+constexpr int kCommThreads = 512;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void record_status(int32_t* status, int32_t code) {
+  if (status != nullptr) {
+    volatile int32_t* s = status;
+    if (*s == 0) *s = code;
+  }
+}
+
+// Per-slot regions of the symmetric buffer, byte offsets from its base.
+struct SlotLayout {
+  uint64_t recv_x;     // [cap][hidden] bf16
+  uint64_t y;          // [cap][hidden] bf16 (expert outputs read by combine)
+  uint64_t topk_idx;   // [cap][max_topk] int64
+  uint64_t topk_w;     // [cap][max_topk] float
+  uint64_t src;        // [cap] int2 {src_rank, src_token}
+  uint64_t counts;     // [world][num_experts] int32
+};
+
+struct SymLayout {
+  SlotLayout slot[2];
+  uint64_t count_flag;  // [2][world] uint64
+  uint64_t data_flag;   // [2][world] uint64
+  uint64_t ready_flag;  // [2][world] uint64
+  uint64_t bytes;
+};
+
+struct Endpoint {
+  int rank, world, num_experts, per_rank, hidden, max_tokens, max_topk;
+  int64_t cap_rows;
+  SymLayout lay;
+  uint8_t* sym = nullptr;          // this rank's symmetric buffer
+  uint8_t* peers[kMaxRanks] = {};  // every rank's buffer as mapped here
+  // local scratch
+  uint8_t* scratch = nullptr;
+  uint8_t** d_peers = nullptr;      // [world]
+  int32_t* block_hist = nullptr;    // [max_blocks][E] -> exclusive block base after count
+  int32_t* rank_in_block = nullptr; // [max_tokens*max_topk]
+  int32_t* send_pos[2] = {};        // [max_tokens*max_topk]
+  int32_t* offsets[2] = {};         // [per_rank+1] receiver expert offsets
+  int32_t* my_counts = nullptr;     // [E]
+  unsigned int* done_ctr = nullptr; // blocks finished in the current scatter
+  int max_blocks = 0;
+  int64_t* host_info = nullptr;     // mapped pinned: [2][2] {epoch, total rows}
+  int device = 0;
+};
+
+struct Params {
+  uint8_t** peers;
+  SymLayout lay;
+  int rank, world, num_experts, per_rank, hidden, max_topk;
+  int64_t cap_rows;
+  int slot;
+  uint64_t epoch;
+  uint64_t wait_ns;
+  int32_t* status;
+  // dispatch
+  const __nv_bfloat16* x;
+  const int64_t* topk_idx;
+  const float* topk_w;
+  int num_tokens, topk;
+  int32_t* block_hist;
+  int32_t* rank_in_block;
+  int32_t* send_pos;
+  int32_t* offsets_out;
+  int32_t* my_counts;
+  unsigned int* done_ctr;
+  int num_layout_blocks;
+  int pad_rows;  // fill recv_topk_idx rows past the received count with -1
+  int64_t* host_info;
+  // combine
+  __nv_bfloat16* out;
+  int weighted;
+};
+
+template <typename T>
+__device__ __forceinline__ T* at(uint8_t* base, uint64_t off) {
+  return reinterpret_cast<T*>(base + off);
+}
+
+// Bounded wait until flag >= epoch.  Returns false on timeout.
+__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t epoch, uint64_t wait_ns) {
+  if (ld_acquire_sys(flag) >= epoch) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(flag) < epoch) {
+    if (globaltimer_ns() - t0 > wait_ns) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// ------------------------------------------------------------ layout phase --
+// Per block of 2048 (token, slot) assignments: per-expert counts, and each
+// assignment's rank among the block's assignments to the same expert, in
+// assignment order (stable).
+__global__ void __launch_bounds__(kLayoutThreads) layout_kernel(Params p) {
+  extern __shared__ int warp_hist[];  // [8][E]
+  const int E = p.num_experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.num_tokens * p.topk;
+  for (int i = threadIdx.x; i < 8 * E; i += blockDim.x) warp_hist[i] = 0;
+  __syncthreads();
+  const int a0 = blockIdx.x * kAssignPerLayoutBlock + warp * 256;
+  int* hist = warp_hist + warp * E;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int c = 0; c < 8; ++c) {
+    const int a = a0 + c * 32 + lane;
+    int e = -1;
+    if (a < total) {
+      const int64_t v = p.topk_idx[a];
+      e = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int before = (e >= 0) ? hist[e] : 0;
+    __syncwarp();
+    if (e >= 0) {
+      p.rank_in_block[a] = before + __popc(peers & lt_mask);
+      if ((__ffs(peers) - 1) == lane) hist[e] = before + __popc(peers);
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  int32_t* out_hist = p.block_hist + static_cast<int64_t>(blockIdx.x) * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 8; ++w) {
+      const int v = warp_hist[w * E + e];
+      warp_hist[w * E + e] = run;
+      run += v;
+    }
+    out_hist[e] = run;
+  }
+  __syncthreads();
+  for (int c = 0; c < 8; ++c) {
+    const int a = a0 + c * 32 + lane;
+    if (a < total) {
+      const int64_t v = p.topk_idx[a];
+      if (v >= 0 && v < E) p.rank_in_block[a] += hist[v];
+    }
+  }
+}
+
+// One block: turn block histograms into exclusive per-block bases, total the
+// per-expert counts, and publish them to every rank (row `rank` of each peer's
+// count matrix for this slot), then raise this rank's count flag there.
+__global__ void count_kernel(Params p) {
+  const int E = p.num_experts;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int b = 0; b < p.num_layout_blocks; ++b) {
+      int32_t* h = p.block_hist + static_cast<int64_t>(b) * E + e;
+      const int v = *h;
+      *h = run;
+      run += v;
+    }
+    p.my_counts[e] = run;
+  }
+  __syncthreads();
+  for (int d = 0; d < p.world; ++d) {
+    int32_t* dst = at<int32_t>(p.peers[d], p.lay.slot[p.slot].counts) + p.rank * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) dst[e] = p.my_counts[e];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world) {
+    uint64_t* f = at<uint64_t>(p.peers[threadIdx.x], p.lay.count_flag) + p.slot * p.world + p.rank;
+    st_release_sys(f, p.epoch);
+  }
+}
+
+// Shared state every scatter/combine block derives from the count matrix.
+struct CountView {
+  int exp_base[kMaxExperts];  // first row of expert e on its owner
+  int my_prefix[kMaxExperts]; // rows of expert e from ranks before this one
+  int recv_total;             // rows this rank receives
+  int overflow;               // some owner would exceed its capacity
+  int fail;
+};
+
+__device__ void build_count_view(const Params& p, CountView& cv) {
+  const int E = p.num_experts;
+  const int32_t* M = at<int32_t>(p.peers[p.rank], p.lay.slot[p.slot].counts);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int col = 0, before = 0;
+    for (int q = 0; q < p.world; ++q) {
+      const int v = M[q * E + e];
+      if (q < p.rank) before += v;
+      col += v;
+    }
+    cv.exp_base[e] = col;  // column sums for now
+    cv.my_prefix[e] = before;
+  }
+  __syncthreads();
+  if (threadIdx.x < p.world) {
+    const int d = threadIdx.x;
+    int run = 0;
+    for (int le = 0; le < p.per_rank; ++le) {
+      const int e = d * p.per_rank + le;
+      const int v = cv.exp_base[e];
+      cv.exp_base[e] = run;
+      run += v;
+    }
+    if (run > p.cap_rows) atomicOr(&cv.overflow, 1);
+    if (d == p.rank) cv.recv_total = run;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ bool wait_all_flags(const Params& p, uint64_t off, int* fail) {
+  if (threadIdx.x < p.world) {
+    const uint64_t* f = at<uint64_t>(p.peers[p.rank], off) + p.slot * p.world + threadIdx.x;
+    if (!wait_flag(f, p.epoch, p.wait_ns)) atomicOr(fail, 1);
+  }
+  __syncthreads();
+  return *fail == 0;
+}
+
+__global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
+  __shared__ CountView cv;
+  if (threadIdx.x == 0) {
+    cv.overflow = 0;
+    cv.fail = 0;
+    cv.recv_total = 0;
+  }
+  __syncthreads();
+  if (!wait_all_flags(p, p.lay.count_flag, &cv.fail)) {
+    if (threadIdx.x == 0) record_status(p.status, MOE_ERR_TIMEOUT);
+    return;
+  }
+  build_count_view(p, cv);
+  const bool overflow = cv.overflow != 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && overflow) record_status(p.status, MOE_ERR_CAPACITY);
+
+  const int E = p.num_experts;
+  if (blockIdx.x == 0) {
+    for (int le = threadIdx.x; le <= p.per_rank; le += blockDim.x) {
+      const int e = p.rank * p.per_rank + le;
+      p.offsets_out[le] = overflow ? 0 : (le < p.per_rank ? cv.exp_base[e] : cv.recv_total);
+    }
+    if (threadIdx.x == 0 && p.host_info != nullptr) {
+      volatile int64_t* hi = p.host_info + 2 * p.slot;
+      hi[1] = overflow ? -1 : cv.recv_total;
+      __threadfence_system();
+      hi[0] = static_cast<int64_t>(p.epoch);
+    }
+  }
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (kCommThreads / 32);
+  const int nvec = p.hidden / 8;  // 16-byte vectors per row
+  const SlotLayout sl = p.lay.slot[p.slot];
+  if (!overflow) {
+    for (int t = blockIdx.x * (kCommThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
+      uint4* dst[8];
+      int nd = 0;
+      for (int j = 0; j < p.topk; ++j) {
+        const int a = t * p.topk + j;
+        const int64_t ev = p.topk_idx[a];
+        if (ev < 0 || ev >= E) {
+          if (lane == 0) p.send_pos[a] = -1;
+          continue;
+        }
+        const int e = static_cast<int>(ev);
+        const int d = e / p.per_rank;
+        const int blk = a / kAssignPerLayoutBlock;
+        const int row = cv.exp_base[e] + cv.my_prefix[e] + p.block_hist[blk * E + e] +
+                        p.rank_in_block[a];
+        uint8_t* peer = p.peers[d];
+        dst[nd++] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+        if (lane < p.topk) {
+          at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
+              (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
+          at<float>(peer, sl.topk_w)[static_cast<int64_t>(row) * p.max_topk + lane] =
+              (lane == j) ? p.topk_w[a] : 0.0f;
+        }
+        if (lane == 0) {
+          at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
+          p.send_pos[a] = row;
+        }
+      }
+      constexpr int U = 4;
+      for (int base = 0; base < nvec; base += 32 * U) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * 32 + lane;
+          if (i < nvec) v[u] = __ldg(src + i);
+        }
+        for (int q = 0; q < nd; ++q) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int i = base + u * 32 + lane;
+            if (i < nvec) dst[q][i] = v[u];
+          }
+        }
+      }
+    }
+    if (p.pad_rows) {
+      // Rows of this rank's own receive area past the received count: no slot.
+      uint8_t* me = p.peers[p.rank];
+      const int64_t first = cv.recv_total;
+      const int64_t n = (p.cap_rows - first) * p.max_topk;
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+           i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        at<int64_t>(me, sl.topk_idx)[first * p.max_topk + i] = -1;
+        at<float>(me, sl.topk_w)[first * p.max_topk + i] = 0.0f;
+      }
+    }
+  } else {
+    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < p.num_tokens * p.topk;
+         a += gridDim.x * blockDim.x)
+      p.send_pos[a] = -1;
+  }
+
+  // Last block to finish tells every rank that this rank's rows have landed.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(p.done_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < p.world; ++d)
+        st_release_sys(at<uint64_t>(p.peers[d], p.lay.data_flag) + p.slot * p.world + p.rank,
+                       p.epoch);
+    }
+  }
+}
+
+__global__ void wait_data_kernel(Params p) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!wait_all_flags(p, p.lay.data_flag, &fail) && threadIdx.x == 0)
+    record_status(p.status, MOE_ERR_TIMEOUT);
+}
+
+// ----------------------------------------------------------------- combine --
+__global__ void ready_kernel(Params p) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world)
+    st_release_sys(at<uint64_t>(p.peers[threadIdx.x], p.lay.ready_flag) + p.slot * p.world + p.rank,
+                   p.epoch);
+}
+
+__device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, float s) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(s, f.x));
+    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(s, f.y));
+  }
+}
+
+__global__ void __launch_bounds__(kCommThreads) pull_kernel(Params p) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!wait_all_flags(p, p.lay.ready_flag, &fail)) {
+    if (threadIdx.x == 0) record_status(p.status, MOE_ERR_TIMEOUT);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (kCommThreads / 32);
+  const int nvec = p.hidden / 8;
+  const SlotLayout sl = p.lay.slot[p.slot];
+  for (int t = blockIdx.x * (kCommThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
+    const uint4* srcs[8];
+    float scale[8];
+    int ns = 0;
+    for (int j = 0; j < p.topk; ++j) {
+      const int a = t * p.topk + j;
+      const int row = p.send_pos[a];
+      if (row < 0) continue;
+      const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
+      srcs[ns] = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
+      scale[ns] = p.weighted ? p.topk_w[a] : 1.0f;
+      ++ns;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(t) * p.hidden);
+    constexpr int U = 2;
+    for (int base = 0; base < nvec; base += 32 * U) {
+      float acc[U][8];
+      uint4 v[U][8];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
+      }
+      // Issue every load of this step before reducing, to keep NVLink busy.
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q < ns) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int i = base + u * 32 + lane;
+            if (i < nvec) v[u][q] = srcs[q][i];
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q < ns) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int i = base + u * 32 + lane;
+            if (i < nvec) acc_bf16x8(acc[u], v[u][q], scale[q]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * 32 + lane;
+        if (i < nvec) {
+          uint4 o;
+          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) h[w] = __floats2bfloat162_rn(acc[u][2 * w], acc[u][2 * w + 1]);
+          dst[i] = o;
+        }
+      }
+    }
+  }
+}
+
+// Tokens per rank (counted once per token) and is_token_in_rank, DeepEP's layout.
+__global__ void token_rank_kernel(const int64_t* topk_idx, int num_tokens, int topk,
+                                  int num_experts, int per_rank, int world, bool* is_in_rank,
+                                  int32_t* tokens_per_rank) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= num_tokens) return;
+  unsigned long long mask = 0;
+  for (int j = 0; j < topk; ++j) {
+    const int64_t e = topk_idx[static_cast<int64_t>(t) * topk + j];
+    if (e >= 0 && e < num_experts) mask |= 1ull << (e / per_rank);
+  }
+  for (int d = 0; d < world; ++d) {
+    const bool in = (mask >> d) & 1ull;
+    if (is_in_rank != nullptr) is_in_rank[static_cast<int64_t>(t) * world + d] = in;
+    if (in && tokens_per_rank != nullptr) atomicAdd(tokens_per_rank + d, 1);
+  }
+}
+
+__global__ void expert_count_kernel(const int64_t* topk_idx, int64_t assigns, int num_experts,
+                                    int32_t* tokens_per_expert) {
+  const int64_t a = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (a >= assigns) return;
+  const int64_t e = topk_idx[a];
+  if (e >= 0 && e < num_experts) atomicAdd(tokens_per_expert + e, 1);
+}
+
+// -------------------------------------------------------------------- host --
+static uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+static SymLayout plan(int world, int num_experts, int hidden, int max_topk, int64_t cap) {
+  SymLayout L{};
+  uint64_t off = 0;
+  for (int s = 0; s < 2; ++s) {
+    SlotLayout& sl = L.slot[s];
+    sl.recv_x = off;
+    off = align_up(off + uint64_t(cap) * hidden * 2, 256);
+    sl.y = off;
+    off = align_up(off + uint64_t(cap) * hidden * 2, 256);
+    sl.topk_idx = off;
+    off = align_up(off + uint64_t(cap) * max_topk * 8, 256);
+    sl.topk_w = off;
+    off = align_up(off + uint64_t(cap) * max_topk * 4, 256);
+    sl.src = off;
+    off = align_up(off + uint64_t(cap) * 8, 256);
+    sl.counts = off;
+    off = align_up(off + uint64_t(world) * num_experts * 4, 256);
+  }
+  L.count_flag = off;
+  off = align_up(off + 2ull * world * 8, 256);
+  L.data_flag = off;
+  off = align_up(off + 2ull * world * 8, 256);
+  L.ready_flag = off;
+  off = align_up(off + 2ull * world * 8, 256);
+  L.bytes = off;
+  return L;
+}
+
+static Params base_params(const Endpoint* ep, int slot, uint64_t epoch, uint64_t wait_ns,
+                          int32_t* status) {
+  Params p{};
+  p.peers = ep->d_peers;
+  p.lay = ep->lay;
+  p.rank = ep->rank;
+  p.world = ep->world;
+  p.num_experts = ep->num_experts;
+  p.per_rank = ep->per_rank;
+  p.hidden = ep->hidden;
+  p.max_topk = ep->max_topk;
+  p.cap_rows = ep->cap_rows;
+  p.slot = slot;
+  p.epoch = epoch;
+  p.wait_ns = wait_ns;
+  p.status = status;
+  return p;
+}
+
+static int check_launch() { return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA; }
+
+}  // namespace ep
+}  // namespace moe
+
+using moe::ep::Endpoint;
+using moe::ep::Params;
+
+struct moe_ep_s : Endpoint {};
+
+extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden,
+                                 int32_t max_tokens, int32_t max_topk, int64_t max_recv_rows,
+                                 moe_ep_t* out) {
+  using namespace moe::ep;
+  if (out == nullptr || world < 1 || world > kMaxRanks || rank < 0 || rank >= world ||
+      num_experts < world || num_experts > kMaxExperts || num_experts % world != 0 ||
+      hidden <= 0 || hidden % 8 != 0 || max_tokens < 0 || max_topk < 1 || max_topk > 8 ||
+      max_recv_rows < 0 || max_recv_rows > INT32_MAX ||
+      int64_t(max_tokens) * max_topk > INT32_MAX)
+    return MOE_ERR_INVALID_ARG;
+  *out = nullptr;
+  moe_ep_s* ep = new (std::nothrow) moe_ep_s();
+  if (ep == nullptr) return MOE_ERR_CAPACITY;
+  ep->rank = rank;
+  ep->world = world;
+  ep->num_experts = num_experts;
+  ep->per_rank = num_experts / world;
+  ep->hidden = hidden;
+  ep->max_tokens = max_tokens;
+  ep->max_topk = max_topk;
+  ep->cap_rows = max_recv_rows;
+  ep->lay = plan(world, num_experts, hidden, max_topk, max_recv_rows);
+  if (cudaGetDevice(&ep->device) != cudaSuccess) {
+    delete ep;
+    return MOE_ERR_CUDA;
+  }
+  const int64_t assigns = std::max<int64_t>(1, int64_t(max_tokens) * max_topk);
+  ep->max_blocks = static_cast<int>((assigns + kAssignPerLayoutBlock - 1) / kAssignPerLayoutBlock);
+  uint64_t off = 0;
+  const uint64_t o_peers = off;
+  off = align_up(off + sizeof(void*) * kMaxRanks, 256);
+  const uint64_t o_hist = off;
+  off = align_up(off + uint64_t(ep->max_blocks) * num_experts * 4, 256);
+  const uint64_t o_rib = off;
+  off = align_up(off + uint64_t(assigns) * 4, 256);
+  uint64_t o_send[2], o_offs[2];
+  for (int s = 0; s < 2; ++s) {
+    o_send[s] = off;
+    off = align_up(off + uint64_t(assigns) * 4, 256);
+    o_offs[s] = off;
+    off = align_up(off + uint64_t(ep->per_rank + 1) * 4, 256);
+  }
+  const uint64_t o_cnt = off;
+  off = align_up(off + uint64_t(num_experts) * 4, 256);
+  const uint64_t o_done = off;
+  off = align_up(off + 256, 256);
+  if (cudaMalloc(&ep->sym, ep->lay.bytes) != cudaSuccess) {
+    delete ep;
+    return MOE_ERR_CUDA;
+  }
+  if (cudaMalloc(&ep->scratch, off) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void**>(&ep->host_info), 4 * sizeof(int64_t),
+                    cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+    cudaFree(ep->sym);
+    if (ep->scratch) cudaFree(ep->scratch);
+    delete ep;
+    return MOE_ERR_CUDA;
+  }
+  // Flags start at 0 (epochs start at 1); everything else is written before read.
+  if (cudaMemset(ep->sym, 0, ep->lay.bytes) != cudaSuccess ||
+      cudaMemset(ep->scratch, 0, off) != cudaSuccess) {
+    moe_ep_destroy(ep);
+    return MOE_ERR_CUDA;
+  }
+  std::memset(ep->host_info, 0, 4 * sizeof(int64_t));
+  ep->d_peers = reinterpret_cast<uint8_t**>(ep->scratch + o_peers);
+  ep->block_hist = reinterpret_cast<int32_t*>(ep->scratch + o_hist);
+  ep->rank_in_block = reinterpret_cast<int32_t*>(ep->scratch + o_rib);
+  for (int s = 0; s < 2; ++s) {
+    ep->send_pos[s] = reinterpret_cast<int32_t*>(ep->scratch + o_send[s]);
+    ep->offsets[s] = reinterpret_cast<int32_t*>(ep->scratch + o_offs[s]);
+  }
+  ep->my_counts = reinterpret_cast<int32_t*>(ep->scratch + o_cnt);
+  ep->done_ctr = reinterpret_cast<unsigned int*>(ep->scratch + o_done);
+  *out = ep;
+  return MOE_OK;
+}
+
+extern "C" int32_t moe_ep_destroy(moe_ep_t ep) {
+  if (ep == nullptr) return MOE_OK;
+  int rc = MOE_OK;
+  if (ep->sym && cudaFree(ep->sym) != cudaSuccess) rc = MOE_ERR_CUDA;
+  if (ep->scratch && cudaFree(ep->scratch) != cudaSuccess) rc = MOE_ERR_CUDA;
+  if (ep->host_info && cudaFreeHost(ep->host_info) != cudaSuccess) rc = MOE_ERR_CUDA;
+  delete ep;
+  return rc;
+}
+
+extern "C" int32_t moe_ep_buffer(moe_ep_t ep, void** base, uint64_t* bytes) {
+  if (ep == nullptr || base == nullptr || bytes == nullptr) return MOE_ERR_INVALID_ARG;
+  *base = ep->sym;
+  *bytes = ep->lay.bytes;
+  return MOE_OK;
+}
+
+extern "C" int32_t moe_ep_connect(moe_ep_t ep, void* const* peer_bases) {
+  if (ep == nullptr || peer_bases == nullptr) return MOE_ERR_INVALID_ARG;
+  for (int d = 0; d < ep->world; ++d) {
+    if (peer_bases[d] == nullptr) return MOE_ERR_INVALID_ARG;
+    ep->peers[d] = static_cast<uint8_t*>(peer_bases[d]);
+  }
+  if (ep->peers[ep->rank] != ep->sym) return MOE_ERR_INVALID_ARG;
+  return cudaMemcpy(ep->d_peers, ep->peers, sizeof(void*) * ep->world, cudaMemcpyHostToDevice) ==
+                 cudaSuccess
+             ? MOE_OK
+             : MOE_ERR_CUDA;
+}
+
+extern "C" int32_t moe_ep_views(moe_ep_t ep, int32_t slot, moe_ep_views_t* v) {
+  if (ep == nullptr || v == nullptr || slot < 0 || slot > 1) return MOE_ERR_INVALID_ARG;
+  const auto& sl = ep->lay.slot[slot];
+  v->recv_x = ep->sym + sl.recv_x;
+  v->expert_out = ep->sym + sl.y;
+  v->recv_topk_idx = reinterpret_cast<int64_t*>(ep->sym + sl.topk_idx);
+  v->recv_topk_weights = reinterpret_cast<float*>(ep->sym + sl.topk_w);
+  v->recv_src = reinterpret_cast<int32_t*>(ep->sym + sl.src);
+  v->expert_offsets = ep->offsets[slot];
+  v->send_pos = ep->send_pos[slot];
+  v->host_info = ep->host_info + 2 * slot;
+  v->cap_rows = ep->cap_rows;
+  v->max_topk = ep->max_topk;
+  return MOE_OK;
+}
+
+extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                         const float* topk_weights, int32_t num_tokens,
+                                         int32_t topk, int32_t slot, uint64_t epoch,
+                                         int32_t* status, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
+      num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk ||
+      (num_tokens > 0 && (x == nullptr || topk_idx == nullptr || topk_weights == nullptr)) ||
+      !moe::aligned16(x))
+    return MOE_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  Params p = base_params(ep, slot, epoch, 0, status);
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.topk_idx = topk_idx;
+  p.topk_w = topk_weights;
+  p.num_tokens = num_tokens;
+  p.topk = topk;
+  p.block_hist = ep->block_hist;
+  p.rank_in_block = ep->rank_in_block;
+  p.my_counts = ep->my_counts;
+  const int64_t assigns = int64_t(num_tokens) * topk;
+  p.num_layout_blocks = static_cast<int>((assigns + kAssignPerLayoutBlock - 1) / kAssignPerLayoutBlock);
+  if (p.num_layout_blocks > 0) {
+    layout_kernel<<<p.num_layout_blocks, kLayoutThreads, 8 * ep->num_experts * sizeof(int), stream>>>(p);
+    if (int rc = check_launch(); rc != MOE_OK) return rc;
+  }
+  count_kernel<<<1, 256, 0, stream>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                           const float* topk_weights, int32_t num_tokens,
+                                           int32_t topk, int32_t slot, uint64_t epoch,
+                                           int32_t num_blocks, int32_t pad_rows, uint64_t wait_ns,
+                                           int32_t* status, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
+      num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1)
+    return MOE_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  Params p = base_params(ep, slot, epoch, wait_ns, status);
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.topk_idx = topk_idx;
+  p.topk_w = topk_weights;
+  p.num_tokens = num_tokens;
+  p.topk = topk;
+  p.block_hist = ep->block_hist;
+  p.rank_in_block = ep->rank_in_block;
+  p.send_pos = ep->send_pos[slot];
+  p.offsets_out = ep->offsets[slot];
+  p.my_counts = ep->my_counts;
+  p.done_ctr = ep->done_ctr;
+  p.pad_rows = pad_rows ? 1 : 0;
+  p.host_info = ep->host_info;
+  if (cudaMemsetAsync(ep->done_ctr, 0, sizeof(unsigned int), stream) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  scatter_kernel<<<num_blocks, kCommThreads, 0, stream>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch, uint64_t wait_ns,
+                                       int32_t* status, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0) return MOE_ERR_INVALID_ARG;
+  Params p = base_params(ep, slot, epoch, wait_ns, status);
+  wait_data_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_combine_begin(moe_ep_t ep, int32_t slot, uint64_t epoch, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0) return MOE_ERR_INVALID_ARG;
+  Params p = base_params(ep, slot, epoch, 0, nullptr);
+  ready_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
+                                      const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                      int32_t slot, uint64_t epoch, int32_t weighted, void* out,
+                                      int32_t num_blocks, uint64_t wait_ns, int32_t* status,
+                                      void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
+      num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
+      (num_tokens > 0 && (out == nullptr || topk_idx == nullptr)) || !moe::aligned16(out) ||
+      (weighted && num_tokens > 0 && topk_weights == nullptr))
+    return MOE_ERR_INVALID_ARG;
+  Params p = base_params(ep, slot, epoch, wait_ns, status);
+  p.topk_idx = topk_idx;
+  p.topk_w = topk_weights;
+  p.num_tokens = num_tokens;
+  p.topk = topk;
+  p.send_pos = ep->send_pos[slot];
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.weighted = weighted ? 1 : 0;
+  pull_kernel<<<num_blocks, kCommThreads, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_layout(const int64_t* topk_idx, int32_t num_tokens,
+                                          int32_t topk, int32_t num_experts, int32_t world,
+                                          int32_t* tokens_per_rank, int32_t* tokens_per_expert,
+                                          bool* is_token_in_rank, void* stream_) {
+  using namespace moe::ep;
+  if (num_tokens < 0 || topk < 1 || world < 1 || world > 64 || num_experts < world ||
+      num_experts % world != 0 || (num_tokens > 0 && topk_idx == nullptr))
+    return MOE_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (tokens_per_rank && cudaMemsetAsync(tokens_per_rank, 0, world * 4, stream) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  if (tokens_per_expert &&
+      cudaMemsetAsync(tokens_per_expert, 0, num_experts * 4, stream) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  if (num_tokens == 0) return MOE_OK;
+  token_rank_kernel<<<(num_tokens + 255) / 256, 256, 0, stream>>>(
+      topk_idx, num_tokens, topk, num_experts, num_experts / world, world, is_token_in_rank,
+      tokens_per_rank);
+  if (int rc = check_launch(); rc != MOE_OK) return rc;
+  if (tokens_per_expert) {
+    const int64_t assigns = int64_t(num_tokens) * topk;
+    expert_count_kernel<<<static_cast<int>((assigns + 255) / 256), 256, 0, stream>>>(
+        topk_idx, assigns, num_experts, tokens_per_expert);
+    if (int rc = check_launch(); rc != MOE_OK) return rc;
+  }
+  return MOE_OK;
+}
+
+extern "C" int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                   const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                   int32_t slot, uint64_t epoch, int32_t num_blocks,
+                                   int32_t pad_rows, uint64_t wait_ns, int32_t* status,
+                                   void* stream) {
+  int rc = moe_ep_dispatch_begin(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
+                                 status, stream);
+  if (rc == MOE_OK)
+    rc = moe_ep_dispatch_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
+                                 num_blocks, pad_rows, wait_ns, status, stream);
+  if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
+  return rc;
+}
+
+extern "C" int32_t moe_ep_combine(moe_ep_t ep, const int64_t* topk_idx, const float* topk_weights,
+                                  int32_t num_tokens, int32_t topk, int32_t slot, uint64_t epoch,
+                                  int32_t weighted, void* out, int32_t num_blocks,
+                                  uint64_t wait_ns, int32_t* status, void* stream) {
+  int rc = moe_ep_combine_begin(ep, slot, epoch, stream);
+  if (rc == MOE_OK)
+    rc = moe_ep_combine_end(ep, topk_idx, topk_weights, num_tokens, topk, slot, epoch, weighted,
+                            out, num_blocks, wait_ns, status, stream);
+  return rc;
+}
+
+extern "C" int32_t moe_ipc_export(void* dev_ptr, void* handle_out) {
+  if (dev_ptr == nullptr || handle_out == nullptr) return MOE_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, dev_ptr) != cudaSuccess) return MOE_ERR_CUDA;
+  static_assert(sizeof(h) == MOE_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return MOE_OK;
+}
+
+extern "C" int32_t moe_ipc_import(const void* handle, void** dev_ptr_out) {
+  if (handle == nullptr || dev_ptr_out == nullptr) return MOE_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+             ? MOE_OK
+             : MOE_ERR_CUDA;
+}
+
+extern "C" int32_t moe_ipc_close(void* dev_ptr) {
+  if (dev_ptr == nullptr) return MOE_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}

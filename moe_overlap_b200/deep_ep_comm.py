@@ -1,0 +1,257 @@
+"""Token dispatch/combine with the call surface of src/deep_ep_comm.py.
+
+``DeepEPDispatcher(group, hidden_size, num_experts, num_sms=24)`` with
+``dispatch(x, topk_idx, topk_weights, previous_event=None) -> DispatchResult``
+and ``combine(expert_out, handle, previous_event=None) -> (combined_x, event)``
+keeps the reference wrapper's names, arguments and results; underneath it is
+the NVLink peer-memory exchange of ``libmoe_overlap_b200.so`` (csrc/ep.cu)
+instead of DeepEP.
+
+Differences a caller can see, all within the reference's contract:
+  * ``recv_x`` has one row per (token, selected local expert), grouped by local
+    expert (DeepEP sends one row per (token, rank) in source-rank order).  Each
+    row's ``recv_topk_idx``/``recv_topk_weights`` hold the expert in that row's
+    slot and -1 / 0 elsewhere, so the reference's per-slot loop
+    ``recv_y += experts(recv_x)[slot k] * gate_k`` (src/train_moe_baseline.py:
+    394-399) followed by the unweighted ``combine`` gives the same sums.
+  * ``DispatchResult`` also carries ``expert_offsets`` (int32 ``[E/W + 1]`` on
+    the device) and ``num_recv_tokens_per_expert``: ``recv_x`` can go straight
+    into ``persistent_grouped_gemm`` with no sort.
+  * With ``exact_size=False`` (DeepEP's ``num_worst_tokens`` mode) nothing
+    synchronises with the host: the results are capacity-sized views whose
+    unused rows have ``recv_topk_idx == -1``.
+  * ``combine(..., weighted=True)`` applies the dispatch's top-k weights inside
+    the reduction (fused weighted combine).
+Returned receive tensors are views of the dispatcher's buffers and stay valid
+until the dispatch after next (two slots alternate).
+"""
+from __future__ import annotations
+
+import collections
+import os
+from dataclasses import dataclass, field
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .ep import Endpoint, default_wait_ns
+
+
+class EventOverlap:
+    """CUDA event returned by dispatch/combine (DeepEP's EventOverlap surface)."""
+
+    def __init__(self, event: Optional[torch.cuda.Event] = None):
+        self.event = event
+
+    def current_stream_wait(self) -> None:
+        if self.event is not None:
+            torch.cuda.current_stream().wait_event(self.event)
+
+
+@dataclass
+class DispatchHandle:
+    slot: int
+    epoch: int
+    num_tokens: int
+    topk: int
+    topk_idx: torch.Tensor
+    topk_weights: torch.Tensor
+    x: torch.Tensor
+    recv_rows: Optional[int]
+    combined: bool = False
+
+
+@dataclass
+class DispatchResult:
+    recv_x: torch.Tensor
+    recv_topk_idx: torch.Tensor
+    recv_topk_weights: torch.Tensor
+    handle: object
+    event: object
+    expert_offsets: Optional[torch.Tensor] = None
+    num_recv_tokens_per_expert: Optional[torch.Tensor] = None
+    recv_src: Optional[torch.Tensor] = None
+    extra: dict = field(default_factory=dict)
+
+
+def _env_int(name: str, default: int) -> int:
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+class DeepEPDispatcher:
+    """Intranode dispatch/combine over NVLink peer memory (drop-in for the DeepEP wrapper).
+
+    ``num_sms`` is the grid of the exchange kernels (the reference reserves the
+    same number of SMs for DeepEP, src/train_moe_baseline.py:151-152).
+    Capacity: ``max_tokens_per_rank`` tokens per dispatch (env
+    ``MOE_B200_MAX_TOKENS``, default 8192), ``max_top_k`` (``MOE_B200_MAX_TOPK``,
+    default 8), and ``max_recv_rows`` rows received per rank per dispatch
+    (``MOE_B200_MAX_RECV_ROWS``, default world * max_tokens_per_rank *
+    min(2, experts per rank)); a dispatch that would exceed it fails on every
+    rank with MOE_ERR_CAPACITY instead of writing out of bounds.
+    """
+
+    def __init__(self, group: dist.ProcessGroup, hidden_size: int, num_experts: int,
+                 num_sms: int = 24, *, max_tokens_per_rank: Optional[int] = None,
+                 max_top_k: Optional[int] = None, max_recv_rows: Optional[int] = None,
+                 exact_size: bool = True):
+        self.group = group
+        self.hidden_size = hidden_size
+        self.num_experts = num_experts
+        self.world = group.size() if group is not None else 1
+        self.rank = group.rank() if group is not None else 0
+        if num_experts % self.world != 0:
+            raise ValueError(f"num_experts ({num_experts}) must be divisible by world_size ({self.world})")
+        if hidden_size % 8 != 0:
+            raise ValueError("hidden_size must be a multiple of 8 (16-byte rows)")
+        self.num_sms = max(1, int(num_sms))
+        self.exact_size = exact_size
+        self.experts_per_rank = num_experts // self.world
+        self.max_tokens = max_tokens_per_rank or _env_int("MOE_B200_MAX_TOKENS", 8192)
+        self.max_topk = max_top_k or _env_int("MOE_B200_MAX_TOPK", 8)
+        default_rows = self.world * self.max_tokens * min(2, self.experts_per_rank, self.max_topk)
+        self.max_recv_rows = max_recv_rows or _env_int("MOE_B200_MAX_RECV_ROWS", default_rows)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.wait_ns = default_wait_ns()
+        self._ep = Endpoint(self.rank, self.world, num_experts, hidden_size, self.max_tokens,
+                            self.max_topk, self.max_recv_rows)
+        bases = [0] * self.world
+        bases[self.rank] = self._ep.base
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self._ep.export_handle(), group=group)
+            for r in range(self.world):
+                if r != self.rank:
+                    bases[r] = self._ep.import_handle(handles[r])
+        self._ep.connect(bases)
+        if self.world > 1:
+            dist.barrier(group=group)
+        self.comm_stream = torch.cuda.Stream(self.device)
+        self._epoch = 0
+        self._outstanding: collections.deque[DispatchHandle] = collections.deque()
+        self._status = _lib.status_word(self.device)
+
+    # ------------------------------------------------------------------------
+    def _enter_comm(self, previous_event) -> None:
+        # Wait for the caller's stream as well as previous_event: the expert
+        # outputs handed to combine are produced there.
+        if previous_event is not None:
+            ev = getattr(previous_event, "event", previous_event)
+            if ev is not None:
+                self.comm_stream.wait_event(ev)
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+
+    def get_dispatch_layout(self, topk_idx: torch.Tensor, num_experts: int):
+        """(num_tokens_per_rank, None, num_tokens_per_expert, is_token_in_rank) as DeepEP returns."""
+        idx = topk_idx.to(torch.int64).contiguous()
+        t, k = idx.shape
+        per_rank = torch.empty(self.world, dtype=torch.int32, device=idx.device)
+        per_expert = torch.empty(num_experts, dtype=torch.int32, device=idx.device)
+        in_rank = torch.empty(t, self.world, dtype=torch.bool, device=idx.device)
+        _lib.check_call(
+            _lib.load().moe_ep_dispatch_layout(idx.data_ptr(), t, k, num_experts, self.world,
+                                               per_rank.data_ptr(), per_expert.data_ptr(),
+                                               in_rank.data_ptr(), _lib.stream_handle(idx.device)),
+            "moe_ep_dispatch_layout")
+        return per_rank, None, per_expert, in_rank
+
+    def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
+                 previous_event: Optional[object] = None, *,
+                 exact_size: Optional[bool] = None) -> DispatchResult:
+        if x.dtype != torch.bfloat16:
+            raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
+        if x.dim() != 2 or x.size(1) != self.hidden_size:
+            raise ValueError(f"x must be [num_tokens, {self.hidden_size}]")
+        if topk_idx.dim() != 2 or topk_idx.shape[0] != x.shape[0] or topk_weights.shape != topk_idx.shape:
+            raise ValueError("topk_idx and topk_weights must be [num_tokens, top_k]")
+        num_tokens, topk = topk_idx.shape
+        if num_tokens > self.max_tokens or topk > self.max_topk:
+            raise ValueError(
+                f"dispatch of {num_tokens} tokens x top-{topk} exceeds the dispatcher's capacity "
+                f"({self.max_tokens} x {self.max_topk}); raise MOE_B200_MAX_TOKENS / MOE_B200_MAX_TOPK")
+        if len(self._outstanding) >= 2:
+            raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
+        exact = self.exact_size if exact_size is None else exact_size
+        _lib.check_status(self.device)
+        self._epoch += 1
+        epoch, slot = self._epoch, self._epoch % 2
+        self._enter_comm(previous_event)
+        with torch.cuda.stream(self.comm_stream):
+            xc = x.contiguous()
+            ic = topk_idx.to(torch.int64).contiguous()
+            wc = topk_weights.to(torch.float32).contiguous()
+            if xc.data_ptr() % 16 != 0:
+                xc = xc.clone()
+            self._ep.dispatch(xc, ic, wc, slot, epoch, self.num_sms, not exact, self.wait_ns,
+                              self._status)
+            offs = self._ep.slots[slot].expert_offsets
+            per_expert = offs[1:] - offs[:-1]
+            event = torch.cuda.Event()
+            event.record(self.comm_stream)
+        for t in (x, topk_idx, topk_weights):
+            t.record_stream(self.comm_stream)
+        views = self._ep.slots[slot]
+        rows = self._ep.received_rows(slot, epoch) if exact else views.recv_x.shape[0]
+        handle = DispatchHandle(slot, epoch, num_tokens, topk, ic, wc, xc, rows if exact else None)
+        self._outstanding.append(handle)
+        kcols = views.recv_topk_idx.stride(0)
+        return DispatchResult(
+            recv_x=views.recv_x[:rows],
+            recv_topk_idx=views.recv_topk_idx.as_strided((rows, topk), (kcols, 1)),
+            recv_topk_weights=views.recv_topk_weights.as_strided((rows, topk), (kcols, 1)),
+            handle=handle,
+            event=EventOverlap(event),
+            expert_offsets=offs,
+            num_recv_tokens_per_expert=per_expert,
+            recv_src=views.recv_src[:rows],
+        )
+
+    def expert_out_buffer(self, handle: DispatchHandle) -> torch.Tensor:
+        """The slot's expert-output rows: write here (e.g. as the GEMM's output) to skip a copy."""
+        return self._ep.slots[handle.slot].expert_out
+
+    def combine(self, expert_out: torch.Tensor, handle: DispatchHandle,
+                previous_event: Optional[object] = None, *,
+                weighted: bool = False) -> Tuple[torch.Tensor, object]:
+        if not isinstance(handle, DispatchHandle) or handle.combined:
+            raise RuntimeError("combine needs the handle of an outstanding dispatch")
+        if expert_out.dtype != torch.bfloat16 or expert_out.dim() != 2 or \
+                expert_out.size(1) != self.hidden_size:
+            raise ValueError(f"expert_out must be bf16 [rows, {self.hidden_size}]")
+        if self._outstanding and self._outstanding[0] is not handle:
+            raise RuntimeError("combine the oldest outstanding dispatch first")
+        _lib.check_status(self.device)
+        views = self._ep.slots[handle.slot]
+        self._enter_comm(previous_event)
+        out = torch.empty((handle.num_tokens, self.hidden_size), dtype=torch.bfloat16,
+                          device=self.device)
+        with torch.cuda.stream(self.comm_stream):
+            if expert_out.data_ptr() != views.expert_out.data_ptr():
+                rows = expert_out.shape[0]
+                if rows > views.expert_out.shape[0]:
+                    raise ValueError("expert_out has more rows than the receive buffer")
+                views.expert_out[:rows].copy_(expert_out)
+            self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot, handle.epoch,
+                             weighted, out, self.num_sms, self.wait_ns, self._status)
+            event = torch.cuda.Event()
+            event.record(self.comm_stream)
+        expert_out.record_stream(self.comm_stream)
+        out.record_stream(self.comm_stream)
+        handle.combined = True
+        self._outstanding.popleft()
+        return out, EventOverlap(event)
+
+    def close(self) -> None:
+        """Collective: every rank unmaps its peers' buffers before any rank frees its own."""
+        if self._ep is not None:
+            torch.cuda.synchronize(self.device)
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self._ep.close_imports()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self._ep.close()
+            self._ep = None

@@ -1,0 +1,275 @@
+"""Host side of the expert-parallel token exchange (NVLink peer memory).
+
+``Endpoint`` wraps one rank's ``moe_ep_t`` from the C ABI and exposes its
+symmetric buffer as zero-copy torch views.  ``LocalGroup`` connects several
+endpoints that live on the same GPU in one process; it runs each phase for
+every rank before the next phase starts, so no kernel ever waits for a launch
+that comes after it.  It is how the multi-rank exchange is exercised on a
+single GPU.  Multi-process use goes through ``DeepEPDispatcher``
+(``deep_ep_comm.py``), which shares the buffers with CUDA IPC.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+
+class _DeviceBytes:
+    """Minimal __cuda_array_interface__ exporter that keeps ``owner`` alive."""
+
+    def __init__(self, ptr: int, nbytes: int, owner):
+        self.__cuda_array_interface__ = {
+            "shape": (nbytes,),
+            "typestr": "|u1",
+            "data": (ptr, False),
+            "version": 3,
+            "strides": None,
+        }
+        self._owner = owner
+
+
+def device_bytes(ptr: int, nbytes: int, device: torch.device, owner) -> torch.Tensor:
+    return torch.as_tensor(_DeviceBytes(ptr, nbytes, owner), device=device)
+
+
+class _Views(ctypes.Structure):
+    _fields_ = [
+        ("recv_x", ctypes.c_void_p),
+        ("expert_out", ctypes.c_void_p),
+        ("recv_topk_idx", ctypes.c_void_p),
+        ("recv_topk_weights", ctypes.c_void_p),
+        ("recv_src", ctypes.c_void_p),
+        ("expert_offsets", ctypes.c_void_p),
+        ("send_pos", ctypes.c_void_p),
+        ("host_info", ctypes.c_void_p),
+        ("cap_rows", ctypes.c_int64),
+        ("max_topk", ctypes.c_int32),
+    ]
+
+
+def default_wait_ns() -> int:
+    """Bound on every device-side wait of the exchange (MOE_B200_EP_TIMEOUT_S, default 30 s)."""
+    return int(float(os.environ.get("MOE_B200_EP_TIMEOUT_S", "30")) * 1e9)
+
+
+@dataclass
+class SlotViews:
+    recv_x: torch.Tensor           # [cap, H] bf16
+    expert_out: torch.Tensor       # [cap, H] bf16
+    recv_topk_idx: torch.Tensor    # [cap, max_topk] int64
+    recv_topk_weights: torch.Tensor  # [cap, max_topk] float32
+    recv_src: torch.Tensor         # [cap, 2] int32
+    expert_offsets: torch.Tensor   # [E_local + 1] int32
+    send_pos: torch.Tensor         # [max_tokens * max_topk] int32
+    host_info: ctypes.Array        # mapped host {epoch, rows}
+
+
+class Endpoint:
+    """One rank's exchange endpoint (symmetric buffer + scratch), on the current device."""
+
+    def __init__(self, rank: int, world: int, num_experts: int, hidden: int, max_tokens: int,
+                 max_topk: int, max_recv_rows: int):
+        self.lib = _lib.load()
+        self.rank, self.world, self.num_experts, self.hidden = rank, world, num_experts, hidden
+        self.experts_per_rank = num_experts // world
+        self.max_tokens, self.max_topk, self.cap_rows = max_tokens, max_topk, max_recv_rows
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        handle = ctypes.c_void_p()
+        _lib.check_call(
+            self.lib.moe_ep_create(rank, world, num_experts, hidden, max_tokens, max_topk,
+                                   max_recv_rows, ctypes.byref(handle)),
+            "moe_ep_create",
+        )
+        self.handle = handle
+        base, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+        _lib.check_call(self.lib.moe_ep_buffer(handle, ctypes.byref(base), ctypes.byref(nbytes)),
+                        "moe_ep_buffer")
+        self.base, self.nbytes = int(base.value), int(nbytes.value)
+        self._imported: list[int] = []
+        self.slots = [self._slot_views(s) for s in range(2)]
+
+    def _slot_views(self, slot: int) -> SlotViews:
+        v = _Views()
+        _lib.check_call(self.lib.moe_ep_views(self.handle, slot, ctypes.byref(v)), "moe_ep_views")
+        cap, k, h = int(v.cap_rows), int(v.max_topk), self.hidden
+        dev = self.device
+
+        def raw(ptr, nbytes):
+            return device_bytes(int(ptr), int(nbytes), dev, self)
+
+        return SlotViews(
+            recv_x=raw(v.recv_x, cap * h * 2).view(torch.bfloat16).view(cap, h),
+            expert_out=raw(v.expert_out, cap * h * 2).view(torch.bfloat16).view(cap, h),
+            recv_topk_idx=raw(v.recv_topk_idx, cap * k * 8).view(torch.int64).view(cap, k),
+            recv_topk_weights=raw(v.recv_topk_weights, cap * k * 4).view(torch.float32).view(cap, k),
+            recv_src=raw(v.recv_src, cap * 8).view(torch.int32).view(cap, 2),
+            expert_offsets=raw(v.expert_offsets, (self.experts_per_rank + 1) * 4)
+            .view(torch.int32),
+            send_pos=raw(v.send_pos, max(1, self.max_tokens * self.max_topk) * 4).view(torch.int32),
+            host_info=(ctypes.c_int64 * 2).from_address(int(v.host_info)),
+        )
+
+    # ------------------------------------------------------------ connection --
+    def export_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        _lib.check_call(self.lib.moe_ipc_export(ctypes.c_void_p(self.base), buf), "moe_ipc_export")
+        return buf.raw
+
+    def import_handle(self, handle: bytes) -> int:
+        ptr = ctypes.c_void_p()
+        _lib.check_call(self.lib.moe_ipc_import(handle, ctypes.byref(ptr)), "moe_ipc_import")
+        self._imported.append(int(ptr.value))
+        return int(ptr.value)
+
+    def connect(self, peer_bases: list[int]) -> None:
+        arr = (ctypes.c_void_p * self.world)(*peer_bases)
+        _lib.check_call(self.lib.moe_ep_connect(self.handle, arr), "moe_ep_connect")
+
+    def close_imports(self) -> None:
+        """Unmaps the peer buffers imported with import_handle."""
+        torch.cuda.synchronize(self.device)
+        for ptr in self._imported:
+            self.lib.moe_ipc_close(ctypes.c_void_p(ptr))
+        self._imported.clear()
+
+    def close(self) -> None:
+        if self.handle is None:
+            return
+        self.close_imports()
+        self.lib.moe_ep_destroy(self.handle)
+        self.handle = None
+
+    # ---------------------------------------------------------------- phases --
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def dispatch_begin(self, x, topk_idx, topk_w, slot, epoch, status):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_begin(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                           topk_w.data_ptr(), t, k, slot, epoch,
+                                           status.data_ptr(), self._stream()),
+            "moe_ep_dispatch_begin")
+
+    def dispatch_scatter(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows, wait_ns,
+                         status):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_scatter(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                             topk_w.data_ptr(), t, k, slot, epoch, num_blocks,
+                                             1 if pad_rows else 0, wait_ns, status.data_ptr(),
+                                             self._stream()),
+            "moe_ep_dispatch_scatter")
+
+    def dispatch_end(self, slot, epoch, wait_ns, status):
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_end(self.handle, slot, epoch, wait_ns, status.data_ptr(),
+                                         self._stream()),
+            "moe_ep_dispatch_end")
+
+    def combine_begin(self, slot, epoch):
+        _lib.check_call(self.lib.moe_ep_combine_begin(self.handle, slot, epoch, self._stream()),
+                        "moe_ep_combine_begin")
+
+    def combine_end(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns,
+                    status):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_combine_end(self.handle, topk_idx.data_ptr(),
+                                        topk_w.data_ptr() if topk_w is not None else None, t, k,
+                                        slot, epoch, 1 if weighted else 0, out.data_ptr(),
+                                        num_blocks, wait_ns, status.data_ptr(), self._stream()),
+            "moe_ep_combine_end")
+
+    def dispatch(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows, wait_ns, status):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                     topk_w.data_ptr(), t, k, slot, epoch, num_blocks,
+                                     1 if pad_rows else 0, wait_ns, status.data_ptr(),
+                                     self._stream()),
+            "moe_ep_dispatch")
+
+    def combine(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns, status):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_combine(self.handle, topk_idx.data_ptr(),
+                                    topk_w.data_ptr() if topk_w is not None else None, t, k, slot,
+                                    epoch, 1 if weighted else 0, out.data_ptr(), num_blocks,
+                                    wait_ns, status.data_ptr(), self._stream()),
+            "moe_ep_combine")
+
+    def received_rows(self, slot: int, epoch: int, timeout_s: float = 60.0) -> int:
+        """Rows received in ``slot`` for ``epoch``, read from mapped host memory.
+
+        Spins on the host until the scatter kernel has published the count, as
+        DeepEP's dispatch does for its receive sizes (deep_ep.cpp:630-653).
+        """
+        import time
+
+        info = self.slots[slot].host_info
+        t0 = time.monotonic()
+        while info[0] != epoch:
+            if time.monotonic() - t0 > timeout_s:
+                raise _lib.MoeError(_lib.MOE_ERR_TIMEOUT, "waiting for the dispatch receive count")
+            time.sleep(0)
+        rows = int(info[1])
+        if rows < 0:
+            raise _lib.MoeError(_lib.MOE_ERR_CAPACITY, "dispatch receive buffer too small")
+        return rows
+
+    def __del__(self):
+        try:
+            if self.handle is not None and self.lib is not None:
+                self.lib.moe_ep_destroy(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+
+class LocalGroup:
+    """``world`` endpoints on the current GPU in this process, wired to each other.
+
+    ``dispatch``/``combine`` run one phase for every rank before the next phase,
+    so each bounded wait finds its flag already raised by an earlier launch.
+    """
+
+    def __init__(self, world: int, num_experts: int, hidden: int, max_tokens: int, max_topk: int,
+                 max_recv_rows: int, num_blocks: int = 16):
+        self.world, self.num_blocks = world, num_blocks
+        self.eps = [Endpoint(r, world, num_experts, hidden, max_tokens, max_topk, max_recv_rows)
+                    for r in range(world)]
+        bases = [ep.base for ep in self.eps]
+        for ep in self.eps:
+            ep.connect(bases)
+        self.epoch = 0
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.eps[0].device)
+        self.wait_ns = default_wait_ns()
+
+    def dispatch(self, xs, idxs, ws, pad_rows: bool = False):
+        self.epoch += 1
+        slot, epoch = self.epoch % 2, self.epoch
+        for r, ep in enumerate(self.eps):
+            ep.dispatch_begin(xs[r], idxs[r], ws[r], slot, epoch, self.status)
+        for r, ep in enumerate(self.eps):
+            ep.dispatch_scatter(xs[r], idxs[r], ws[r], slot, epoch, self.num_blocks, pad_rows,
+                                self.wait_ns, self.status)
+        for ep in self.eps:
+            ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
+        return slot, epoch
+
+    def combine(self, idxs, ws, slot, epoch, weighted, outs):
+        for ep in self.eps:
+            ep.combine_begin(slot, epoch)
+        for r, ep in enumerate(self.eps):
+            ep.combine_end(idxs[r], ws[r], slot, epoch, weighted, outs[r], self.num_blocks,
+                           self.wait_ns, self.status)
+
+    def close(self):
+        for ep in self.eps:
+            ep.close()

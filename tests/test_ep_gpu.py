@@ -1,0 +1,168 @@
+"""GPU parity of the expert-parallel exchange against the CPU oracle (oracle/ep.py).
+
+W ranks are emulated on one GPU by LocalGroup (every rank's endpoint in this
+process, each phase run for all ranks before the next), so the peer stores,
+flags and pulls are the same code the multi-GPU path runs.  Everything the
+exchange moves is compared bit for bit: received rows (bf16 copies), local
+expert ids, weights, source tags, expert_offsets and send positions; the
+combine sums in fp32 in slot order exactly as the oracle does, so it is
+bit-exact too.  The DeepEP test invariants (thirdParty/DeepEP/tests/
+test_intranode.py:62-66 layout, :119-131 counts and local ids) are checked
+through the oracle's layout.
+"""
+import numpy as np
+import pytest
+import torch
+
+from moe_overlap_b200 import _lib
+from moe_overlap_b200.ep import LocalGroup
+from oracle import ep as oep
+from tests._inputs import to_storage
+
+pytestmark = pytest.mark.gpu
+
+
+def routing(world, tokens, num_experts, topk, seed, hidden=256, drop=0.05):
+    g = torch.Generator().manual_seed(seed)
+    xs, idxs, ws = [], [], []
+    for r in range(world):
+        xs.append(torch.randn(tokens, hidden, generator=g).to(torch.bfloat16))
+        scores = torch.rand(tokens, num_experts, generator=g)
+        idx = torch.topk(scores, topk, dim=-1).indices.to(torch.int64)
+        idx[torch.rand(tokens, topk, generator=g) < drop] = -1
+        idxs.append(idx)
+        ws.append(torch.rand(tokens, topk, generator=g).to(torch.float32))
+    return xs, idxs, ws
+
+
+def test_dispatch_layout_matches_oracle(cuda_device):
+    lib = _lib.load()
+    xs, idxs, _ = routing(1, 3000, 16, 4, seed=1)
+    idx = idxs[0].to(cuda_device)
+    for world in (1, 2, 4, 8):
+        per_rank = torch.empty(world, dtype=torch.int32, device=cuda_device)
+        per_expert = torch.empty(16, dtype=torch.int32, device=cuda_device)
+        in_rank = torch.empty(3000, world, dtype=torch.bool, device=cuda_device)
+        rc = lib.moe_ep_dispatch_layout(idx.data_ptr(), 3000, 4, 16, world, per_rank.data_ptr(),
+                                        per_expert.data_ptr(), in_rank.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        want = oep.dispatch_layout(idxs[0].numpy(), 16, world)
+        assert np.array_equal(per_rank.cpu().numpy(), want[0])
+        assert np.array_equal(per_expert.cpu().numpy(), want[1])
+        assert np.array_equal(in_rank.cpu().numpy(), want[2])
+
+
+@pytest.mark.parametrize("world,tokens,topk,num_experts", [
+    (1, 700, 2, 16), (2, 513, 2, 16), (4, 300, 3, 16), (8, 257, 2, 16), (8, 64, 8, 64)])
+def test_dispatch_combine_match_oracle(cuda_device, world, tokens, topk, num_experts):
+    hidden = 256
+    xs, idxs, ws = routing(world, tokens, num_experts, topk, seed=world * 100 + topk, hidden=hidden)
+    cap = world * tokens * topk
+    grp = LocalGroup(world, num_experts, hidden, tokens, topk, cap, num_blocks=7)
+    recv, send_pos = oep.dispatch([to_storage(x) for x in xs], [i.numpy() for i in idxs],
+                                  [w.numpy() for w in ws], num_experts)
+    try:
+        dx = [x.to(cuda_device) for x in xs]
+        di = [i.to(cuda_device) for i in idxs]
+        dw = [w.to(cuda_device) for w in ws]
+        for weighted in (False, True):
+            slot, epoch = grp.dispatch(dx, di, dw, pad_rows=True)
+            torch.cuda.synchronize()
+            assert int(grp.status.item()) == 0, _lib.status_string(int(grp.status.item()))
+            ys = []
+            for d, ep in enumerate(grp.eps):
+                v = ep.slots[slot]
+                want = recv[d]
+                n = int(want["offsets"][-1])
+                assert np.array_equal(v.expert_offsets.cpu().numpy(), want["offsets"])
+                assert np.array_equal(to_storage(v.recv_x[:n]), want["x"])
+                assert np.array_equal(v.recv_topk_idx[:n, :topk].cpu().numpy(), want["topk_idx"])
+                assert np.array_equal(v.recv_topk_weights[:n, :topk].cpu().numpy(),
+                                      want["topk_weights"])
+                assert np.array_equal(v.recv_src[:n, 0].cpu().numpy(), want["src_rank"])
+                assert np.array_equal(v.recv_src[:n, 1].cpu().numpy(), want["src_token"])
+                assert bool((v.recv_topk_idx[n:] == -1).all())  # padded rows
+                # DeepEP invariants: local ids in {-1} u [0, E/W), per-expert counts.
+                ids = v.recv_topk_idx[:n, :topk]
+                assert bool(((ids == -1) | ((ids >= 0) & (ids < num_experts // world))).all())
+                for le, c in enumerate(np.diff(want["offsets"])):
+                    assert int((ids == le).sum()) == c
+                # Expert outputs for the combine: a deterministic function of the rows.
+                y = (v.recv_x[:n].float() * (1.5 + d) - 0.25).to(torch.bfloat16)
+                v.expert_out[:n].copy_(y)
+                ys.append(to_storage(y))
+            for r, ep in enumerate(grp.eps):
+                got = ep.slots[slot].send_pos[: tokens * topk].view(tokens, topk).cpu().numpy()
+                assert np.array_equal(got, send_pos[r])
+            outs = [torch.empty(tokens, hidden, dtype=torch.bfloat16, device=cuda_device)
+                    for _ in range(world)]
+            grp.combine(di, dw, slot, epoch, weighted, outs)
+            torch.cuda.synchronize()
+            assert int(grp.status.item()) == 0
+            want = oep.combine(ys, [i.numpy() for i in idxs], send_pos, num_experts,
+                               weights=[w.numpy() for w in ws] if weighted else None)
+            for r in range(world):
+                assert np.array_equal(to_storage(outs[r]), want[r]), (weighted, r)
+    finally:
+        grp.close()
+
+
+def test_two_slots_alternate_and_epochs_advance(cuda_device):
+    world, tokens, topk, hidden = 4, 200, 2, 128
+    grp = LocalGroup(world, 16, hidden, tokens, topk, world * tokens * topk, num_blocks=3)
+    try:
+        seen = []
+        for it in range(5):
+            xs, idxs, ws = routing(world, tokens, 16, topk, seed=50 + it, hidden=hidden)
+            slot, epoch = grp.dispatch([x.to(cuda_device) for x in xs],
+                                       [i.to(cuda_device) for i in idxs],
+                                       [w.to(cuda_device) for w in ws])
+            torch.cuda.synchronize()
+            assert int(grp.status.item()) == 0
+            recv, _ = oep.dispatch([to_storage(x) for x in xs], [i.numpy() for i in idxs],
+                                   [w.numpy() for w in ws], 16)
+            for d, ep in enumerate(grp.eps):
+                n = int(recv[d]["offsets"][-1])
+                assert np.array_equal(to_storage(ep.slots[slot].recv_x[:n]), recv[d]["x"])
+                assert ep.received_rows(slot, epoch) == n
+            seen.append((slot, epoch))
+        assert [s for s, _ in seen] == [1, 0, 1, 0, 1] and [e for _, e in seen] == [1, 2, 3, 4, 5]
+    finally:
+        grp.close()
+
+
+def test_capacity_overflow_is_reported_not_written(cuda_device):
+    world, tokens, topk, hidden = 2, 300, 2, 64
+    xs, idxs, ws = routing(world, tokens, 8, topk, seed=9, hidden=hidden, drop=0.0)
+    grp = LocalGroup(world, 8, hidden, tokens, topk, max_recv_rows=40, num_blocks=4)
+    try:
+        grp.dispatch([x.to(cuda_device) for x in xs], [i.to(cuda_device) for i in idxs],
+                     [w.to(cuda_device) for w in ws])
+        torch.cuda.synchronize()
+        assert int(grp.status.item()) == _lib.MOE_ERR_CAPACITY
+        for ep in grp.eps:
+            assert int(ep.slots[1].expert_offsets[-1]) == 0
+            with pytest.raises(_lib.MoeError):
+                ep.received_rows(1, 1)
+    finally:
+        grp.close()
+
+
+def test_wait_that_nobody_satisfies_times_out_with_status(cuda_device):
+    """Rank 1 never posts its counts: rank 0's bounded wait must expire and report."""
+    world, tokens, topk, hidden = 2, 64, 2, 64
+    xs, idxs, ws = routing(world, tokens, 8, topk, seed=3, hidden=hidden)
+    grp = LocalGroup(world, 8, hidden, tokens, topk, world * tokens * topk, num_blocks=2)
+    try:
+        ep0 = grp.eps[0]
+        x, i, w = xs[0].to(cuda_device), idxs[0].to(cuda_device), ws[0].to(cuda_device)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        ep0.dispatch_begin(x, i, w, 1, 1, status)
+        ep0.dispatch_scatter(x, i, w, 1, 1, 2, False, 50_000_000, status)  # 50 ms bound
+        torch.cuda.synchronize()
+        assert int(status.item()) == _lib.MOE_ERR_TIMEOUT
+        # The context is still usable afterwards.
+        assert float((torch.ones(4, device=cuda_device) * 2).sum()) == 8.0
+    finally:
+        grp.close()
