@@ -76,6 +76,25 @@ class DispatchResult:
     extra: dict = field(default_factory=dict)
 
 
+def exchange_buffers(group, rank: int, world: int, own_base: int, export_handle,
+                     import_handle) -> list[int]:
+    """Every rank's symmetric buffer as addressable here, indexed by rank.
+
+    Each rank exports an IPC handle for its own buffer, the handles are
+    gathered over ``group`` (as DeepEP's Buffer does, buffer.py:96-101), and the
+    peers' handles are opened locally; this rank's entry is its own pointer.
+    """
+    bases = [0] * world
+    bases[rank] = own_base
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, export_handle(), group=group)
+        for r in range(world):
+            if r != rank:
+                bases[r] = import_handle(handles[r])
+    return bases
+
+
 def _env_int(name: str, default: int) -> int:
     v = os.environ.get(name)
     return int(v) if v not in (None, "") else default
@@ -118,14 +137,8 @@ class DeepEPDispatcher:
         self.wait_ns = default_wait_ns()
         self._ep = Endpoint(self.rank, self.world, num_experts, hidden_size, self.max_tokens,
                             self.max_topk, self.max_recv_rows)
-        bases = [0] * self.world
-        bases[self.rank] = self._ep.base
-        if self.world > 1:
-            handles = [None] * self.world
-            dist.all_gather_object(handles, self._ep.export_handle(), group=group)
-            for r in range(self.world):
-                if r != self.rank:
-                    bases[r] = self._ep.import_handle(handles[r])
+        bases = exchange_buffers(group, self.rank, self.world, self._ep.base,
+                                 self._ep.export_handle, self._ep.import_handle)
         self._ep.connect(bases)
         if self.world > 1:
             dist.barrier(group=group)
