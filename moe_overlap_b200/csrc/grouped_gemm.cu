@@ -26,9 +26,11 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/moe_overlap.h"
+#include "gemm_common.cuh"
 #include "host_common.h"
 #include "ptx.cuh"
 #include "sched.cuh"
@@ -48,7 +50,7 @@ constexpr int A_STAGE_BYTES = BM * BK * 2;    // 16 KiB
 constexpr int B_STAGE_BYTES = BK * BN * 2;    // 32 KiB
 constexpr int B_NCHUNK_BYTES = BK * 64 * 2;   // one 64-column slab of an N-major B stage
 constexpr uint32_t TMEM_COLS = 2 * BN;        // two fp32 accumulators of 128 x 256
-constexpr int MAX_EXPERTS = 1024;
+constexpr int MAX_EXPERTS = kMaxExperts;
 
 struct Ctrl {
   uint64_t full[STAGES];
@@ -63,47 +65,9 @@ struct Ctrl {
   int abort;
 };
 
-struct Params {
-  void* c;
-  int64_t ldc;
-  const void* offsets;
-  int offsets_int64;
-  int m_total;
-  int k;
-  int n;
-  int num_experts;
-  int activation;
-  int use_atomic;
-  int tile_order;
-  int* work_counter;
-  int32_t* status;
-};
-
 __host__ __device__ constexpr size_t smem_bytes(int num_experts) {
   return 1024 /* alignment slack */ + size_t(STAGES) * (A_STAGE_BYTES + B_STAGE_BYTES) +
          ((sizeof(Ctrl) + 15) / 16) * 16 + size_t(3) * 4 * (num_experts + 1);
-}
-
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
-}
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  if constexpr (BF16) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-  } else {
-    __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-}
-
-// All lanes of the calling warp wait; the outcome is made warp-uniform so a
-// following .sync.aligned tcgen05 instruction is never reached by part of a warp.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const volatile int* abort) {
-  const bool ok = mbar_wait(bar, parity, abort);
-  return __all_sync(0xffffffffu, ok);
 }
 
 template <bool BF16, bool B_MN_MAJOR>
@@ -163,18 +127,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int total_tiles = tile_prefix[p.num_experts];
   const int num_kb = (p.k + BK - 1) / BK;
   volatile int* abort_flag = &ctrl->abort;
-  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
 
   if (total_tiles == 0) {
     // No expert owns a row: the result is all zeros (src/triton_grouped_gemm.py:369-371).
-    const int64_t chunks_per_row = p.n / 8;
-    const int64_t total_chunks = int64_t(p.m_total) * chunks_per_row;
-    for (int64_t i = int64_t(blockIdx.x) * NUM_THREADS + threadIdx.x; i < total_chunks;
-         i += int64_t(gridDim.x) * NUM_THREADS) {
-      const int64_t r = i / chunks_per_row, cc = i % chunks_per_row;
-      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.c) + r * p.ldc + cc * 8) =
-          make_uint4(0, 0, 0, 0);
-    }
+    zero_output<BF16>(p, NUM_THREADS);
   } else if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
@@ -317,7 +273,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue --
     const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
-    const int row_in_tile = quad * 32 + lane;
     int q = 0;
     uint32_t qphase = 0;
     int acc = 0;
@@ -341,42 +296,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const bool row_ok = row_in_tile < s.y;
-      T* crow = reinterpret_cast<T*>(p.c) + (int64_t(s.x) + row_in_tile) * p.ldc;
-      const uint32_t t_base = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_base + ch * 32, r);
-        tmem_wait_ld();
-        const int col = s.z + ch * 32;
-        if (row_ok && col < p.n) {
-          uint32_t packed[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float lo = __uint_as_float(r[2 * j]);
-            float hi = __uint_as_float(r[2 * j + 1]);
-            if (p.activation == MOE_ACT_GELU) {
-              lo = gelu_erf(lo);
-              hi = gelu_erf(hi);
-            }
-            packed[j] = pack2<BF16>(lo, hi);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(crow + col);
-          if (col + 32 <= p.n) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
-                                  packed[4 * v + 3]);
-          } else {
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (col + 8 * v + 8 <= p.n)
-                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
-                                    packed[4 * v + 3]);
-          }
-        }
-      }
+      store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
+                              lane, s.x, s.y, s.z, p);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->tempty[acc]));
@@ -401,6 +322,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ------------------------------------------------------------------- host --
+// MOE_B200_GEMM_KERNEL=1 forces the 1-SM kernel, =2 (default) the CTA-pair kernel.
+static int gemm_kernel_choice() {
+  static const int v = [] {
+    const char* e = std::getenv("MOE_B200_GEMM_KERNEL");
+    return e ? std::atoi(e) : 2;
+  }();
+  return v;
+}
+
 template <bool BF16, bool B_MN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
                   cudaStream_t stream) {
@@ -465,6 +395,11 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
   if (int rc = current_device_info(&dev, &info); rc != MOE_OK) return rc;
   if (info.major != 10) return MOE_ERR_UNSUPPORTED;
 
+  // Grids of two or more SMs run the CTA-pair kernel (256x256 tiles, grid
+  // rounded down to even); a single SM runs the 1-SM kernel (128x256 tiles).
+  int grid = std::max(1, std::min<int>(num_sms > 0 ? num_sms : info.sm_count, info.sm_count));
+  const bool use_pair = grid >= 2 && gemm_kernel_choice() != 1;
+  if (use_pair) grid &= ~1;
   const CUtensorMapDataType dt =
       dtype == MOE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
@@ -484,7 +419,7 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
     } else {
       const uint64_t dims[3] = {uint64_t(k), uint64_t(n), uint64_t(num_experts)};
       const uint64_t strides[2] = {uint64_t(b_stride_n) * 2, uint64_t(se) * 2};
-      const uint32_t box[3] = {BK, BN, 1};
+      const uint32_t box[3] = {BK, use_pair ? uint32_t(BN / 2) : uint32_t(BN), 1};
       if (int rc = encode_tiled(&tb, dt, 3, b, dims, strides, box); rc != MOE_OK) return rc;
     }
   }
@@ -507,8 +442,8 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
   if (p.use_atomic &&
       cudaMemsetAsync(work_counter, 0, sizeof(int32_t), stream) != cudaSuccess)
     return MOE_ERR_CUDA;
-  const int grid = std::max(1, std::min<int>(num_sms > 0 ? num_sms : info.sm_count, info.sm_count));
   const bool bf16 = dtype == MOE_DTYPE_BF16;
+  if (use_pair) return launch_pair_kernel(bf16, b_mn, ta, tb, p, grid, stream);
   if (bf16 && b_mn) return launch<true, true>(ta, tb, p, grid, stream);
   if (bf16 && !b_mn) return launch<true, false>(ta, tb, p, grid, stream);
   if (!bf16 && b_mn) return launch<false, true>(ta, tb, p, grid, stream);

@@ -1,0 +1,371 @@
+// Grouped GEMM on CTA pairs (tcgen05 cta_group::2): 256x256 output tiles.
+//
+// Same contract as the 1-SM kernel in grouped_gemm.cu (C[off[e]:off[e+1]] =
+// act(A[off[e]:off[e+1]] @ B[e]), fp32 accumulation), for grids of two or more
+// SMs.  A (2,1,1) cluster is one CTA pair; the even CTA ("leader") owns the
+// schedule and issues tcgen05.mma.cta_group::2 with M=256, N=256.  Each CTA
+// TMA-loads its own 128 rows of A and its own 128 columns of B per k-block
+// (32 KB per SM instead of the 48 KB a 1-SM 128x256 tile needs for the same
+// tensor work), so six stages fit in shared memory, and each CTA receives its
+// 128 rows of the accumulator in its own TMEM.
+//
+// Roles per CTA (192 threads):
+//   warp 0   producer.  Leader: takes the next tile (striped over the pairs, or
+//            from the global atomic counter), posts it to both CTAs' tile rings,
+//            loads its halves.  Follower: reads the posted tile, loads its halves.
+//            Both CTAs' loads complete on the leader's stage barrier.
+//   warp 1   TMEM (both CTAs allocate the pair's 512 columns); in the leader it
+//            also issues the MMAs and commits stage/accumulator completion to the
+//            barriers of both CTAs.
+//   warps 2-5 epilogue of this CTA's 128 rows (see store_accumulator).
+// No load uses cluster multicast; the pair exchanges only barrier arrivals and
+// the tile ring entries through shared::cluster addresses.
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
+#include "gemm_common.cuh"
+#include "host_common.h"
+#include "sched.cuh"
+
+namespace moe {
+namespace gg {
+namespace pair {
+
+constexpr int BM = 256;      // rows per pair tile
+constexpr int BM_CTA = 128;  // rows per CTA
+constexpr int BN = 256;
+constexpr int BN_CTA = 128;  // B columns held by each CTA
+constexpr int BK = 64;
+constexpr int UMMA_K = 16;
+constexpr int STAGES = 6;
+constexpr int QDEPTH = 8;
+constexpr int NUM_THREADS = 192;
+constexpr int NUM_EPI_WARPS = 4;
+constexpr int A_STAGE_BYTES = BM_CTA * BK * 2;  // 16 KiB
+constexpr int B_STAGE_BYTES = BK * BN_CTA * 2;  // 16 KiB
+constexpr int B_SLAB_BYTES = BK * 64 * 2;       // one 64-column slab of an N-major B stage
+constexpr uint32_t PAIR_TX_BYTES = 2 * (A_STAGE_BYTES + B_STAGE_BYTES);
+constexpr uint32_t TMEM_COLS = 2 * BN;
+
+struct Ctrl {
+  uint64_t full[STAGES];   // leader: both CTAs' loads of a stage landed
+  uint64_t empty[STAGES];  // each CTA: its stage buffers are free again
+  uint64_t tfull[2];       // each CTA: accumulator ready
+  uint64_t tempty[2];      // leader: both CTAs' epilogues drained the accumulator
+  uint64_t qfull[QDEPTH];  // each CTA: tile ring entry posted
+  uint64_t qempty[QDEPTH]; // leader: entry read by every consumer of both CTAs
+  uint64_t drain;
+  int4 slot[QDEPTH];       // {row0, rows (1..256), n0 (-1 = end), expert}
+  uint32_t tmem_base;
+  int abort;
+};
+
+__host__ __device__ constexpr size_t smem_bytes(int num_experts) {
+  return 1024 + size_t(STAGES) * (A_STAGE_BYTES + B_STAGE_BYTES) + ((sizeof(Ctrl) + 15) / 16) * 16 +
+         size_t(3) * 4 * (num_experts + 1);
+}
+
+template <bool BF16, bool B_MN_MAJOR>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                             const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  Ctrl* ctrl = reinterpret_cast<Ctrl*>(sB + STAGES * B_STAGE_BYTES);
+  int* tile_prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ctrl) +
+                                            ((sizeof(Ctrl) + 15) / 16) * 16);
+  int* seg_start = tile_prefix + (p.num_experts + 1);
+  int* seg_rows = seg_start + (p.num_experts + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = lane_id();
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int tiles_n = (p.n + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&ctrl->full[s]), 1);
+      mbar_init(smem_u32(&ctrl->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&ctrl->tfull[a]), 1);
+      mbar_init(smem_u32(&ctrl->tempty[a]), 2 * NUM_EPI_WARPS);
+    }
+    for (int q = 0; q < QDEPTH; ++q) {
+      mbar_init(smem_u32(&ctrl->qfull[q]), 1);
+      // leader MMA + follower producer + the epilogue warps of both CTAs
+      mbar_init(smem_u32(&ctrl->qempty[q]), 2 + 2 * NUM_EPI_WARPS);
+    }
+    mbar_init(smem_u32(&ctrl->drain), 1);
+    ctrl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+    }
+    build_tile_prefix(p.offsets, p.offsets_int64, p.num_experts, p.m_total, BM, tiles_n,
+                      tile_prefix, seg_start, seg_rows, leader ? p.status : nullptr);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc_pair(smem_u32(&ctrl->tmem_base), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits of both CTAs visible before any remote arrive
+  tc_fence_after();
+
+  const uint32_t tmem_base = ctrl->tmem_base;
+  const int total_tiles = tile_prefix[p.num_experts];
+  const int num_kb = (p.k + BK - 1) / BK;
+  volatile int* abort_flag = &ctrl->abort;
+
+  if (total_tiles == 0) {
+    zero_output<BF16>(p, NUM_THREADS);
+  } else if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int q = 0;
+      uint32_t qphase = 0;
+      bool failed = false;
+      const int pair_id = static_cast<int>(cluster_id_x());
+      const int npairs = static_cast<int>(nclusters_x());
+      for (int iter = 0;; ++iter) {
+        int4 s;
+        if (leader) {
+          const int t = p.use_atomic ? atomicAdd(p.work_counter, 1) : pair_id + iter * npairs;
+          if (!mbar_wait_cluster(smem_u32(&ctrl->qempty[q]), qphase ^ 1, abort_flag)) {
+            failed = true;
+            break;
+          }
+          if (t >= total_tiles || t < 0) {
+            s = make_int4(0, 0, -1, 0);
+          } else {
+            const TileCoord tc = decode_tile(t, p.num_experts, tile_prefix, seg_start, seg_rows,
+                                             BM, tiles_n, p.tile_order);
+            s = make_int4(tc.row0, tc.rows, tc.tile_n * BN, tc.expert);
+          }
+          ctrl->slot[q] = s;
+          st_shared_cluster_v4(mapa_shared(smem_u32(&ctrl->slot[q]), 1), s);
+          mbar_arrive(smem_u32(&ctrl->qfull[q]));
+          mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->qfull[q]), 1));
+        } else {
+          if (!mbar_wait_cluster(smem_u32(&ctrl->qfull[q]), qphase, abort_flag)) {
+            failed = true;
+            break;
+          }
+          s = ctrl->slot[q];
+          mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->qempty[q]), 0));
+        }
+        if (++q == QDEPTH) {
+          q = 0;
+          qphase ^= 1;
+        }
+        if (s.z < 0) break;
+        const int row_a = s.x + static_cast<int>(crank) * BM_CTA;
+        const int n_b = s.z + static_cast<int>(crank) * BN_CTA;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(smem_u32(&ctrl->empty[stage]), phase ^ 1, abort_flag)) {
+            failed = true;
+            break;
+          }
+          const uint32_t full_local = smem_u32(&ctrl->full[stage]);
+          if (leader) mbar_arrive_expect_tx(full_local, PAIR_TX_BYTES);
+          const uint32_t full_leader = mapa_shared(full_local, 0);
+          tma_load_2d_pair(smem_u32(sA + stage * A_STAGE_BYTES), &tmap_a, full_leader, kb * BK, row_a);
+          const uint32_t b_dst = smem_u32(sB + stage * B_STAGE_BYTES);
+          if constexpr (B_MN_MAJOR) {
+#pragma unroll
+            for (int j = 0; j < BN_CTA / 64; ++j)
+              tma_load_3d_pair(b_dst + j * B_SLAB_BYTES, &tmap_b, full_leader, n_b + 64 * j, kb * BK,
+                               s.w);
+          } else {
+            tma_load_3d_pair(b_dst, &tmap_b, full_leader, kb * BK, n_b, s.w);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (failed) break;
+      }
+      if (failed) {
+        record_status(p.status, MOE_ERR_TIMEOUT);
+        *abort_flag = 1;
+        // Give loads already issued time to land before this CTA can leave.
+        const long long t0 = clock64();
+        while (clock64() - t0 < (1ll << 22)) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA (leader only) --
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
+      int stage = 0;
+      uint32_t phase = 0;
+      int q = 0;
+      uint32_t qphase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      bool failed = false;
+      bool issued_any = false;
+      while (true) {
+        if (!mbar_wait_cluster(smem_u32(&ctrl->qfull[q]), qphase, abort_flag)) {
+          failed = true;
+          break;
+        }
+        const int4 s = ctrl->slot[q];
+        mbar_arrive(smem_u32(&ctrl->qempty[q]));
+        if (++q == QDEPTH) {
+          q = 0;
+          qphase ^= 1;
+        }
+        if (s.z < 0) break;
+        if (!mbar_wait_cluster(smem_u32(&ctrl->tempty[acc]), aphase ^ 1, abort_flag)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(smem_u32(&ctrl->full[stage]), phase, abort_flag)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t adesc = smem_desc_sw128(a_base + kk * UMMA_K * 2, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (B_MN_MAJOR) {
+              bdesc = smem_desc_sw128(b_base + kk * UMMA_K * 128, B_SLAB_BYTES, 1024);
+            } else {
+              bdesc = smem_desc_sw128(b_base + kk * UMMA_K * 2, 16, 1024);
+            }
+            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          const uint32_t e_local = smem_u32(&ctrl->empty[stage]);
+          umma_commit_pair(e_local);
+          umma_commit_pair(mapa_shared(e_local, 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (failed) break;
+        const uint32_t tf_local = smem_u32(&ctrl->tfull[acc]);
+        umma_commit_pair(tf_local);
+        umma_commit_pair(mapa_shared(tf_local, 1));
+        if (++acc == 2) {
+          acc = 0;
+          aphase ^= 1;
+        }
+      }
+      if (failed) {
+        record_status(p.status, MOE_ERR_TIMEOUT);
+        *abort_flag = 1;
+        if (issued_any) {
+          umma_commit_pair(smem_u32(&ctrl->drain));
+          mbar_wait(smem_u32(&ctrl->drain), 0, nullptr);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue --
+    const int quad = warp & 3;
+    int q = 0;
+    uint32_t qphase = 0;
+    int acc = 0;
+    uint32_t aphase = 0;
+    bool failed = false;
+    while (true) {
+      const bool ok = mbar_wait_cluster(smem_u32(&ctrl->qfull[q]), qphase, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        failed = true;
+        break;
+      }
+      const int4 s = ctrl->slot[q];
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->qempty[q]), 0));
+      if (++q == QDEPTH) {
+        q = 0;
+        qphase ^= 1;
+      }
+      if (s.z < 0) break;
+      const bool ok2 = mbar_wait_cluster(smem_u32(&ctrl->tfull[acc]), aphase, abort_flag);
+      if (!__all_sync(0xffffffffu, ok2)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const int rows_here = min(int(BM_CTA), max(0, s.y - static_cast<int>(crank) * int(BM_CTA)));
+      store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
+                              lane, s.x + static_cast<int>(crank) * BM_CTA, rows_here, s.z, p);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->tempty[acc]), 0));
+      if (++acc == 2) {
+        acc = 0;
+        aphase ^= 1;
+      }
+    }
+    if (failed && lane == 0) {
+      record_status(p.status, MOE_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the pair still uses its memory
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+template <bool BF16, bool B_MN>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
+           cudaStream_t stream) {
+  auto kern = grouped_gemm_pair_kernel<BF16, B_MN>;
+  static std::once_flag once[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MOE_ERR_CUDA;
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev], [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem_bytes(kMaxExperts)));
+  });
+  if (attr_err != cudaSuccess) return MOE_ERR_CUDA;
+  kern<<<grid, NUM_THREADS, smem_bytes(p.num_experts), stream>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+}  // namespace pair
+
+int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const Params& p, int grid, cudaStream_t stream) {
+  if (grid < 2 || grid % 2 != 0) return MOE_ERR_INVALID_ARG;
+  if (bf16 && b_mn) return pair::launch<true, true>(ta, tb, p, grid, stream);
+  if (bf16 && !b_mn) return pair::launch<true, false>(ta, tb, p, grid, stream);
+  if (!bf16 && b_mn) return pair::launch<false, true>(ta, tb, p, grid, stream);
+  return pair::launch<false, false>(ta, tb, p, grid, stream);
+}
+
+}  // namespace gg
+}  // namespace moe
