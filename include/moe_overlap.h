@@ -133,9 +133,9 @@ MOE_API int32_t moe_grouped_gemm_noalloc(const void* a, int64_t lda, const void*
  *
  * Replaces _build_work_queue (src/triton_grouped_gemm.py:240-297).  With
  * order == 0 the list is expert-major, then tile_m, then tile_n (the
- * reference's order, :277-286); order == 1 is the GEMM kernel's own order
- * (expert-major, then tile_n, then tile_m) that keeps CTAs sharing a weight
- * column block adjacent.  Writes up to max_items entries to out_expert /
+ * reference's order, :277-286), the order the GEMM kernel walks by default;
+ * order == 1 is expert-major, then tile_n, then tile_m (CTAs sharing a weight
+ * column block adjacent).  Writes up to max_items entries to out_expert /
  * out_tile_m / out_tile_n (int32 device arrays) and the total count to
  * *out_count (int32 device word).
  */

@@ -331,6 +331,17 @@ static int gemm_kernel_choice() {
   return v;
 }
 
+// Tile walk order: 0 (default) = the reference's expert, tile_m, tile_n fastest
+// (measured ~1 % faster on BASELINE configs 2/3 than 1 = expert, tile_n, tile_m
+// fastest).  MOE_B200_GEMM_ORDER overrides.
+static int gemm_tile_order() {
+  static const int v = [] {
+    const char* e = std::getenv("MOE_B200_GEMM_ORDER");
+    return (e && std::atoi(e) == 1) ? 1 : 0;
+  }();
+  return v;
+}
+
 template <bool BF16, bool B_MN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
                   cudaStream_t stream) {
@@ -435,7 +446,7 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
   p.num_experts = num_experts;
   p.activation = activation;
   p.use_atomic = use_atomic_queue ? 1 : 0;
-  p.tile_order = 1;
+  p.tile_order = gemm_tile_order();
   p.work_counter = work_counter;
   p.status = status;
 
