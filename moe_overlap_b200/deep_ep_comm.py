@@ -228,7 +228,8 @@ class DeepEPDispatcher:
 
     def combine(self, expert_out: torch.Tensor, handle: DispatchHandle,
                 previous_event: Optional[object] = None, *,
-                weighted: bool = False) -> Tuple[torch.Tensor, object]:
+                weighted: bool = False,
+                out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, object]:
         if not isinstance(handle, DispatchHandle) or handle.combined:
             raise RuntimeError("combine needs the handle of an outstanding dispatch")
         if expert_out.dtype != torch.bfloat16 or expert_out.dim() != 2 or \
@@ -239,8 +240,12 @@ class DeepEPDispatcher:
         _lib.check_status(self.device)
         views = self._ep.slots[handle.slot]
         self._enter_comm(previous_event)
-        out = torch.empty((handle.num_tokens, self.hidden_size), dtype=torch.bfloat16,
-                          device=self.device)
+        if out is None:
+            out = torch.empty((handle.num_tokens, self.hidden_size), dtype=torch.bfloat16,
+                              device=self.device)
+        elif (out.shape != (handle.num_tokens, self.hidden_size) or out.dtype != torch.bfloat16
+              or not out.is_contiguous() or out.data_ptr() % 16 != 0):
+            raise ValueError("out must be a contiguous, 16-byte aligned bf16 [num_tokens, hidden]")
         with torch.cuda.stream(self.comm_stream):
             if expert_out.data_ptr() != views.expert_out.data_ptr():
                 rows = expert_out.shape[0]

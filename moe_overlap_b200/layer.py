@@ -1,0 +1,158 @@
+"""Routed MoE layer on B200: router -> dispatch -> grouped GEMMs -> weighted combine.
+
+The forward of SimpleMoE's routed path (src/train_moe_baseline.py:315-441)
+built from this package's kernels, with none of the reference's per-call host
+work:
+  * expert weights stay in nn.Linear layout ([E_local, F, H] and [E_local, H, F])
+    and are fed to the grouped GEMM as K-major views (the reference re-stacks and
+    transposes them on every call, :187-191);
+  * dispatch writes rows straight into each owner's expert-ordered receive slot
+    and produces expert_offsets on the device, so there is no sort, bincount or
+    .item() (:219-234);
+  * GELU is fused into the up-projection's epilogue (:243), the down-projection
+    writes into the exchange buffer, and the combine applies the top-k weights
+    while it reduces (:394-399 + deep_ep_comm.combine);
+  * chunks of ``micro_batch_size`` tokens pipeline like the reference's loop
+    (:349-441): the next chunk's dispatch runs on the exchange stream while the
+    current chunk's GEMMs run on the compute stream.
+World size 1 (no process group) runs the same kernels with a local exchange.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .deep_ep_comm import DeepEPDispatcher
+from .gemm import grouped_gemm
+
+
+@dataclass
+class RouterStats:
+    entropy: float
+    load_std: float
+    load_cv: float
+
+
+def random_weights(num_experts: int, hidden: int, ffn: int, std: float = 0.02, seed: int = 0):
+    """(router [E, H], w1 [E, F, H], w2 [E, H, F]) fp32 CPU tensors, N(0, std), seeded."""
+    g = torch.Generator().manual_seed(seed)
+    rw = torch.randn(num_experts, hidden, generator=g) * std
+    w1 = torch.randn(num_experts, ffn, hidden, generator=g) * std
+    w2 = torch.randn(num_experts, hidden, ffn, generator=g) * std
+    return rw, w1, w2
+
+
+class MoELayer:
+    def __init__(self, hidden_size: int, ffn_size: int, num_experts: int, top_k: int, *,
+                 group: Optional[dist.ProcessGroup] = None, renormalize: bool = False,
+                 router_bias: bool = False, num_comm_sms: int = 24,
+                 micro_batch_size: int = 4096, use_atomic_queue: bool = False,
+                 max_recv_rows: Optional[int] = None):
+        self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
+        self.group = group
+        self.world = group.size() if group is not None else 1
+        self.rank = group.rank() if group is not None else 0
+        if num_experts % self.world != 0:
+            raise ValueError(f"num_routed_experts ({num_experts}) must be divisible by world_size ({self.world})")
+        self.experts_per_rank = num_experts // self.world
+        self.expert_offset = self.rank * self.experts_per_rank
+        self.renormalize = renormalize
+        self.micro = max(1, int(micro_batch_size))
+        self.use_atomic = use_atomic_queue
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        dev, bf16 = self.device, torch.bfloat16
+        self.router_w = torch.zeros(num_experts, hidden_size, dtype=bf16, device=dev)
+        self.router_b = torch.zeros(num_experts, dtype=torch.float32, device=dev) if router_bias else None
+        self.w1 = torch.zeros(self.experts_per_rank, ffn_size, hidden_size, dtype=bf16, device=dev)
+        self.w2 = torch.zeros(self.experts_per_rank, hidden_size, ffn_size, dtype=bf16, device=dev)
+        self.dispatcher = DeepEPDispatcher(group, hidden_size, num_experts, num_sms=num_comm_sms,
+                                           max_tokens_per_rank=self.micro, max_top_k=top_k,
+                                           max_recv_rows=max_recv_rows, exact_size=False)
+        self.compute_stream = torch.cuda.Stream(dev)
+        self.gemm_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.h = torch.empty(self.dispatcher.max_recv_rows, ffn_size, dtype=bf16, device=dev)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    # ----------------------------------------------------------------- weights --
+    def init_random(self, std: float = 0.02, seed: int = 0) -> "MoELayer":
+        """N(0, std) weights drawn on the CPU: every rank draws all experts and keeps its own."""
+        rw, w1, w2 = random_weights(self.num_experts, self.hidden, self.ffn, std, seed)
+        lo, hi = self.expert_offset, self.expert_offset + self.experts_per_rank
+        self.router_w.copy_(rw.to(torch.bfloat16))
+        self.w1.copy_(w1[lo:hi].to(torch.bfloat16))
+        self.w2.copy_(w2[lo:hi].to(torch.bfloat16))
+        return self
+
+    def load_reference_state_dict(self, sd: dict) -> "MoELayer":
+        """Weights from a single-process SimpleMoE state_dict (global expert ids)."""
+        self.router_w.copy_(sd["router.weight"].to(torch.bfloat16))
+        for le in range(self.experts_per_rank):
+            e = self.expert_offset + le
+            self.w1[le].copy_(sd[f"routed_experts.{e}.w1.weight"].to(torch.bfloat16))
+            self.w2[le].copy_(sd[f"routed_experts.{e}.w2.weight"].to(torch.bfloat16))
+        return self
+
+    # ----------------------------------------------------------------- forward --
+    def route(self, x: torch.Tensor):
+        """softmax router and top-k (src/train_moe_baseline.py:316-318); float32 weights."""
+        logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t()).float()
+        if self.router_b is not None:
+            logits = logits + self.router_b
+        probs = F.softmax(logits, dim=-1)
+        w, idx = torch.topk(probs, k=self.top_k, dim=-1)
+        if self.renormalize:
+            w = w / w.sum(dim=-1, keepdim=True)
+        return probs, idx.to(torch.int64), w.contiguous()
+
+    def _experts(self, res) -> torch.Tensor:
+        """GEMM1 (+GELU) and GEMM2 on the current stream; returns the expert-output rows."""
+        y = self.dispatcher.expert_out_buffer(res.handle)
+        kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
+        grouped_gemm(res.recv_x, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
+                     activation="gelu", **kw)
+        grouped_gemm(self.h, self.w2.transpose(1, 2), res.expert_offsets, out=y, **kw)
+        return y
+
+    def forward(self, x: torch.Tensor, return_stats: bool = False, routing=None):
+        """Returns (out [T, H] bf16, RouterStats or None).  ``routing`` = (probs, idx, w) to reuse."""
+        x = x.to(torch.bfloat16).contiguous()
+        probs, idx, w = routing if routing is not None else self.route(x)
+        t_total = x.shape[0]
+        out = torch.empty_like(x)
+        chunks = [(s, min(s + self.micro, t_total)) for s in range(0, t_total, self.micro)] or [(0, 0)]
+        disp = self.dispatcher
+        cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
+                            w[chunks[0][0]:chunks[0][1]])
+        for i, (s, e) in enumerate(chunks):
+            nxt = None
+            if i + 1 < len(chunks):
+                ns, ne = chunks[i + 1]
+                nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne])
+            with torch.cuda.stream(self.compute_stream):
+                cur.event.current_stream_wait()
+                y = self._experts(cur)
+                done = torch.cuda.Event()
+                done.record(self.compute_stream)
+            disp.combine(y, cur.handle, previous_event=done, weighted=True, out=out[s:e])
+            cur = nxt
+        torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
+        stats = self.stats(probs, idx) if return_stats else None
+        return out, stats
+
+    __call__ = forward
+
+    def stats(self, probs: torch.Tensor, idx: torch.Tensor) -> RouterStats:
+        """Router entropy and expert-load spread (src/train_moe_baseline.py:450-461)."""
+        counts = torch.bincount(idx.reshape(-1), minlength=self.num_experts).float()
+        if self.world > 1:
+            dist.all_reduce(counts, group=self.group)
+        mean = counts.mean().clamp_min(1e-6)
+        entropy = (-probs * probs.clamp_min(1e-9).log()).sum(dim=-1).mean()
+        return RouterStats(float(entropy), float(counts.std()), float(counts.std() / mean))
+
+    def close(self) -> None:
+        self.dispatcher.close()

@@ -30,15 +30,24 @@ def _worlds() -> list[int]:
     return sorted({2, min(n, 8)}) if n >= 2 else []
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_dispatcher_across_processes(world):
+def _run(world: int, worker: str, marker: str) -> None:
     if world not in _worlds():
         pytest.skip(f"needs {world} GPUs (have {torch.cuda.device_count()})")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MOE_B200_EP_TIMEOUT_S="20",
                PYTHONDONTWRITEBYTECODE="1")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
-           "--master-port", str(_free_port()), str(REPO / "tests" / "_ep_worker.py")]
+           "--master-port", str(_free_port()), str(REPO / "tests" / worker)]
     proc = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
     assert proc.returncode == 0, proc.stdout[-4000:] + proc.stderr[-4000:]
-    assert proc.stdout.count("exchange matches the oracle") == world
+    assert proc.stdout.count(marker) == world
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_dispatcher_across_processes(world):
+    _run(world, "_ep_worker.py", "exchange matches the oracle")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_moe_layer_across_processes(world):
+    _run(world, "_layer_worker.py", "moe layer matches the oracle")

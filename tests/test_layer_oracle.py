@@ -1,0 +1,33 @@
+"""Pins the MoE-layer oracle to SimpleMoE outputs made by the reference itself.
+
+tests/golden/moe_layer_golden.npz comes from tests/golden/make_golden_layer.py,
+which runs src/train_moe_baseline.py's SimpleMoE on the CPU in fp32: the
+single-process routed path and the torch_a2a expert-parallel path on 2 gloo
+ranks.  The oracle's fp32 forward must agree to fp32 rounding, and its router
+statistics to 1e-5.
+"""
+from pathlib import Path
+
+import numpy as np
+
+from oracle import moe_layer as ol
+
+G = np.load(Path(__file__).parent / "golden" / "moe_layer_golden.npz")
+
+
+def test_oracle_layer_matches_reference_local_path():
+    out = ol.layer_forward_f32(G["x"], G["router_w"], G["w1"], G["w2"], int(G["top_k"]))
+    np.testing.assert_allclose(out, G["out_local"], rtol=1e-4, atol=1e-5)
+
+
+def test_oracle_layer_matches_reference_expert_parallel_path():
+    out = ol.layer_forward_f32(G["x"], G["router_w"], G["w1"], G["w2"], int(G["top_k"]))
+    half = out.shape[0] // 2
+    np.testing.assert_allclose(out[:half], G["out_a2a_rank0"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(out[half:], G["out_a2a_rank1"], rtol=1e-4, atol=1e-5)
+
+
+def test_oracle_router_stats_match_reference():
+    probs, idx, _ = ol.route(G["x"], G["router_w"], int(G["top_k"]))
+    ent, std, cv = ol.router_stats(probs, idx, G["router_w"].shape[0])
+    np.testing.assert_allclose([ent, std, cv], G["stats"], rtol=1e-5, atol=1e-6)
