@@ -53,6 +53,19 @@ WORKLOADS = {
 }
 
 
+LAYER_WORKLOADS = {
+    "ep_layer": dict(tokens=8 * 1024, hidden=2048, ffn=8192, experts=16, top_k=2, renorm=False,
+                     zipf_bias=True,
+                     desc="BASELINE config 5: expert-parallel MoE layer forward, per rank 8x1024 "
+                          "tokens, H=2048, F=8192, 16 experts sharded over the ranks, top-2 "
+                          "softmax, Zipf(1.0) gate bias"),
+    "layer_fwd": dict(tokens=8 * 2048, hidden=2048, ffn=8192, experts=16, top_k=2, renorm=True,
+                      zipf_bias=False,
+                      desc="BASELINE config 4 forward: MoE layer on one GPU, batch 8 x seq 2048, "
+                           "H=2048, FFN 4H, 16 experts, renormalised top-2"),
+}
+
+
 def workload_counts(name: str) -> list[int]:
     from tests._inputs import zipf_counts
 
@@ -71,7 +84,12 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm_cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(LAYER_WORKLOADS),
+                    default="gemm_cfg2")
+    ap.add_argument("--comm-sms", type=int, default=24,
+                    help="layer workloads: SM budget (grid) of the dispatch/combine kernels")
+    ap.add_argument("--micro-batch", type=int, default=4096,
+                    help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     return ap.parse_args()
@@ -298,6 +316,160 @@ class ClockSampler(threading.Thread):
 
 
 # ---------------------------------------------------------------- GPU side --
+def zipf_gate_bias(router_w, num_experts: int, top_k: int, seed: int = 12345):
+    """Per-expert gate bias whose top-k routing follows Zipf(1.0) over expert ids.
+
+    Target shares p_e ~ 1/(e+1) (expert 0 hottest).  Starting from log p, the
+    bias is refined on a 32768-token N(0,1) sample through this router by
+    b_e += 0.5 * log(p_e / share_e) until the realised top-k assignment shares
+    match; returns (bias, iterations, max relative share error).
+    """
+    import numpy as np
+
+    p = 1.0 / np.arange(1, num_experts + 1, dtype=np.float64)
+    p /= p.sum()
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((32768, router_w.shape[1])).astype(np.float32)
+    logits = (x @ router_w.astype(np.float32).T).astype(np.float64)
+    bias = np.log(p)
+    err, it = 1e9, 0
+    for it in range(1, 301):
+        z = logits + bias
+        top = np.argpartition(-z, top_k - 1, axis=-1)[:, :top_k]
+        share = np.bincount(top.reshape(-1), minlength=num_experts) / top.size
+        err = float(np.max(np.abs(share - p) / p))
+        if err < 0.02:
+            break
+        bias += 0.5 * np.log(p / np.maximum(share, 1e-6))
+    return bias.astype(np.float32), it, err
+
+
+def run_layer(args, rank: int, world: int, local_rank: int) -> None:
+    """MoE-layer workloads: tokens/s of the forward, overlap accounting, NVLink GB/s."""
+    import torch
+    import torch.distributed as dist
+
+    import moe_overlap_b200 as mo
+    from moe_overlap_b200.layer import MoELayer, random_weights
+
+    cfg = LAYER_WORKLOADS[args.workload]
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
+        group = dist.group.WORLD
+    T, H, Fd, E, K = cfg["tokens"], cfg["hidden"], cfg["ffn"], cfg["experts"], cfg["top_k"]
+    layer = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
+                     router_bias=cfg["zipf_bias"], num_comm_sms=args.comm_sms,
+                     micro_batch_size=args.micro_batch).init_random(std=0.02, seed=0)
+    bias_info = None
+    if cfg["zipf_bias"]:
+        rw, _, _ = random_weights(E, H, Fd, 0.02, 0)
+        bias, iters, err = zipf_gate_bias(rw.to(torch.bfloat16).float().numpy(), E, K)
+        layer.router_b.copy_(torch.from_numpy(bias))
+        bias_info = {"fit": "per-expert, Zipf(1.0) target shares", "iterations": iters,
+                     "max_rel_share_error_on_sample": round(err, 3)}
+    g = torch.Generator().manual_seed(1000 + rank)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(device)
+    routing = layer.route(x)
+    idx = routing[1]
+    flops_local = torch.zeros(1, dtype=torch.float64, device=device)
+    owner = idx // layer.experts_per_rank
+    rows_to = torch.bincount(owner[idx >= 0].reshape(-1), minlength=world).double()
+    if world > 1:
+        recv_rows = rows_to.clone()
+        dist.all_reduce(recv_rows, group=group)  # rows each rank receives, summed over senders
+    else:
+        recv_rows = rows_to
+    remote_rows = float(rows_to.sum() - rows_to[rank])
+    expert_counts = torch.bincount(idx[idx >= 0].reshape(-1), minlength=E).double()
+    if world > 1:
+        dist.all_reduce(expert_counts, group=group)
+    realised_share = (expert_counts / expert_counts.sum()).tolist()
+    flops_local[0] = 4.0 * float(recv_rows[rank]) * H * Fd  # two GEMMs on this rank's rows
+    for _ in range(max(3, args.warmup)):
+        layer(x, routing=routing)
+    torch.cuda.synchronize(device)
+    mo.check_status(device, sync=True)
+
+    sampler = ClockSampler(device)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        layer(x, routing=routing)
+    end.record()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    mo.check_status(device, sync=True)
+    step_ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([step_ms], dtype=torch.float64, device=device)
+    total_flops = flops_local.clone()
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(total_flops)
+    step_ms = float(t.item())
+
+    _, phases = layer.forward_serialized(x, routing)
+    comm_ms = phases["dispatch_ms"] + phases["combine_ms"]
+    comp_ms = phases["experts_ms"]
+    hidden = max(0.0, min(1.0, (comm_ms + comp_ms - step_ms) / comm_ms)) if comm_ms > 0 else None
+    row_bytes = H * 2
+    dispatch_bytes = remote_rows * (row_bytes + K * 12 + 8)
+    combine_bytes = remote_rows * row_bytes
+    peak, peak_src = load_peaks()
+    if rank == 0:
+        tokens_per_s = world * T / (step_ms / 1e3)
+        tflops = float(total_flops.item()) / (step_ms / 1e3) / 1e12
+        line = {
+            "metric": "MoE-layer tokens/s",
+            "value": round(tokens_per_s, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
+            "config": {"workload": args.workload, "description": cfg["desc"],
+                       "tokens_per_rank": T, "micro_batch": args.micro_batch,
+                       "comm_sms": args.comm_sms, "gate_bias": bias_info,
+                       "realised_expert_share": [round(v, 4) for v in realised_share],
+                       "rows_received_per_rank": [int(v) for v in recv_rows.tolist()],
+                       "parallelism": f"ep{world}"},
+            "expert_gemm_tflops": round(tflops, 2),
+            "expert_gemm_frac_of_peak": round(tflops / (world * peak), 4),
+            "communication_hidden_ratio": None if hidden is None else round(hidden, 4),
+            "serial_phase_ms": {k: round(v, 4) for k, v in phases.items()},
+            "nvlink": {
+                "dispatch_GBps_per_rank": round(dispatch_bytes / (phases["dispatch_ms"] / 1e3) / 1e9, 1)
+                if world > 1 and phases["dispatch_ms"] > 0 else None,
+                "combine_GBps_per_rank": round(combine_bytes / (phases["combine_ms"] / 1e3) / 1e9, 1)
+                if world > 1 and phases["combine_ms"] > 0 else None,
+                "rank0_remote_rows": int(remote_rows),
+                "peer_copy_reference_GBps": 770,
+            },
+            "clocks": clocks,
+            "gpu_launches_per_step": None,
+        }
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -305,6 +477,9 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload in LAYER_WORKLOADS:
+        run_layer(args, rank, world, local_rank)
         return
 
     import torch

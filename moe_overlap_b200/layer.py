@@ -145,6 +145,50 @@ class MoELayer:
 
     __call__ = forward
 
+    def forward_serialized(self, x: torch.Tensor, routing) -> tuple[torch.Tensor, dict]:
+        """The same forward with every phase run alone, for overlap accounting.
+
+        Each chunk's dispatch, expert GEMMs and combine run one after another
+        with a device synchronisation (and, across ranks, a barrier) between
+        phases; returns the output and the summed device time of each phase in
+        ms (max over ranks), i.e. the serial times that the overlapped forward
+        hides behind each other.
+        """
+        x = x.to(torch.bfloat16).contiguous()
+        _, idx, w = routing
+        out = torch.empty_like(x)
+        t_total = x.shape[0]
+        chunks = [(s, min(s + self.micro, t_total)) for s in range(0, t_total, self.micro)]
+        times = {"dispatch_ms": 0.0, "experts_ms": 0.0, "combine_ms": 0.0}
+        disp = self.dispatcher
+
+        def timed(key, fn):
+            self._sync_all()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            r = fn()
+            torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
+            end.record()
+            self._sync_all()
+            times[key] += start.elapsed_time(end)
+            return r
+
+        for s, e in chunks:
+            res = timed("dispatch_ms", lambda: disp.dispatch(x[s:e], idx[s:e], w[s:e]))
+            res.event.current_stream_wait()
+            y = timed("experts_ms", lambda: self._experts(res))
+            timed("combine_ms", lambda: disp.combine(y, res.handle, weighted=True, out=out[s:e]))
+        if self.world > 1:
+            t = torch.tensor([times[k] for k in sorted(times)], dtype=torch.float64, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            times = dict(zip(sorted(times), t.tolist()))
+        return out, times
+
+    def _sync_all(self) -> None:
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
     def stats(self, probs: torch.Tensor, idx: torch.Tensor) -> RouterStats:
         """Router entropy and expert-load spread (src/train_moe_baseline.py:450-461)."""
         counts = torch.bincount(idx.reshape(-1), minlength=self.num_experts).float()
