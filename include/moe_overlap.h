@@ -45,7 +45,8 @@ extern "C" {
 
 /* ------------------------------------------------------------ activations -- */
 #define MOE_ACT_NONE 0
-#define MOE_ACT_GELU 1 /* exact GELU, 0.5*x*(1+erf(x/sqrt(2))), on the fp32 accumulator */
+#define MOE_ACT_GELU 1  /* exact GELU, 0.5*x*(1+erf(x/sqrt(2))), on the fp32 accumulator */
+#define MOE_ACT_DGELU 2 /* acc * gelu'(aux_in): the GELU backward fused into a dgrad GEMM  */
 
 /* Human-readable text for a status code (static storage). */
 MOE_API const char* moe_status_string(int32_t code);
@@ -94,6 +95,44 @@ MOE_API int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int6
                          int64_t k, int64_t n, int32_t num_experts, int32_t dtype,
                          int32_t activation, int32_t num_sms, int32_t use_atomic_queue,
                          int32_t* work_counter, int32_t* status, void* stream);
+
+/*
+ * moe_grouped_gemm with optional epilogue operands (any may be NULL / 0):
+ *   row_scale  float[m_total]: v = acc * row_scale[row]
+ *   aux_out    m_total x n (row stride ld_aux), dtype: receives v before the
+ *              activation (the pre-activation a backward pass needs)
+ *   aux_in     m_total x n (row stride ld_aux), dtype: with activation
+ *              MOE_ACT_DGELU the result is v * gelu'(aux_in), the GELU backward
+ *              fused into a dgrad GEMM
+ * then C = act(v) as in moe_grouped_gemm.  No counterpart in the reference, which
+ * runs inference only (src/train_moe_baseline.py:524-552); these serve the
+ * forward-with-saved-activations and backward of the routed experts.
+ */
+MOE_API int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b, int64_t b_stride_e,
+                                    int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                                    const void* expert_offsets, int32_t offsets_int64,
+                                    int64_t m_total, int64_t k, int64_t n, int32_t num_experts,
+                                    int32_t dtype, int32_t activation, int32_t num_sms,
+                                    int32_t use_atomic_queue, int32_t* work_counter,
+                                    const float* row_scale, const void* aux_in, void* aux_out,
+                                    int64_t ld_aux, int32_t* status, void* stream);
+
+/*
+ * Weight-gradient grouped GEMM: for every expert e with rows r in
+ * [off[e], off[e+1]) of A (rows_total x m, row stride lda) and B (rows_total x n,
+ * row stride ldb):  C[e] (m x n, row stride ldc, expert stride c_stride_e) =
+ * sum_r A[r]^T B[r], fp32 accumulation rounded to dtype.  Every segment must
+ * start and end on a multiple of 64 rows (see expert_alignment of the exchange;
+ * otherwise MOE_ERR_OFFSETS); an expert without rows gets zeros.  With A = dY and
+ * B = H (or A = dA, B = X) of the routed experts this is dW2 (dW1) in nn.Linear
+ * layout.  No counterpart in the reference, which has no backward pass.
+ */
+MOE_API int32_t moe_grouped_gemm_wgrad(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                       void* c, int64_t ldc, int64_t c_stride_e,
+                                       const void* expert_offsets, int32_t offsets_int64,
+                                       int64_t rows_total, int64_t m, int64_t n,
+                                       int32_t num_experts, int32_t dtype, int32_t num_sms,
+                                       int32_t* status, void* stream);
 
 /*
  * Allocation-free variant of moe_grouped_gemm with the dynamic (atomic) tile
@@ -227,6 +266,9 @@ MOE_API int32_t moe_ep_views(moe_ep_t ep, int32_t slot, moe_ep_views_t* views);
  *            selected token's bf16 row and its metadata into the owner's receive
  *            slot and raises this rank's data flag everywhere; pad_rows != 0 also
  *            sets recv_topk_idx = -1 for this rank's unused receive rows;
+ *            expert_alignment (>= 1, DeepEP's argument of that name,
+ *            deep_ep/buffer.py:327) rounds every local expert's segment up to a
+ *            multiple of that many rows; the padding rows are zeroed with no slot;
  *                                                       ~ intranode.cu dispatch
  *   end      waits (bounded) until every rank's rows have landed here.
  * x: [num_tokens][hidden] bf16; topk_idx: [num_tokens][topk] int64 global expert ids
@@ -240,14 +282,16 @@ MOE_API int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64_t*
 MOE_API int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
                                         const float* topk_weights, int32_t num_tokens,
                                         int32_t topk, int32_t slot, uint64_t epoch,
-                                        int32_t num_blocks, int32_t pad_rows, uint64_t wait_ns,
+                                        int32_t num_blocks, int32_t pad_rows,
+                                        int32_t expert_alignment, uint64_t wait_ns,
                                         int32_t* status, void* stream);
 MOE_API int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch, uint64_t wait_ns,
                                     int32_t* status, void* stream);
 MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_idx,
                                 const float* topk_weights, int32_t num_tokens, int32_t topk,
                                 int32_t slot, uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
-                                uint64_t wait_ns, int32_t* status, void* stream);
+                                int32_t expert_alignment, uint64_t wait_ns, int32_t* status,
+                                void* stream);
 
 /*
  * Combine, in two phases (moe_ep_combine runs both):

@@ -34,6 +34,7 @@ MOE_DTYPE_BF16 = 0
 MOE_DTYPE_F16 = 1
 MOE_ACT_NONE = 0
 MOE_ACT_GELU = 1
+MOE_ACT_DGELU = 2
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -54,6 +55,31 @@ SIGNATURES: dict[str, tuple] = {
             _i64, _i64, _i64, _i32,  # m_total, k, n, num_experts
             _i32, _i32, _i32, _i32,  # dtype, activation, num_sms, use_atomic_queue
             _c_void_p, _c_void_p, _c_void_p,  # work_counter, status, stream
+        ],
+    ),
+    "moe_grouped_gemm_ex": (
+        _i32,
+        [
+            _c_void_p, _i64,  # a, lda
+            _c_void_p, _i64, _i64, _i64,  # b, strides e/k/n
+            _c_void_p, _i64,  # c, ldc
+            _c_void_p, _i32,  # offsets, offsets_int64
+            _i64, _i64, _i64, _i32,  # m_total, k, n, num_experts
+            _i32, _i32, _i32, _i32,  # dtype, activation, num_sms, use_atomic_queue
+            _c_void_p,  # work_counter
+            _c_void_p, _c_void_p, _c_void_p, _i64,  # row_scale, aux_in, aux_out, ld_aux
+            _c_void_p, _c_void_p,  # status, stream
+        ],
+    ),
+    "moe_grouped_gemm_wgrad": (
+        _i32,
+        [
+            _c_void_p, _i64, _c_void_p, _i64,  # a, lda, b, ldb
+            _c_void_p, _i64, _i64,  # c, ldc, c_stride_e
+            _c_void_p, _i32,  # offsets, offsets_int64
+            _i64, _i64, _i64, _i32,  # rows_total, m, n, num_experts
+            _i32, _i32,  # dtype, num_sms
+            _c_void_p, _c_void_p,  # status, stream
         ],
     ),
     "moe_grouped_gemm_noalloc": (
@@ -88,11 +114,11 @@ SIGNATURES: dict[str, tuple] = {
                _c_void_p]),
     "moe_ep_dispatch_scatter": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
-               _u64, _c_void_p, _c_void_p]),
+               _i32, _u64, _c_void_p, _c_void_p]),
     "moe_ep_dispatch_end": (_i32, [_c_void_p, _i32, _u64, _u64, _c_void_p, _c_void_p]),
     "moe_ep_dispatch": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
-               _u64, _c_void_p, _c_void_p]),
+               _i32, _u64, _c_void_p, _c_void_p]),
     "moe_ep_combine_begin": (_i32, [_c_void_p, _i32, _u64, _c_void_p]),
     "moe_ep_combine_end": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _c_void_p, _i32,

@@ -45,6 +45,7 @@ constexpr int kMaxExperts = 1024;
 constexpr int kAssignPerLayoutBlock = 2048;  // 8 warps x 8 chunks x 32 lanes
 constexpr int kLayoutThreads = 256;
 constexpr int kCommThreads = 512;
+constexpr int kPullThreads = 256;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -126,6 +127,7 @@ struct Params {
   unsigned int* done_ctr;
   int num_layout_blocks;
   int pad_rows;  // fill recv_topk_idx rows past the received count with -1
+  int align;     // receive segments of each local expert rounded up to this many rows
   int64_t* host_info;
   // combine
   __nv_bfloat16* out;
@@ -231,6 +233,7 @@ __global__ void count_kernel(Params p) {
 struct CountView {
   int exp_base[kMaxExperts];  // first row of expert e on its owner
   int my_prefix[kMaxExperts]; // rows of expert e from ranks before this one
+  int exp_count[kMaxExperts]; // rows of expert e from all ranks (before alignment)
   int recv_total;             // rows this rank receives
   int overflow;               // some owner would exceed its capacity
   int fail;
@@ -257,7 +260,8 @@ __device__ void build_count_view(const Params& p, CountView& cv) {
       const int e = d * p.per_rank + le;
       const int v = cv.exp_base[e];
       cv.exp_base[e] = run;
-      run += v;
+      cv.exp_count[e] = v;
+      run += (v + p.align - 1) / p.align * p.align;
     }
     if (run > p.cap_rows) atomicOr(&cv.overflow, 1);
     if (d == p.rank) cv.recv_total = run;
@@ -338,7 +342,9 @@ __global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
           p.send_pos[a] = row;
         }
       }
-      constexpr int U = 4;
+      // Each lane loads 8 x 16 B per pass (a 4 KB row per warp for H = 2048)
+      // before storing anything, so every load of the pass is in flight at once.
+      constexpr int U = 8;
       for (int base = 0; base < nvec; base += 32 * U) {
         uint4 v[U];
 #pragma unroll
@@ -351,6 +357,27 @@ __global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
             if (i < nvec) dst[q][i] = v[u];
+          }
+        }
+      }
+    }
+    if (p.align > 1) {
+      // Alignment padding inside this rank's expert segments: zero rows, no slot.
+      uint8_t* me = p.peers[p.rank];
+      for (int le = 0; le < p.per_rank; ++le) {
+        const int e = p.rank * p.per_rank + le;
+        const int64_t first = cv.exp_base[e] + cv.exp_count[e];
+        const int64_t npad = (cv.exp_count[e] + p.align - 1) / p.align * p.align - cv.exp_count[e];
+        for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+             i < npad * nvec; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+          const int64_t r = first + i / nvec;
+          at<uint4>(me, sl.recv_x)[r * nvec + i % nvec] = make_uint4(0, 0, 0, 0);
+          if (i % nvec == 0) {
+            for (int j = 0; j < p.max_topk; ++j) {
+              at<int64_t>(me, sl.topk_idx)[r * p.max_topk + j] = -1;
+              at<float>(me, sl.topk_w)[r * p.max_topk + j] = 0.0f;
+            }
+            at<int2>(me, sl.src)[r] = make_int2(-1, -1);
           }
         }
       }
@@ -413,7 +440,44 @@ __device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, floa
   }
 }
 
-__global__ void __launch_bounds__(kCommThreads) pull_kernel(Params p) {
+// Reduces one token: every lane first loads its U 16-byte vectors of each of
+// the token's ns source rows (up to MAXR), then sums them in fp32 in slot order.
+template <int U, int MAXR>
+__device__ __forceinline__ void pull_token(const uint4* const* srcs, const float* scale, int ns,
+                                           uint4* dst, int nvec, int lane) {
+  for (int base = 0; base < nvec; base += 32 * U) {
+    uint4 v[MAXR][U];
+#pragma unroll
+    for (int q = 0; q < MAXR; ++q) {
+      if (q < ns) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * 32 + lane;
+          if (i < nvec) v[q][u] = srcs[q][i];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * 32 + lane;
+      if (i >= nvec) continue;
+      float acc[8];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) acc[w] = 0.0f;
+#pragma unroll
+      for (int q = 0; q < MAXR; ++q)
+        if (q < ns) acc_bf16x8(acc, v[q][u], scale[q]);
+      uint4 o;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) h[w] = __floats2bfloat162_rn(acc[2 * w], acc[2 * w + 1]);
+      dst[i] = o;
+    }
+  }
+}
+
+template <int U, int MAXR>
+__global__ void __launch_bounds__(kPullThreads, 2) pull_kernel(Params p) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
   __syncthreads();
@@ -422,12 +486,12 @@ __global__ void __launch_bounds__(kCommThreads) pull_kernel(Params p) {
     return;
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int warps_total = gridDim.x * (kCommThreads / 32);
+  const int warps_total = gridDim.x * (kPullThreads / 32);
   const int nvec = p.hidden / 8;
   const SlotLayout sl = p.lay.slot[p.slot];
-  for (int t = blockIdx.x * (kCommThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
-    const uint4* srcs[8];
-    float scale[8];
+  for (int t = blockIdx.x * (kPullThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
+    const uint4* srcs[MAXR];
+    float scale[MAXR];
     int ns = 0;
     for (int j = 0; j < p.topk; ++j) {
       const int a = t * p.topk + j;
@@ -439,48 +503,7 @@ __global__ void __launch_bounds__(kCommThreads) pull_kernel(Params p) {
       ++ns;
     }
     uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(t) * p.hidden);
-    constexpr int U = 2;
-    for (int base = 0; base < nvec; base += 32 * U) {
-      float acc[U][8];
-      uint4 v[U][8];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
-      }
-      // Issue every load of this step before reducing, to keep NVLink busy.
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (q < ns) {
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int i = base + u * 32 + lane;
-            if (i < nvec) v[u][q] = srcs[q][i];
-          }
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (q < ns) {
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int i = base + u * 32 + lane;
-            if (i < nvec) acc_bf16x8(acc[u], v[u][q], scale[q]);
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int i = base + u * 32 + lane;
-        if (i < nvec) {
-          uint4 o;
-          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-          for (int w = 0; w < 4; ++w) h[w] = __floats2bfloat162_rn(acc[u][2 * w], acc[u][2 * w + 1]);
-          dst[i] = o;
-        }
-      }
-    }
+    pull_token<U, MAXR>(srcs, scale, ns, dst, nvec, lane);
   }
 }
 
@@ -727,11 +750,13 @@ extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64
 extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
                                            const float* topk_weights, int32_t num_tokens,
                                            int32_t topk, int32_t slot, uint64_t epoch,
-                                           int32_t num_blocks, int32_t pad_rows, uint64_t wait_ns,
+                                           int32_t num_blocks, int32_t pad_rows,
+                                           int32_t expert_alignment, uint64_t wait_ns,
                                            int32_t* status, void* stream_) {
   using namespace moe::ep;
   if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
-      num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1)
+      num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
+      expert_alignment < 1 || expert_alignment > 4096)
     return MOE_ERR_INVALID_ARG;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   Params p = base_params(ep, slot, epoch, wait_ns, status);
@@ -747,6 +772,7 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
   p.my_counts = ep->my_counts;
   p.done_ctr = ep->done_ctr;
   p.pad_rows = pad_rows ? 1 : 0;
+  p.align = expert_alignment;
   p.host_info = ep->host_info;
   if (cudaMemsetAsync(ep->done_ctr, 0, sizeof(unsigned int), stream) != cudaSuccess)
     return MOE_ERR_CUDA;
@@ -790,7 +816,15 @@ extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
   p.send_pos = ep->send_pos[slot];
   p.out = static_cast<__nv_bfloat16*>(out);
   p.weighted = weighted ? 1 : 0;
-  pull_kernel<<<num_blocks, kCommThreads, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  // The pass width bounds the registers a lane needs for all of a token's rows.
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int grid = num_blocks;
+  if (topk <= 2)
+    pull_kernel<8, 2><<<grid, kPullThreads, 0, stream>>>(p);
+  else if (topk <= 4)
+    pull_kernel<4, 4><<<grid, kPullThreads, 0, stream>>>(p);
+  else
+    pull_kernel<2, 8><<<grid, kPullThreads, 0, stream>>>(p);
   return check_launch();
 }
 
@@ -825,13 +859,13 @@ extern "C" int32_t moe_ep_dispatch_layout(const int64_t* topk_idx, int32_t num_t
 extern "C" int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_idx,
                                    const float* topk_weights, int32_t num_tokens, int32_t topk,
                                    int32_t slot, uint64_t epoch, int32_t num_blocks,
-                                   int32_t pad_rows, uint64_t wait_ns, int32_t* status,
-                                   void* stream) {
+                                   int32_t pad_rows, int32_t expert_alignment, uint64_t wait_ns,
+                                   int32_t* status, void* stream) {
   int rc = moe_ep_dispatch_begin(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
                                  status, stream);
   if (rc == MOE_OK)
     rc = moe_ep_dispatch_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
-                                 num_blocks, pad_rows, wait_ns, status, stream);
+                                 num_blocks, pad_rows, expert_alignment, wait_ns, status, stream);
   if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
   return rc;
 }

@@ -29,10 +29,31 @@ struct Params {
   int tile_order;
   int* work_counter;
   int32_t* status;
+  // optional epilogue operands (all may be null)
+  const float* row_scale;  // v = acc * row_scale[row]
+  const void* aux_in;      // MOE_ACT_DGELU: C = v * gelu'(aux_in[row, col])
+  void* aux_out;           // aux_out[row, col] = v (before the activation)
+  int64_t ld_aux;
 };
 
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+// d/dx [x * Phi(x)] = Phi(x) + x * phi(x), with Phi the standard normal CDF.
+__device__ __forceinline__ float gelu_erf_grad(float x) {
+  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+  const float pdf = 0.39894228040143267794f * expf(-0.5f * x * x);
+  return cdf + x * pdf;
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (BF16) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+  }
 }
 
 template <bool BF16>
@@ -54,15 +75,19 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const v
 }
 
 // Epilogue of one 128-row x 256-column fp32 accumulator held in TMEM lanes
-// [32*quad, 32*quad+32) of this warp: optional GELU, round, and 16-byte stores of
-// rows [0, rows) of the tile starting at global row `row0`, columns n0.. (< n).
+// [32*quad, 32*quad+32) of this warp, for rows [0, rows) of the tile starting at
+// global row `row0`, columns n0.. (< n): v = acc (* row_scale), optionally saved
+// to aux_out, then C = act(v) with act none, GELU or v * gelu'(aux_in), rounded
+// and written with 16-byte stores.
 template <bool BF16>
 __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int lane, int row0,
                                                   int rows, int n0, const Params& p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int row_in_tile = quad * 32 + lane;
   const bool row_ok = row_in_tile < rows;
-  T* crow = reinterpret_cast<T*>(p.c) + (int64_t(row0) + row_in_tile) * p.ldc;
+  const int64_t grow = int64_t(row0) + row_in_tile;
+  T* crow = reinterpret_cast<T*>(p.c) + grow * p.ldc;
+  const float rs = (p.row_scale != nullptr && row_ok) ? p.row_scale[grow] : 1.0f;
 #pragma unroll 1
   for (int ch = 0; ch < 256 / 32; ++ch) {
     uint32_t r[32];
@@ -70,28 +95,46 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
     tmem_wait_ld();
     const int col = n0 + ch * 32;
     if (row_ok && col < p.n) {
-      uint32_t packed[16];
+      const int nvec = min(4, (p.n - col) / 8);  // 16-byte vectors inside the matrix
+      float v[32];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float lo = __uint_as_float(r[2 * j]);
-        float hi = __uint_as_float(r[2 * j + 1]);
-        if (p.activation == MOE_ACT_GELU) {
-          lo = gelu_erf(lo);
-          hi = gelu_erf(hi);
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
+      if (p.aux_out != nullptr) {
+        uint4* ad = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.aux_out) + grow * p.ld_aux + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (q < nvec)
+            ad[q] = make_uint4(pack2<BF16>(v[8 * q], v[8 * q + 1]), pack2<BF16>(v[8 * q + 2], v[8 * q + 3]),
+                               pack2<BF16>(v[8 * q + 4], v[8 * q + 5]),
+                               pack2<BF16>(v[8 * q + 6], v[8 * q + 7]));
+      }
+      if (p.activation == MOE_ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      } else if (p.activation == MOE_ACT_DGELU) {
+        const uint4* ai =
+            reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux_in) + grow * p.ld_aux + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (q < nvec) {
+            const uint4 a = ai[q];
+            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float2 f = unpack2<BF16>(w[h]);
+              v[8 * q + 2 * h] *= gelu_erf_grad(f.x);
+              v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
+            }
+          }
         }
-        packed[j] = pack2<BF16>(lo, hi);
       }
       uint4* dst = reinterpret_cast<uint4*>(crow + col);
-      if (col + 32 <= p.n) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-      } else {
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          if (col + 8 * v + 8 <= p.n)
-            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-      }
+      for (int q = 0; q < 4; ++q)
+        if (q < nvec)
+          dst[q] = make_uint4(pack2<BF16>(v[8 * q], v[8 * q + 1]), pack2<BF16>(v[8 * q + 2], v[8 * q + 3]),
+                              pack2<BF16>(v[8 * q + 4], v[8 * q + 5]),
+                              pack2<BF16>(v[8 * q + 6], v[8 * q + 7]));
     }
   }
 }

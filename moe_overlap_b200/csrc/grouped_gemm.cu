@@ -365,17 +365,25 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
 
 using namespace moe;
 
-extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int64_t b_stride_e,
-                                    int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
-                                    const void* expert_offsets, int32_t offsets_int64,
-                                    int64_t m_total, int64_t k, int64_t n, int32_t num_experts,
-                                    int32_t dtype, int32_t activation, int32_t num_sms,
-                                    int32_t use_atomic_queue, int32_t* work_counter,
-                                    int32_t* status, void* stream_) {
+extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b,
+                                       int64_t b_stride_e, int64_t b_stride_k, int64_t b_stride_n,
+                                       void* c, int64_t ldc, const void* expert_offsets,
+                                       int32_t offsets_int64, int64_t m_total, int64_t k,
+                                       int64_t n, int32_t num_experts, int32_t dtype,
+                                       int32_t activation, int32_t num_sms,
+                                       int32_t use_atomic_queue, int32_t* work_counter,
+                                       const float* row_scale, const void* aux_in, void* aux_out,
+                                       int64_t ld_aux, int32_t* status, void* stream_) {
   using namespace moe::gg;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_F16) return MOE_ERR_INVALID_ARG;
-  if (activation != MOE_ACT_NONE && activation != MOE_ACT_GELU) return MOE_ERR_INVALID_ARG;
+  if (activation != MOE_ACT_NONE && activation != MOE_ACT_GELU && activation != MOE_ACT_DGELU)
+    return MOE_ERR_INVALID_ARG;
+  if (activation == MOE_ACT_DGELU && aux_in == nullptr) return MOE_ERR_INVALID_ARG;
+  if ((aux_in != nullptr || aux_out != nullptr) &&
+      (ld_aux < n || ld_aux % 8 != 0 || (aux_in && !aligned16(aux_in)) ||
+       (aux_out && !aligned16(aux_out))))
+    return MOE_ERR_INVALID_ARG;
   if (m_total < 0 || k < 0 || n < 0 || num_experts < 0) return MOE_ERR_INVALID_ARG;
   if (m_total > INT32_MAX || k > INT32_MAX || n > INT32_MAX) return MOE_ERR_INVALID_ARG;
   if (num_experts > MAX_EXPERTS) return MOE_ERR_UNSUPPORTED;
@@ -449,6 +457,10 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
   p.tile_order = gemm_tile_order();
   p.work_counter = work_counter;
   p.status = status;
+  p.row_scale = row_scale;
+  p.aux_in = aux_in;
+  p.aux_out = aux_out;
+  p.ld_aux = ld_aux;
 
   if (p.use_atomic &&
       cudaMemsetAsync(work_counter, 0, sizeof(int32_t), stream) != cudaSuccess)
@@ -459,4 +471,18 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
   if (bf16 && !b_mn) return launch<true, false>(ta, tb, p, grid, stream);
   if (!bf16 && b_mn) return launch<false, true>(ta, tb, p, grid, stream);
   return launch<false, false>(ta, tb, p, grid, stream);
+}
+
+extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int64_t b_stride_e,
+                                    int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                                    const void* expert_offsets, int32_t offsets_int64,
+                                    int64_t m_total, int64_t k, int64_t n, int32_t num_experts,
+                                    int32_t dtype, int32_t activation, int32_t num_sms,
+                                    int32_t use_atomic_queue, int32_t* work_counter,
+                                    int32_t* status, void* stream) {
+  if (activation == MOE_ACT_DGELU) return MOE_ERR_INVALID_ARG;  // needs aux_in: use _ex
+  return moe_grouped_gemm_ex(a, lda, b, b_stride_e, b_stride_k, b_stride_n, c, ldc,
+                             expert_offsets, offsets_int64, m_total, k, n, num_experts, dtype,
+                             activation, num_sms, use_atomic_queue, work_counter, nullptr,
+                             nullptr, nullptr, 0, status, stream);
 }

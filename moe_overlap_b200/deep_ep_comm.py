@@ -173,7 +173,7 @@ class DeepEPDispatcher:
 
     def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
                  previous_event: Optional[object] = None, *,
-                 exact_size: Optional[bool] = None) -> DispatchResult:
+                 exact_size: Optional[bool] = None, expert_alignment: int = 1) -> DispatchResult:
         if x.dtype != torch.bfloat16:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
@@ -199,7 +199,7 @@ class DeepEPDispatcher:
             if xc.data_ptr() % 16 != 0:
                 xc = xc.clone()
             self._ep.dispatch(xc, ic, wc, slot, epoch, self.num_sms, not exact, self.wait_ns,
-                              self._status)
+                              self._status, expert_alignment)
             offs = self._ep.slots[slot].expert_offsets
             per_expert = offs[1:] - offs[:-1]
             event = torch.cuda.Event()

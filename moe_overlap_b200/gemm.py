@@ -24,7 +24,8 @@ __all__ = [
 ]
 
 _DTYPE_CODE = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_F16}
-_ACT_CODE = {None: _lib.MOE_ACT_NONE, "none": _lib.MOE_ACT_NONE, "gelu": _lib.MOE_ACT_GELU}
+_ACT_CODE = {None: _lib.MOE_ACT_NONE, "none": _lib.MOE_ACT_NONE, "gelu": _lib.MOE_ACT_GELU,
+             "dgelu": _lib.MOE_ACT_DGELU}
 
 
 def _aligned(t: torch.Tensor) -> bool:
@@ -61,8 +62,16 @@ def grouped_gemm(
     num_sms: Optional[int] = None,
     use_atomic_queue: bool = False,
     work_counter: Optional[torch.Tensor] = None,
+    row_scale: Optional[torch.Tensor] = None,
+    aux_in: Optional[torch.Tensor] = None,
+    aux_out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """``out[off[e]:off[e+1]] = act(a_cat[off[e]:off[e+1]] @ b_expert[e])`` on the GPU.
+
+    Optional epilogue operands: ``row_scale`` (float32 ``[M]``, multiplies each
+    row of the product), ``aux_out`` (``[M, N]``, receives the product before
+    the activation) and ``aux_in`` (``[M, N]``; with ``activation="dgelu"`` the
+    result is the product times gelu'(aux_in), the fused GELU backward).
 
     The extended entry point behind ``persistent_grouped_gemm``: optional fused
     exact GELU (``activation="gelu"``), caller-provided output, and ``num_sms``
@@ -103,19 +112,35 @@ def grouped_gemm(
             work_counter = torch.empty(1, device=device, dtype=torch.int32)
         counter_ptr = work_counter.data_ptr()
 
+    ld_aux = 0
+    for t in (aux_in, aux_out):
+        if t is not None:
+            if (t.shape != (m_total, n_size) or t.dtype != a_cat.dtype or t.stride(1) != 1
+                    or n_pad or t.data_ptr() % 16 != 0 or t.stride(0) % 8 != 0):
+                raise ValueError("aux tensors must be [M, N] in the input dtype, 16-byte aligned rows")
+            if ld_aux and t.stride(0) != ld_aux:
+                raise ValueError("aux_in and aux_out must share a row stride")
+            ld_aux = t.stride(0)
+    if row_scale is not None and (row_scale.dtype != torch.float32 or row_scale.numel() < m_total
+                                  or not row_scale.is_contiguous()):
+        raise ValueError("row_scale must be a contiguous float32 tensor of M entries")
     lib = _lib.load()
     _lib.check_status(device)
     status = _lib.status_word(device)
-    rc = lib.moe_grouped_gemm(
+    rc = lib.moe_grouped_gemm_ex(
         a_use.data_ptr(), a_use.stride(0),
         b_use.data_ptr(), b_use.stride(0), b_use.stride(1), b_use.stride(2),
         c_use.data_ptr(), c_use.stride(0),
         offs.data_ptr(), offs64,
         m_total, k_size + k_pad, n_use, num_experts,
         dtype_code, act_code, int(num_sms), 1 if use_atomic_queue else 0,
-        counter_ptr, status.data_ptr(), _lib.stream_handle(device),
+        counter_ptr,
+        row_scale.data_ptr() if row_scale is not None else None,
+        aux_in.data_ptr() if aux_in is not None else None,
+        aux_out.data_ptr() if aux_out is not None else None,
+        ld_aux, status.data_ptr(), _lib.stream_handle(device),
     )
-    _lib.check_call(rc, "moe_grouped_gemm")
+    _lib.check_call(rc, "moe_grouped_gemm_ex")
     if c_use is not out:
         out.copy_(c_use[:, :n_size])
     if _lib.sync_check_enabled():

@@ -47,10 +47,18 @@ def random_weights(num_experts: int, hidden: int, ffn: int, std: float = 0.02, s
 
 
 class MoELayer:
+    """Expert-parallel routed MoE layer.
+
+    The grouped GEMMs use the atomic tile queue by default: they share the SMs
+    with the exchange kernels, and a CTA pair that starts late (its SM still
+    busy with a dispatch or combine block) then simply takes fewer tiles
+    instead of delaying a fixed striped share.
+    """
+
     def __init__(self, hidden_size: int, ffn_size: int, num_experts: int, top_k: int, *,
                  group: Optional[dist.ProcessGroup] = None, renormalize: bool = False,
                  router_bias: bool = False, num_comm_sms: int = 24,
-                 micro_batch_size: int = 4096, use_atomic_queue: bool = False,
+                 micro_batch_size: int = 4096, use_atomic_queue: bool = True,
                  max_recv_rows: Optional[int] = None):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         self.group = group
@@ -128,15 +136,18 @@ class MoELayer:
         cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
                             w[chunks[0][0]:chunks[0][1]])
         for i, (s, e) in enumerate(chunks):
-            nxt = None
-            if i + 1 < len(chunks):
-                ns, ne = chunks[i + 1]
-                nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne])
+            # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
+            # starts them as soon as this chunk's rows have landed, and the host
+            # time spent enqueuing the next dispatch overlaps them.
             with torch.cuda.stream(self.compute_stream):
                 cur.event.current_stream_wait()
                 y = self._experts(cur)
                 done = torch.cuda.Event()
                 done.record(self.compute_stream)
+            nxt = None
+            if i + 1 < len(chunks):
+                ns, ne = chunks[i + 1]
+                nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne])
             disp.combine(y, cur.handle, previous_event=done, weighted=True, out=out[s:e])
             cur = nxt
         torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)

@@ -41,8 +41,13 @@ def dispatch_layout(topk_idx: np.ndarray, num_experts: int, world: int):
     return per_rank_counts, per_expert, in_rank
 
 
-def dispatch(xs, topk_idxs, topk_weights, num_experts: int):
+def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: int = 1):
     """Expert-ordered dispatch over ``W = len(xs)`` ranks.
+
+    ``expert_alignment`` rounds each local expert's segment up to a multiple of
+    that many rows (DeepEP's dispatch argument of that name,
+    thirdParty/DeepEP/deep_ep/buffer.py:327); the padding rows are zero with
+    ``topk_idx`` -1, weight 0 and source (-1, -1).
 
     xs[r]: [T_r, H] bf16 bits (uint16); topk_idxs[r]: [T_r, k] int64 global
     expert ids (-1 = none); topk_weights[r]: [T_r, k] float32.
@@ -64,17 +69,25 @@ def dispatch(xs, topk_idxs, topk_weights, num_experts: int):
                 if 0 <= e < num_experts:
                     buckets[e // per_rank][e % per_rank].append((r, t, j))
     recv, send_pos = [], [np.full(np.asarray(topk_idxs[r]).shape, -1, np.int32) for r in range(world)]
+    al = max(1, int(expert_alignment))
     for d in range(world):
-        order = [a for le in range(per_rank) for a in buckets[d][le]]
-        counts = [len(buckets[d][le]) for le in range(per_rank)]
+        order, counts = [], []
+        for le in range(per_rank):
+            seg = list(buckets[d][le])
+            padded = -(-len(seg) // al) * al
+            counts.append(padded)
+            order += seg + [None] * (padded - len(seg))
         n = len(order)
         hidden = xs[0].shape[1]
         rx = np.zeros((n, hidden), dtype=np.uint16)
         ridx = np.full((n, k), -1, dtype=np.int64)
         rw = np.zeros((n, k), dtype=np.float32)
-        src_rank = np.zeros(n, dtype=np.int32)
-        src_tok = np.zeros(n, dtype=np.int32)
-        for row, (r, t, j) in enumerate(order):
+        src_rank = np.full(n, -1, dtype=np.int32)
+        src_tok = np.full(n, -1, dtype=np.int32)
+        for row, item in enumerate(order):
+            if item is None:
+                continue
+            r, t, j = item
             e = int(topk_idxs[r][t, j])
             rx[row] = xs[r][t]
             ridx[row, j] = e % per_rank

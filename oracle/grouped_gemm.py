@@ -103,3 +103,37 @@ def grouped_gemm(a: np.ndarray, b: np.ndarray, offsets, dtype: str,
     if not defined.any():
         defined[:] = True
     return from_f32(acc, dtype), defined
+
+
+def gelu_erf_grad(x: np.ndarray) -> np.ndarray:
+    """d/dx of exact GELU: Phi(x) + x * phi(x), in float64."""
+    x64 = np.asarray(x, dtype=np.float64)
+    return 0.5 * (1.0 + erf(x64 / np.sqrt(2.0))) + x64 * np.exp(-0.5 * x64 * x64) / np.sqrt(2.0 * np.pi)
+
+
+def grouped_gemm_ex(a, b, offsets, dtype: str, activation=None, row_scale=None, aux_in=None):
+    """Extended epilogue: v = acc * row_scale; returns (C, aux_out=v) as storage arrays
+    and the defined-row mask.  activation None / "gelu" / "dgelu" (v * gelu'(aux_in))."""
+    acc, defined = grouped_gemm_f32(a, b, offsets, dtype)
+    if row_scale is not None:
+        acc = (acc * np.asarray(row_scale, np.float32)[:, None]).astype(np.float32)
+    aux = from_f32(acc, dtype)
+    if activation == "gelu":
+        out = gelu_erf(acc).astype(np.float32)
+    elif activation == "dgelu":
+        out = (acc * gelu_erf_grad(to_f32(aux_in, dtype))).astype(np.float32)
+    else:
+        out = acc
+    return from_f32(out, dtype), aux, defined
+
+
+def wgrad(a, b, offsets, dtype: str):
+    """C[e] = A[off[e]:off[e+1]]^T @ B[off[e]:off[e+1]] in fp32, rounded; [E, M, N]."""
+    off = np.asarray(offsets, dtype=np.int64)
+    af, bf = to_f32(a, dtype), to_f32(b, dtype)
+    out = np.zeros((len(off) - 1, af.shape[1], bf.shape[1]), dtype=np.float32)
+    for e in range(len(off) - 1):
+        s, t = int(off[e]), int(off[e + 1])
+        if t > s:
+            out[e] = af[s:t].T @ bf[s:t]
+    return from_f32(out, dtype)

@@ -166,3 +166,30 @@ def test_wait_that_nobody_satisfies_times_out_with_status(cuda_device):
         assert float((torch.ones(4, device=cuda_device) * 2).sum()) == 8.0
     finally:
         grp.close()
+
+
+@pytest.mark.parametrize("world,align", [(1, 64), (2, 64), (4, 16)])
+def test_expert_alignment_pads_segments(cuda_device, world, align):
+    tokens, topk, hidden, E = 300, 2, 128, 8
+    xs, idxs, ws = routing(world, tokens, E, topk, seed=70 + world, hidden=hidden)
+    grp = LocalGroup(world, E, hidden, tokens, topk, world * tokens * topk + E * align, num_blocks=5)
+    try:
+        slot, epoch = grp.dispatch([x.to(cuda_device) for x in xs], [i.to(cuda_device) for i in idxs],
+                                   [w.to(cuda_device) for w in ws], expert_alignment=align)
+        torch.cuda.synchronize()
+        assert int(grp.status.item()) == 0
+        recv, send_pos = oep.dispatch([to_storage(x) for x in xs], [i.numpy() for i in idxs],
+                                      [w.numpy() for w in ws], E, expert_alignment=align)
+        for d, ep in enumerate(grp.eps):
+            v, want = ep.slots[slot], recv[d]
+            n = int(want["offsets"][-1])
+            assert np.array_equal(v.expert_offsets.cpu().numpy(), want["offsets"])
+            assert all(int(o) % align == 0 for o in want["offsets"])
+            assert np.array_equal(to_storage(v.recv_x[:n]), want["x"])
+            assert np.array_equal(v.recv_topk_idx[:n, :topk].cpu().numpy(), want["topk_idx"])
+            assert np.array_equal(v.recv_src[:n, 1].cpu().numpy(), want["src_token"])
+        for r, ep in enumerate(grp.eps):
+            got = ep.slots[slot].send_pos[: tokens * topk].view(tokens, topk).cpu().numpy()
+            assert np.array_equal(got, send_pos[r])
+    finally:
+        grp.close()

@@ -170,3 +170,66 @@ def test_expert_offsets_on_device(cuda_device):
 def test_status_word_clean_after_valid_calls(cuda_device):
     _lib.check_status(cuda_device, sync=True)
     assert int(_lib.status_word(cuda_device)[0]) == 0
+
+
+def test_epilogue_row_scale_aux_out_and_dgelu(cuda_device):
+    counts = [70, 0, 130, 64]
+    a, b, off = gemm_inputs(counts, 256, 384, "bf16", seed=31, w_std=0.05)
+    m = a.shape[0]
+    g = torch.Generator().manual_seed(32)
+    scale = torch.rand(m, generator=g) + 0.5
+    aux_in = torch.randn(m, 384, generator=g).to(torch.bfloat16)
+    da, db, doff = a.to(cuda_device), b.to(cuda_device), off.to(cuda_device)
+    aux_out = torch.empty(m, 384, dtype=torch.bfloat16, device=cuda_device)
+    c = mo.grouped_gemm(da, db, doff, activation="gelu", row_scale=scale.to(cuda_device),
+                        aux_out=aux_out)
+    c2 = mo.grouped_gemm(da, db, doff, activation="dgelu", aux_in=aux_in.to(cuda_device))
+    mo.check_status(cuda_device, sync=True)
+    want, want_aux, defined = og.grouped_gemm_ex(to_storage(a), to_storage(b), off.numpy(), "bf16",
+                                                 "gelu", row_scale=scale.numpy())
+    assert_matches_oracle(c, want, defined, "bf16")
+    assert_matches_oracle(aux_out, want_aux, defined, "bf16")
+    want2, _, _ = og.grouped_gemm_ex(to_storage(a), to_storage(b), off.numpy(), "bf16", "dgelu",
+                                     aux_in=to_storage(aux_in))
+    assert_matches_oracle(c2, want2, defined, "bf16")
+
+
+@pytest.mark.parametrize("m,n", [(256, 512), (192, 136)])
+def test_wgrad_matches_oracle(cuda_device, m, n):
+    counts = [128, 0, 64, 384, 192]  # 64-row aligned segments, one empty expert
+    g = torch.Generator().manual_seed(m + n)
+    rows = sum(counts)
+    a = torch.randn(rows, m, generator=g).to(torch.bfloat16)
+    b = torch.randn(rows, n, generator=g).to(torch.bfloat16)
+    off = torch.tensor(og.expert_offsets_from_recv_counts(counts).astype(np.int32))
+    c = torch.full((len(counts), m, n), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    da, db, doff = a.to(cuda_device), b.to(cuda_device), off.to(cuda_device)
+    rc = lib.moe_grouped_gemm_wgrad(da.data_ptr(), m, db.data_ptr(), n, c.data_ptr(), n, m * n,
+                                    doff.data_ptr(), 0, rows, m, n, len(counts),
+                                    _lib.MOE_DTYPE_BF16, 148, status.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    want = og.wgrad(to_storage(a), to_storage(b), off.numpy(), "bf16")
+    got = to_storage(c.reshape(len(counts) * m, n))
+    assert_matches_oracle(torch.from_numpy(got.view(np.int16)).view(torch.bfloat16),
+                          want.reshape(len(counts) * m, n), np.ones(len(counts) * m, bool), "bf16")
+
+
+def test_wgrad_rejects_misaligned_segments(cuda_device):
+    rows, m, n = 200, 64, 64
+    a = torch.zeros(rows, m, dtype=torch.bfloat16, device=cuda_device)
+    b = torch.zeros(rows, n, dtype=torch.bfloat16, device=cuda_device)
+    off = torch.tensor([0, 100, 200], dtype=torch.int32, device=cuda_device)
+    c = torch.empty(2, m, n, dtype=torch.bfloat16, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    rc = _lib.load().moe_grouped_gemm_wgrad(a.data_ptr(), m, b.data_ptr(), n, c.data_ptr(), n,
+                                            m * n, off.data_ptr(), 0, rows, m, n, 2,
+                                            _lib.MOE_DTYPE_BF16, 148, status.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == _lib.MOE_ERR_OFFSETS
