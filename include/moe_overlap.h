@@ -269,6 +269,8 @@ MOE_API int32_t moe_ep_views(moe_ep_t ep, int32_t slot, moe_ep_views_t* views);
  *            expert_alignment (>= 1, DeepEP's argument of that name,
  *            deep_ep/buffer.py:327) rounds every local expert's segment up to a
  *            multiple of that many rows; the padding rows are zeroed with no slot;
+ *            scale_rows != 0 pushes each row multiplied by its slot's weight
+ *            (rounded to bf16), e.g. the weighted output gradient of a backward;
  *                                                       ~ intranode.cu dispatch
  *   end      waits (bounded) until every rank's rows have landed here.
  * x: [num_tokens][hidden] bf16; topk_idx: [num_tokens][topk] int64 global expert ids
@@ -283,15 +285,15 @@ MOE_API int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_
                                         const float* topk_weights, int32_t num_tokens,
                                         int32_t topk, int32_t slot, uint64_t epoch,
                                         int32_t num_blocks, int32_t pad_rows,
-                                        int32_t expert_alignment, uint64_t wait_ns,
-                                        int32_t* status, void* stream);
+                                        int32_t expert_alignment, int32_t scale_rows,
+                                        uint64_t wait_ns, int32_t* status, void* stream);
 MOE_API int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch, uint64_t wait_ns,
                                     int32_t* status, void* stream);
 MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_idx,
                                 const float* topk_weights, int32_t num_tokens, int32_t topk,
                                 int32_t slot, uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
-                                int32_t expert_alignment, uint64_t wait_ns, int32_t* status,
-                                void* stream);
+                                int32_t expert_alignment, int32_t scale_rows, uint64_t wait_ns,
+                                int32_t* status, void* stream);
 
 /*
  * Combine, in two phases (moe_ep_combine runs both):
@@ -314,6 +316,17 @@ MOE_API int32_t moe_ep_combine(moe_ep_t ep, const int64_t* topk_idx, const float
                                int32_t num_tokens, int32_t topk, int32_t slot, uint64_t epoch,
                                int32_t weighted, void* out, int32_t num_blocks, uint64_t wait_ns,
                                int32_t* status, void* stream);
+
+/*
+ * Gradient of the top-k weights for the routed experts' backward:
+ * out[t][j] = <grad_out[t], y(t, j)> in fp32, y(t, j) being the expert-output row
+ * the owner produced for (token t, slot j) in `slot` (read through the peer
+ * pointers, so it works at any world size); 0 where the slot had no expert.
+ * grad_out: [num_tokens][hidden] bf16.  No counterpart in the reference.
+ */
+MOE_API int32_t moe_ep_topk_weight_grad(moe_ep_t ep, const void* grad_out, const int64_t* topk_idx,
+                                        int32_t num_tokens, int32_t topk, int32_t slot, float* out,
+                                        int32_t num_blocks, void* stream);
 
 /*
  * DeepEP's get_dispatch_layout (thirdParty/DeepEP/deep_ep/buffer.py:293-319,

@@ -128,6 +128,7 @@ struct Params {
   int num_layout_blocks;
   int pad_rows;  // fill recv_topk_idx rows past the received count with -1
   int align;     // receive segments of each local expert rounded up to this many rows
+  int scale_rows;  // multiply each pushed row by its slot's weight (bf16 result)
   int64_t* host_info;
   // combine
   __nv_bfloat16* out;
@@ -229,6 +230,18 @@ __global__ void count_kernel(Params p) {
   }
 }
 
+__device__ __forceinline__ uint4 scale_bf16x8(const uint4& v, float s) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  uint4 o;
+  __nv_bfloat162* r = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    r[i] = __floats2bfloat162_rn(__fmul_rn(f.x, s), __fmul_rn(f.y, s));
+  }
+  return o;
+}
+
 // Shared state every scatter/combine block derives from the count matrix.
 struct CountView {
   int exp_base[kMaxExperts];  // first row of expert e on its owner
@@ -316,6 +329,7 @@ __global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
     for (int t = blockIdx.x * (kCommThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
       const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
       uint4* dst[8];
+      float dscale[8];
       int nd = 0;
       for (int j = 0; j < p.topk; ++j) {
         const int a = t * p.topk + j;
@@ -330,6 +344,7 @@ __global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
         const int row = cv.exp_base[e] + cv.my_prefix[e] + p.block_hist[blk * E + e] +
                         p.rank_in_block[a];
         uint8_t* peer = p.peers[d];
+        dscale[nd] = p.topk_w[a];
         dst[nd++] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
         if (lane < p.topk) {
           at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
@@ -356,7 +371,7 @@ __global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (i < nvec) dst[q][i] = v[u];
+            if (i < nvec) dst[q][i] = p.scale_rows ? scale_bf16x8(v[u], dscale[q]) : v[u];
           }
         }
       }
@@ -504,6 +519,41 @@ __global__ void __launch_bounds__(kPullThreads, 2) pull_kernel(Params p) {
     }
     uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(t) * p.hidden);
     pull_token<U, MAXR>(srcs, scale, ns, dst, nvec, lane);
+  }
+}
+
+// d loss / d w[t][j] = <grad_out[t], y(t, j)>: the row the owner returned for
+// (token t, slot j) in `slot`'s expert outputs, read through the peer pointers.
+// One warp per (token, slot); fp32 dot product.
+__global__ void __launch_bounds__(256) topk_weight_grad_kernel(Params p, const __nv_bfloat16* grad_out,
+                                                             float* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (blockDim.x / 32);
+  const int nvec = p.hidden / 8;
+  const SlotLayout sl = p.lay.slot[p.slot];
+  for (int a = blockIdx.x * (blockDim.x / 32) + warp; a < p.num_tokens * p.topk; a += warps_total) {
+    const int t = a / p.topk;
+    const int row = p.send_pos[a];
+    float acc = 0.0f;
+    if (row >= 0) {
+      const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
+      const uint4* y = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
+      const uint4* g = reinterpret_cast<const uint4*>(grad_out + static_cast<int64_t>(t) * p.hidden);
+      for (int i = lane; i < nvec; i += 32) {
+        const uint4 yv = y[i], gv = g[i];
+        const __nv_bfloat162* yh = reinterpret_cast<const __nv_bfloat162*>(&yv);
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 yf = __bfloat1622float2(yh[h]), gf = __bfloat1622float2(gh[h]);
+          acc = fmaf(yf.x, gf.x, acc);
+          acc = fmaf(yf.y, gf.y, acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    }
+    if (lane == 0) out[a] = acc;
   }
 }
 
@@ -751,8 +801,8 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
                                            const float* topk_weights, int32_t num_tokens,
                                            int32_t topk, int32_t slot, uint64_t epoch,
                                            int32_t num_blocks, int32_t pad_rows,
-                                           int32_t expert_alignment, uint64_t wait_ns,
-                                           int32_t* status, void* stream_) {
+                                           int32_t expert_alignment, int32_t scale_rows,
+                                           uint64_t wait_ns, int32_t* status, void* stream_) {
   using namespace moe::ep;
   if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
@@ -773,6 +823,7 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
   p.done_ctr = ep->done_ctr;
   p.pad_rows = pad_rows ? 1 : 0;
   p.align = expert_alignment;
+  p.scale_rows = scale_rows ? 1 : 0;
   p.host_info = ep->host_info;
   if (cudaMemsetAsync(ep->done_ctr, 0, sizeof(unsigned int), stream) != cudaSuccess)
     return MOE_ERR_CUDA;
@@ -859,13 +910,14 @@ extern "C" int32_t moe_ep_dispatch_layout(const int64_t* topk_idx, int32_t num_t
 extern "C" int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_idx,
                                    const float* topk_weights, int32_t num_tokens, int32_t topk,
                                    int32_t slot, uint64_t epoch, int32_t num_blocks,
-                                   int32_t pad_rows, int32_t expert_alignment, uint64_t wait_ns,
-                                   int32_t* status, void* stream) {
+                                   int32_t pad_rows, int32_t expert_alignment, int32_t scale_rows,
+                                   uint64_t wait_ns, int32_t* status, void* stream) {
   int rc = moe_ep_dispatch_begin(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
                                  status, stream);
   if (rc == MOE_OK)
     rc = moe_ep_dispatch_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
-                                 num_blocks, pad_rows, expert_alignment, wait_ns, status, stream);
+                                 num_blocks, pad_rows, expert_alignment, scale_rows, wait_ns,
+                                 status, stream);
   if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
   return rc;
 }
@@ -902,4 +954,25 @@ extern "C" int32_t moe_ipc_import(const void* handle, void** dev_ptr_out) {
 extern "C" int32_t moe_ipc_close(void* dev_ptr) {
   if (dev_ptr == nullptr) return MOE_ERR_INVALID_ARG;
   return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+extern "C" int32_t moe_ep_topk_weight_grad(moe_ep_t ep, const void* grad_out,
+                                           const int64_t* topk_idx, int32_t num_tokens,
+                                           int32_t topk, int32_t slot, float* out,
+                                           int32_t num_blocks, void* stream) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 || num_tokens > ep->max_tokens ||
+      topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
+      (num_tokens > 0 && (grad_out == nullptr || topk_idx == nullptr || out == nullptr)) ||
+      !moe::aligned16(grad_out))
+    return MOE_ERR_INVALID_ARG;
+  if (num_tokens == 0) return MOE_OK;
+  Params p = base_params(ep, slot, 1, 0, nullptr);
+  p.topk_idx = topk_idx;
+  p.num_tokens = num_tokens;
+  p.topk = topk;
+  p.send_pos = ep->send_pos[slot];
+  topk_weight_grad_kernel<<<num_blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      p, static_cast<const __nv_bfloat16*>(grad_out), out);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }

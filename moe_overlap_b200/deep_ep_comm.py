@@ -173,7 +173,8 @@ class DeepEPDispatcher:
 
     def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
                  previous_event: Optional[object] = None, *,
-                 exact_size: Optional[bool] = None, expert_alignment: int = 1) -> DispatchResult:
+                 exact_size: Optional[bool] = None, expert_alignment: int = 1,
+                 scale_rows: bool = False) -> DispatchResult:
         if x.dtype != torch.bfloat16:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
@@ -199,7 +200,7 @@ class DeepEPDispatcher:
             if xc.data_ptr() % 16 != 0:
                 xc = xc.clone()
             self._ep.dispatch(xc, ic, wc, slot, epoch, self.num_sms, not exact, self.wait_ns,
-                              self._status, expert_alignment)
+                              self._status, expert_alignment, scale_rows)
             offs = self._ep.slots[slot].expert_offsets
             per_expert = offs[1:] - offs[:-1]
             event = torch.cuda.Event()
@@ -222,8 +223,32 @@ class DeepEPDispatcher:
             recv_src=views.recv_src[:rows],
         )
 
+    @property
+    def last_epoch(self) -> int:
+        """Epoch of the most recent dispatch (0 before the first)."""
+        return self._epoch
+
+    def _check_slot_live(self, handle: DispatchHandle) -> None:
+        if self._epoch - handle.epoch >= 2:
+            raise RuntimeError("the dispatch's exchange slot has been reused by a later dispatch")
+
+    def topk_weight_grad(self, grad_out: torch.Tensor, handle: DispatchHandle) -> torch.Tensor:
+        """d loss / d topk_weights of a combined dispatch: <grad_out[t], y(t, j)> (float32 [T, k]).
+
+        Reads the expert outputs that ``handle``'s combine summed, so call it before
+        the dispatch after next reuses that slot.
+        """
+        self._check_slot_live(handle)
+        if grad_out.shape != (handle.num_tokens, self.hidden_size):
+            raise ValueError(f"grad_out must be [{handle.num_tokens}, {self.hidden_size}]")
+        out = torch.empty(handle.num_tokens, handle.topk, dtype=torch.float32, device=self.device)
+        g = grad_out.to(torch.bfloat16).contiguous()
+        self._ep.topk_weight_grad(g, handle.topk_idx, handle.slot, out, 2 * self.num_sms)
+        return out
+
     def expert_out_buffer(self, handle: DispatchHandle) -> torch.Tensor:
         """The slot's expert-output rows: write here (e.g. as the GEMM's output) to skip a copy."""
+        self._check_slot_live(handle)
         return self._ep.slots[handle.slot].expert_out
 
     def combine(self, expert_out: torch.Tensor, handle: DispatchHandle,

@@ -157,13 +157,14 @@ class Endpoint:
             "moe_ep_dispatch_begin")
 
     def dispatch_scatter(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows, wait_ns,
-                         status, expert_alignment: int = 1):
+                         status, expert_alignment: int = 1, scale_rows: bool = False):
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch_scatter(self.handle, x.data_ptr(), topk_idx.data_ptr(),
                                              topk_w.data_ptr(), t, k, slot, epoch, num_blocks,
-                                             1 if pad_rows else 0, expert_alignment, wait_ns,
-                                             status.data_ptr(), self._stream()),
+                                             1 if pad_rows else 0, expert_alignment,
+                                             1 if scale_rows else 0, wait_ns, status.data_ptr(),
+                                             self._stream()),
             "moe_ep_dispatch_scatter")
 
     def dispatch_end(self, slot, epoch, wait_ns, status):
@@ -187,14 +188,23 @@ class Endpoint:
             "moe_ep_combine_end")
 
     def dispatch(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows, wait_ns, status,
-                 expert_alignment: int = 1):
+                 expert_alignment: int = 1, scale_rows: bool = False):
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch(self.handle, x.data_ptr(), topk_idx.data_ptr(),
                                      topk_w.data_ptr(), t, k, slot, epoch, num_blocks,
-                                     1 if pad_rows else 0, expert_alignment, wait_ns,
-                                     status.data_ptr(), self._stream()),
+                                     1 if pad_rows else 0, expert_alignment,
+                                     1 if scale_rows else 0, wait_ns, status.data_ptr(),
+                                     self._stream()),
             "moe_ep_dispatch")
+
+    def topk_weight_grad(self, grad_out, topk_idx, slot, out, num_blocks):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_topk_weight_grad(self.handle, grad_out.data_ptr(), topk_idx.data_ptr(),
+                                             t, k, slot, out.data_ptr(), num_blocks,
+                                             self._stream()),
+            "moe_ep_topk_weight_grad")
 
     def combine(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns, status):
         t, k = topk_idx.shape
@@ -252,14 +262,15 @@ class LocalGroup:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.eps[0].device)
         self.wait_ns = default_wait_ns()
 
-    def dispatch(self, xs, idxs, ws, pad_rows: bool = False, expert_alignment: int = 1):
+    def dispatch(self, xs, idxs, ws, pad_rows: bool = False, expert_alignment: int = 1,
+                 scale_rows: bool = False):
         self.epoch += 1
         slot, epoch = self.epoch % 2, self.epoch
         for r, ep in enumerate(self.eps):
             ep.dispatch_begin(xs[r], idxs[r], ws[r], slot, epoch, self.status)
         for r, ep in enumerate(self.eps):
             ep.dispatch_scatter(xs[r], idxs[r], ws[r], slot, epoch, self.num_blocks, pad_rows,
-                                self.wait_ns, self.status, expert_alignment)
+                                self.wait_ns, self.status, expert_alignment, scale_rows)
         for ep in self.eps:
             ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
         return slot, epoch

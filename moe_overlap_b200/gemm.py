@@ -18,6 +18,7 @@ from . import _lib
 __all__ = [
     "persistent_grouped_gemm",
     "grouped_gemm",
+    "grouped_gemm_wgrad",
     "expert_offsets_from_recv_counts",
     "reference_grouped_gemm",
     "tile_list",
@@ -293,3 +294,38 @@ def tile_list(
                                count.data_ptr(), None, stream)
         _lib.check_call(rc, "moe_tile_list")
     return we, wm, wn
+
+
+def grouped_gemm_wgrad(a: torch.Tensor, b: torch.Tensor, expert_offsets: torch.Tensor, *,
+                       out: Optional[torch.Tensor] = None,
+                       num_sms: Optional[int] = None) -> torch.Tensor:
+    """``out[e] = a[off[e]:off[e+1]].T @ b[off[e]:off[e+1]]`` (weight gradients).
+
+    ``a`` [R, M] and ``b`` [R, N] share the row index (token rows grouped by
+    expert); every segment must start and end on a multiple of 64 rows (the
+    exchange's ``expert_alignment=64``).  Returns ``[E, M, N]`` in the input dtype.
+    """
+    device = a.device
+    rows, m = a.shape
+    num_experts = expert_offsets.numel() - 1
+    n = b.shape[1]
+    if b.shape[0] != rows or b.dtype != a.dtype or a.dtype not in _DTYPE_CODE:
+        raise ValueError("a [R, M] and b [R, N] must share R and a bf16/fp16 dtype")
+    if out is None:
+        out = torch.empty((num_experts, m, n), dtype=a.dtype, device=device)
+    a_c = a if (a.stride(1) == 1 and a.data_ptr() % 16 == 0 and a.stride(0) % 8 == 0) else a.contiguous()
+    b_c = b if (b.stride(1) == 1 and b.data_ptr() % 16 == 0 and b.stride(0) % 8 == 0) else b.contiguous()
+    offs64 = 1 if expert_offsets.dtype == torch.int64 else 0
+    offs = expert_offsets.contiguous() if expert_offsets.dtype in (torch.int32, torch.int64) \
+        else expert_offsets.to(torch.int32).contiguous()
+    if num_sms is None:
+        num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+    lib = _lib.load()
+    _lib.check_status(device)
+    rc = lib.moe_grouped_gemm_wgrad(a_c.data_ptr(), a_c.stride(0), b_c.data_ptr(), b_c.stride(0),
+                                    out.data_ptr(), out.stride(1), out.stride(0), offs.data_ptr(),
+                                    offs64, rows, m, n, num_experts, _DTYPE_CODE[a.dtype],
+                                    int(num_sms), _lib.status_word(device).data_ptr(),
+                                    _lib.stream_handle(device))
+    _lib.check_call(rc, "moe_grouped_gemm_wgrad")
+    return out

@@ -27,7 +27,11 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .deep_ep_comm import DeepEPDispatcher
-from .gemm import grouped_gemm
+from .gemm import grouped_gemm, grouped_gemm_wgrad
+
+# Expert segments of a training dispatch are padded to this many rows so the
+# weight-gradient GEMM's 64-row k-blocks never straddle two experts.
+TRAIN_ALIGNMENT = 64
 
 
 @dataclass
@@ -59,7 +63,7 @@ class MoELayer:
                  group: Optional[dist.ProcessGroup] = None, renormalize: bool = False,
                  router_bias: bool = False, num_comm_sms: int = 24,
                  micro_batch_size: int = 4096, use_atomic_queue: bool = True,
-                 max_recv_rows: Optional[int] = None):
+                 max_recv_rows: Optional[int] = None, training: bool = False):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         self.group = group
         self.world = group.size() if group is not None else 1
@@ -77,6 +81,10 @@ class MoELayer:
         self.router_b = torch.zeros(num_experts, dtype=torch.float32, device=dev) if router_bias else None
         self.w1 = torch.zeros(self.experts_per_rank, ffn_size, hidden_size, dtype=bf16, device=dev)
         self.w2 = torch.zeros(self.experts_per_rank, hidden_size, ffn_size, dtype=bf16, device=dev)
+        if training and max_recv_rows is None:
+            # worst case of one dispatch plus the alignment padding of every local expert
+            max_recv_rows = (self.world * self.micro * min(2, self.experts_per_rank, top_k)
+                             + self.experts_per_rank * TRAIN_ALIGNMENT)
         self.dispatcher = DeepEPDispatcher(group, hidden_size, num_experts, num_sms=num_comm_sms,
                                            max_tokens_per_rank=self.micro, max_top_k=top_k,
                                            max_recv_rows=max_recv_rows, exact_size=False)
@@ -209,5 +217,90 @@ class MoELayer:
         entropy = (-probs * probs.clamp_min(1e-9).log()).sum(dim=-1).mean()
         return RouterStats(float(entropy), float(counts.std()), float(counts.std() / mean))
 
+    # ---------------------------------------------------------------- training --
+    def forward_autograd(self, x: torch.Tensor):
+        """Differentiable forward: returns (out, probs, topk_idx).
+
+        The router, softmax, top-k and optional renormalisation run in torch
+        autograd; the routed experts run on this package's kernels through
+        RoutedExperts (dispatch, GEMM1+GELU with the pre-activation saved, GEMM2,
+        weighted combine; backward: top-k weight gradient, weighted dispatch of the
+        output gradient, dgrad GEMMs with GELU' fused, combine, weight-gradient
+        GEMMs).  ``router_w``, ``w1`` and ``w2`` receive ``.grad`` when they
+        require it.  The whole batch is one chunk (micro_batch_size must cover it).
+        """
+        logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t()).float()
+        if self.router_b is not None:
+            logits = logits + self.router_b
+        probs = F.softmax(logits, dim=-1)
+        w, idx = torch.topk(probs, k=self.top_k, dim=-1)
+        if self.renormalize:
+            w = w / w.sum(dim=-1, keepdim=True)
+        out = RoutedExperts.apply(x, w, self.w1, self.w2, idx.to(torch.int64), self)
+        return out, probs, idx
+
+    def _train_forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor):
+        disp = self.dispatcher
+        if x.shape[0] > self.micro:
+            raise ValueError("training forward runs the batch as one chunk: raise micro_batch_size")
+        x = x.to(torch.bfloat16).contiguous()
+        res = disp.dispatch(x, idx, w.float(), exact_size=False, expert_alignment=TRAIN_ALIGNMENT)
+        res.event.current_stream_wait()
+        rows = res.recv_x.shape[0]
+        pre = torch.empty(rows, self.ffn, dtype=torch.bfloat16, device=self.device)
+        h = torch.empty_like(pre)
+        kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
+        grouped_gemm(res.recv_x, self.w1.detach().transpose(1, 2), res.expert_offsets, out=h,
+                     activation="gelu", aux_out=pre, **kw)
+        y = disp.expert_out_buffer(res.handle)
+        grouped_gemm(h, self.w2.detach().transpose(1, 2), res.expert_offsets, out=y, **kw)
+        out, ev = disp.combine(y, res.handle, weighted=True)
+        ev.current_stream_wait()
+        return out, dict(res=res, pre=pre, h=h, idx=idx, w=w.float())
+
+    def _train_backward(self, state: dict, dout: torch.Tensor):
+        disp, res = self.dispatcher, state["res"]
+        if disp.last_epoch != res.handle.epoch:
+            # The forward's receive rows and expert outputs stay in its exchange slot;
+            # the backward reads them and its own dispatch takes the other slot, so no
+            # dispatch may run in between.
+            raise RuntimeError("another dispatch ran on this layer between its forward and backward; "
+                               "run backward before the layer's next forward")
+        dout = dout.to(torch.bfloat16).contiguous()
+        kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
+        # d/d topk weight: <dout[t], y(t, j)>, read from the forward's expert outputs.
+        dw = disp.topk_weight_grad(dout, res.handle)
+        # The output gradient goes back to the experts weighted: dY = w * dout rows,
+        # laid out exactly like the forward rows (same routing and alignment).
+        rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False,
+                           expert_alignment=TRAIN_ALIGNMENT, scale_rows=True)
+        rb.event.current_stream_wait()
+        d_pre = torch.empty_like(state["pre"])
+        grouped_gemm(rb.recv_x, self.w2.detach(), rb.expert_offsets, out=d_pre, activation="dgelu",
+                     aux_in=state["pre"], **kw)
+        dx_rows = disp.expert_out_buffer(rb.handle)
+        grouped_gemm(d_pre, self.w1.detach(), rb.expert_offsets, out=dx_rows, **kw)
+        dx, ev = disp.combine(dx_rows, rb.handle, weighted=False)
+        dw2 = grouped_gemm_wgrad(rb.recv_x, state["h"], rb.expert_offsets, num_sms=self.gemm_sms)
+        dw1 = grouped_gemm_wgrad(d_pre, res.recv_x, rb.expert_offsets, num_sms=self.gemm_sms)
+        ev.current_stream_wait()
+        return dx, dw, dw1, dw2
+
     def close(self) -> None:
         self.dispatcher.close()
+
+
+class RoutedExperts(torch.autograd.Function):
+    """Autograd node of the routed experts (x, top-k weights, W1, W2 -> out)."""
+
+    @staticmethod
+    def forward(ctx, x, topk_w, w1, w2, topk_idx, layer):
+        out, state = layer._train_forward(x, topk_idx, topk_w)
+        ctx.layer, ctx.state = layer, state
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        dx, dw, dw1, dw2 = ctx.layer._train_backward(ctx.state, dout)
+        ctx.state = None
+        return dx, dw, dw1, dw2, None, None

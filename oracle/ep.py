@@ -41,7 +41,8 @@ def dispatch_layout(topk_idx: np.ndarray, num_experts: int, world: int):
     return per_rank_counts, per_expert, in_rank
 
 
-def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: int = 1):
+def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: int = 1,
+             scale_rows: bool = False):
     """Expert-ordered dispatch over ``W = len(xs)`` ranks.
 
     ``expert_alignment`` rounds each local expert's segment up to a multiple of
@@ -89,7 +90,11 @@ def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: in
                 continue
             r, t, j = item
             e = int(topk_idxs[r][t, j])
-            rx[row] = xs[r][t]
+            if scale_rows:
+                prod = bf16_bits_to_f32(xs[r][t]) * np.float32(topk_weights[r][t, j])
+                rx[row] = f32_to_bf16_bits(prod.astype(np.float32))
+            else:
+                rx[row] = xs[r][t]
             ridx[row, j] = e % per_rank
             rw[row, j] = topk_weights[r][t, j]
             src_rank[row], src_tok[row] = r, t
@@ -99,6 +104,24 @@ def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: in
         recv.append(dict(x=rx, topk_idx=ridx, topk_weights=rw, src_rank=src_rank,
                          src_token=src_tok, offsets=offsets))
     return recv, send_pos
+
+
+def topk_weight_grad(grad_outs, ys, topk_idxs, send_pos, num_experts: int):
+    """d loss / d w[t, j] of the weighted combine: <grad_out[t], y_{owner}(row(t, j))>
+    in float64 (the product sums in fp32 in its own order), 0 for empty slots."""
+    world = len(ys)
+    per_rank = num_experts // world
+    outs = []
+    for r in range(world):
+        idx = np.asarray(topk_idxs[r], dtype=np.int64)
+        g = bf16_bits_to_f32(grad_outs[r]).astype(np.float64)
+        out = np.zeros(idx.shape, dtype=np.float64)
+        for (t, j), pos in np.ndenumerate(send_pos[r]):
+            if pos >= 0:
+                y = bf16_bits_to_f32(ys[int(idx[t, j]) // per_rank][pos]).astype(np.float64)
+                out[t, j] = float(g[t] @ y)
+        outs.append(out)
+    return outs
 
 
 def combine(ys, topk_idxs, send_pos, num_experts: int, weights=None):

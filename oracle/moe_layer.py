@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .grouped_gemm import gelu_erf
+from .grouped_gemm import gelu_erf, gelu_erf_grad
 from .numerics import bf16_bits_to_f32, f32_to_bf16_bits
 
 
@@ -108,3 +108,96 @@ def router_stats(probs: np.ndarray, idx: np.ndarray, num_experts: int):
     entropy = float((-probs * np.log(np.maximum(probs, 1e-9))).sum(axis=-1).mean())
     std = float(counts.std(ddof=1))
     return entropy, std, std / mean
+
+
+def layer_backward_f32(x, router_w, w1, w2, top_k, dout, router_b=None, renormalize=False):
+    """Gradients of the routed layer (fp32 math, float64 accumulation).
+
+    Analytic backward of layer_forward_f32: per (token, slot) with expert e,
+    a = x W1[e]^T, h = gelu(a), y = h W2[e]^T, out = sum_j w_j y_j; then
+    dy = w dout, dw_j = <dout, y_j>, dh = dy W2[e], da = dh * gelu'(a),
+    dx += da W1[e], dW2[e] += dy^T h, dW1[e] += da^T x; the top-k weights'
+    gradient flows through the optional renormalisation and the softmax into
+    the router: dlogits = p * (dp - <p, dp>), dWr = dlogits^T x, dx += dlogits Wr.
+    Returns (dx, d_router_w, d_w1, d_w2).
+    """
+    x64 = x.astype(np.float64)
+    probs, idx, w = route(x, router_w, top_k, router_b, renormalize)
+    t_count = x.shape[0]
+    dx = np.zeros_like(x64)
+    dw1 = np.zeros(w1.shape, dtype=np.float64)
+    dw2 = np.zeros(w2.shape, dtype=np.float64)
+    dwt = np.zeros((t_count, top_k), dtype=np.float64)
+    d = dout.astype(np.float64)
+    for j in range(top_k):
+        for e in np.unique(idx[:, j]):
+            rows = np.nonzero(idx[:, j] == e)[0]
+            a = x64[rows] @ w1[e].T.astype(np.float64)
+            h = gelu_erf(a)
+            y = h @ w2[e].T.astype(np.float64)
+            dwt[rows, j] = (d[rows] * y).sum(axis=1)
+            dy = w[rows, j:j + 1].astype(np.float64) * d[rows]
+            dh = dy @ w2[e].astype(np.float64)
+            da = dh * gelu_erf_grad(a)
+            dx[rows] += da @ w1[e].astype(np.float64)
+            dw2[e] += dy.T @ h
+            dw1[e] += da.T @ x64[rows]
+    if renormalize:
+        raw = np.take_along_axis(probs, idx, axis=-1).astype(np.float64)
+        ssum = raw.sum(axis=-1, keepdims=True)
+        wt = raw / ssum
+        dwt = (dwt - (dwt * wt).sum(axis=-1, keepdims=True)) / ssum
+    dp = np.zeros(probs.shape, dtype=np.float64)
+    np.put_along_axis(dp, idx, dwt, axis=-1)
+    p64 = probs.astype(np.float64)
+    dlogits = p64 * (dp - (p64 * dp).sum(axis=-1, keepdims=True))
+    d_router = dlogits.T @ x64
+    dx += dlogits @ router_w.astype(np.float64)
+    return dx, d_router, dw1, dw2
+
+
+def experts_backward_bf16(x_bits, idx, w, w1_bits, w2_bits, dout_bits):
+    """Routed-expert gradients at the build's rounding points, for a given routing.
+
+    Per (token, slot) with expert e (numpy fp32 matmuls, bf16 where the pipeline
+    stores):  pre = bf16(x W1[e]^T), h = bf16(gelu(x W1[e]^T)), y = bf16(h W2[e]^T);
+    dy = bf16(w * dout); dpre = bf16((dy W2[e]) * gelu'(pre)); dxr = bf16(dpre W1[e]).
+    Returns a dict of
+      ``dx``   bf16 bits [T, H]: the slot sum of dxr in fp32, rounded once;
+      ``dw``   float64 [T, k]:  <dout, y>;
+      ``dw1``  bf16 bits [E, F, H] = sum dpre^T x;  ``dw2`` bf16 bits [E, H, F] = sum dy^T h;
+      ``mag_dx``, ``mag_dw1``, ``mag_dw2``: the sums of absolute terms behind each
+      element, against which summation-order differences are judged.
+    """
+    t_count, hidden = x_bits.shape
+    n_exp, ffn, _ = w1_bits.shape
+    rnd = lambda v: bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(v, dtype=np.float32)))
+    xf, dof = bf16_bits_to_f32(x_bits), bf16_bits_to_f32(dout_bits)
+    dx = np.zeros((t_count, hidden), np.float32)
+    mag_dx = np.zeros_like(dx)
+    dw = np.zeros(idx.shape, np.float64)
+    dw1 = np.zeros((n_exp, ffn, hidden), np.float32)
+    dw2 = np.zeros((n_exp, hidden, ffn), np.float32)
+    mag1, mag2 = np.zeros_like(dw1), np.zeros_like(dw2)
+    for e in range(n_exp):
+        sel = np.argwhere(idx == e)
+        if sel.size == 0:
+            continue
+        toks, slots = sel[:, 0], sel[:, 1]
+        w1f, w2f = bf16_bits_to_f32(w1_bits[e]), bf16_bits_to_f32(w2_bits[e])
+        acc = xf[toks] @ w1f.T
+        pre = rnd(acc)
+        h = rnd(gelu_erf(acc))
+        y = rnd(h @ w2f.T)
+        dw[toks, slots] = (dof[toks].astype(np.float64) * y).sum(axis=1)
+        dy = rnd(w[toks, slots][:, None].astype(np.float32) * dof[toks])
+        dpre = rnd((dy @ w2f) * gelu_erf_grad(pre))
+        dxr = rnd(dpre @ w1f)
+        np.add.at(dx, toks, dxr)
+        np.add.at(mag_dx, toks, np.abs(dxr))
+        dw2[e] = dy.T @ h
+        dw1[e] = dpre.T @ xf[toks]
+        mag2[e] = np.abs(dy).T @ np.abs(h)
+        mag1[e] = np.abs(dpre).T @ np.abs(xf[toks])
+    return dict(dx=f32_to_bf16_bits(dx), dw=dw, dw1=f32_to_bf16_bits(dw1),
+                dw2=f32_to_bf16_bits(dw2), mag_dx=mag_dx, mag_dw1=mag1, mag_dw2=mag2)

@@ -9,6 +9,9 @@ Records, on the CPU in fp32:
   * the single-process routed path (src/train_moe_baseline.py:342-348,
     expert_kernel="torch", no shared experts): router weight, expert weights,
     input, output and router stats;
+  * the gradients torch autograd gives that same path for a seeded output
+    gradient (the reference never runs backward, :524-552, but its local path
+    is differentiable): d input, d router weight, d w1 / d w2 per expert;
   * the torch_a2a expert-parallel path (:269-313, 323-341) of the same model
     sharded over 2 gloo ranks (each rank's output for its own tokens).
 The fixture pins the numpy layer oracle (oracle/moe_layer.py); nothing on the
@@ -75,7 +78,16 @@ def main() -> None:
     with torch.no_grad():
         out, stats = m(x)
     sd = m.state_dict()
+    xg = x.clone().requires_grad_(True)
+    out_g, _ = m(xg)
+    dout = torch.randn(out_g.shape, generator=torch.Generator().manual_seed(77))
+    out_g.backward(dout)
     data = {
+        "dout": dout.numpy(),
+        "dx": xg.grad.numpy(),
+        "d_router_w": m.router.weight.grad.numpy(),
+        "d_w1": np.stack([m.routed_experts[e].w1.weight.grad.numpy() for e in range(E)]),
+        "d_w2": np.stack([m.routed_experts[e].w2.weight.grad.numpy() for e in range(E)]),
         "x": x.numpy(),
         "router_w": sd["router.weight"].numpy(),
         "w1": np.stack([sd[f"routed_experts.{e}.w1.weight"].numpy() for e in range(E)]),

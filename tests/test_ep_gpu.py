@@ -193,3 +193,43 @@ def test_expert_alignment_pads_segments(cuda_device, world, align):
             assert np.array_equal(got, send_pos[r])
     finally:
         grp.close()
+
+
+@pytest.mark.parametrize("world", [1, 4])
+def test_scale_rows_and_topk_weight_grad_match_oracle(cuda_device, world):
+    """scale_rows: received rows are bf16(x * w) bit for bit; topk_weight_grad:
+    <grad_out[t], y(t, j)> within fp32 summation-order rounding."""
+    tokens, topk, hidden, E = 333, 3, 256, 16
+    xs, idxs, ws = routing(world, tokens, E, topk, seed=90 + world, hidden=hidden)
+    grp = LocalGroup(world, E, hidden, tokens, topk, world * tokens * topk + E * 64, num_blocks=6)
+    try:
+        di = [i.to(cuda_device) for i in idxs]
+        dw = [w.to(cuda_device) for w in ws]
+        slot, epoch = grp.dispatch([x.to(cuda_device) for x in xs], di, dw, pad_rows=True,
+                                   expert_alignment=64, scale_rows=True)
+        torch.cuda.synchronize()
+        assert int(grp.status.item()) == 0
+        recv, send_pos = oep.dispatch([to_storage(x) for x in xs], [i.numpy() for i in idxs],
+                                      [w.numpy() for w in ws], E, expert_alignment=64,
+                                      scale_rows=True)
+        ys = []
+        for d, ep in enumerate(grp.eps):
+            v, want = ep.slots[slot], recv[d]
+            n = int(want["offsets"][-1])
+            assert np.array_equal(to_storage(v.recv_x[:n]), want["x"])
+            y = (v.recv_x[:n].float() * 3.0 - 0.5).to(torch.bfloat16)
+            v.expert_out[:n].copy_(y)
+            ys.append(to_storage(y))
+        g = torch.Generator().manual_seed(5)
+        gouts = [torch.randn(tokens, hidden, generator=g).to(torch.bfloat16) for _ in range(world)]
+        want = oep.topk_weight_grad([to_storage(t) for t in gouts], ys, [i.numpy() for i in idxs],
+                                    send_pos, E)
+        for r, ep in enumerate(grp.eps):
+            out = torch.empty(tokens, topk, dtype=torch.float32, device=cuda_device)
+            ep.topk_weight_grad(gouts[r].to(cuda_device), di[r], slot, out, 5)
+            torch.cuda.synchronize()
+            got = out.cpu().numpy().astype(np.float64)
+            np.testing.assert_allclose(got, want[r], rtol=0, atol=2e-4 * np.abs(want[r]).max() + 1e-6)
+            assert np.all(got[send_pos[r] < 0] == 0.0)
+    finally:
+        grp.close()

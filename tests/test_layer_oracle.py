@@ -31,3 +31,10 @@ def test_oracle_router_stats_match_reference():
     probs, idx, _ = ol.route(G["x"], G["router_w"], int(G["top_k"]))
     ent, std, cv = ol.router_stats(probs, idx, G["router_w"].shape[0])
     np.testing.assert_allclose([ent, std, cv], G["stats"], rtol=1e-5, atol=1e-6)
+
+
+def test_oracle_layer_backward_matches_reference_autograd():
+    dx, dr, dw1, dw2 = ol.layer_backward_f32(G["x"], G["router_w"], G["w1"], G["w2"],
+                                             int(G["top_k"]), G["dout"])
+    for got, want in ((dx, G["dx"]), (dr, G["d_router_w"]), (dw1, G["d_w1"]), (dw2, G["d_w2"])):
+        np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-5)
