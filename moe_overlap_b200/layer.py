@@ -82,8 +82,9 @@ class MoELayer:
         self.w1 = torch.zeros(self.experts_per_rank, ffn_size, hidden_size, dtype=bf16, device=dev)
         self.w2 = torch.zeros(self.experts_per_rank, hidden_size, ffn_size, dtype=bf16, device=dev)
         if training and max_recv_rows is None:
-            # worst case of one dispatch plus the alignment padding of every local expert
-            max_recv_rows = (self.world * self.micro * min(2, self.experts_per_rank, top_k)
+            # worst case of one dispatch (every rank sends all its assignments here)
+            # plus the alignment padding of every local expert
+            max_recv_rows = (self.world * self.micro * min(top_k, self.experts_per_rank)
                              + self.experts_per_rank * TRAIN_ALIGNMENT)
         self.dispatcher = DeepEPDispatcher(group, hidden_size, num_experts, num_sms=num_comm_sms,
                                            max_tokens_per_rank=self.micro, max_top_k=top_k,

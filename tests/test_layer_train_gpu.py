@@ -83,7 +83,7 @@ def test_expert_gradients_match_oracle(cuda_device, tokens, hidden, ffn, experts
     x = torch.randn(tokens, hidden, generator=g).to(torch.bfloat16).to(cuda_device)
     _, idx, w = layer.route(x)
     x.requires_grad_(True)
-    w = w.clone().requires_grad_(True)
+    w = w.detach().clone().requires_grad_(True)
     out = RoutedExperts.apply(x, w, layer.w1, layer.w2, idx, layer)
     dout = torch.randn(tokens, hidden, generator=g).to(torch.bfloat16).to(cuda_device)
     out.backward(dout)
