@@ -63,6 +63,10 @@ LAYER_WORKLOADS = {
                       zipf_bias=False,
                       desc="BASELINE config 4 forward: MoE layer on one GPU, batch 8 x seq 2048, "
                            "H=2048, FFN 4H, 16 experts, renormalised top-2"),
+    "layer_train": dict(tokens=8 * 2048, hidden=2048, ffn=8192, experts=16, top_k=2, renorm=True,
+                        zipf_bias=False,
+                        desc="BASELINE config 4: MoE layer forward + backward on one GPU, batch 8 x "
+                             "seq 2048, H=2048, FFN 4H, 16 experts, renormalised top-2"),
 }
 
 
@@ -470,6 +474,162 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 4: tokens/s of one MoE-layer forward + backward (router, experts, exchange).
+
+    A step is forward_autograd + backward of a fixed dout on the resident batch,
+    producing dx and the router, W1 and W2 gradients (gradients are reset to None
+    first, so there is no accumulation kernel).  With N ranks each runs its own
+    replica of the layer on its own batch (config 4 is a one-GPU layer), so
+    ``value`` is N x tokens / step.
+    """
+    import torch
+    import torch.distributed as dist
+
+    import moe_overlap_b200 as mo
+    from moe_overlap_b200.layer import MoELayer
+
+    cfg = LAYER_WORKLOADS[args.workload]
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
+    T, H, Fd, E, K = cfg["tokens"], cfg["hidden"], cfg["ffn"], cfg["experts"], cfg["top_k"]
+    layer = MoELayer(H, Fd, E, K, renormalize=cfg["renorm"], num_comm_sms=args.comm_sms,
+                     micro_batch_size=T, training=True).init_random(std=0.02, seed=0)
+    params = (layer.router_w, layer.w1, layer.w2)
+    for p in params:
+        p.requires_grad_(True)
+    g = torch.Generator().manual_seed(1000 + rank)
+    x_host = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    dout_host = (torch.randn(T, H, generator=g) * 1e-2).to(torch.bfloat16)
+    x = x_host.to(device).requires_grad_(True)
+    dout = dout_host.to(device)
+
+    def step(xin, gout):
+        for p in params:
+            p.grad = None
+        xin.grad = None
+        out, probs, idx = layer.forward_autograd(xin)
+        out.backward(gout)
+        return probs, idx
+
+    for _ in range(max(3, args.warmup)):
+        step(x, dout)
+    torch.cuda.synchronize(device)
+    mo.check_status(device, sync=True)
+
+    sampler = ClockSampler(device)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        probs, idx = step(x, dout)
+    end.record()
+    torch.cuda.synchronize(device)
+    clocks = sampler.stop()
+    mo.check_status(device, sync=True)
+    step_ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([step_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+
+    # Per-phase device times of one more step (phase boundaries on the compute stream).
+    def mark(name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        layer.trace.append((name, ev))
+
+    layer.trace = []
+    mark("step_start")
+    step(x, dout)
+    mark("router_bwd")
+    torch.cuda.synchronize(device)
+    marks, layer.trace = layer.trace, None
+    phases = {}
+    for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
+        phases["router_fwd" if name == "start" else name] = round(a.elapsed_time(b), 4)
+
+    stats = layer.stats(probs, idx)
+    rows = T * K
+    expert_flops = 12.0 * rows * H * Fd  # 2 forward + 2 dgrad + 2 wgrad GEMMs of 2*rows*H*F each
+    tflops = expert_flops / (step_ms / 1e3) / 1e12
+
+    e2e = None
+    if not args.no_e2e:
+        # Through the public API from pinned host memory: copy the batch and the
+        # output gradient in, run the step, read the expert-load counts back.
+        xh, gh = x_host.pin_memory(), dout_host.pin_memory()
+        counts_h = torch.empty(E, dtype=torch.int64).pin_memory()
+        n_e2e = max(3, args.steps // 2)
+        xd = torch.empty_like(x.detach())
+        gd = torch.empty_like(dout)
+        torch.cuda.synchronize(device)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(n_e2e):
+            xd.copy_(xh, non_blocking=True)
+            gd.copy_(gh, non_blocking=True)
+            xd.requires_grad_(True)
+            _, idx_e = step(xd, gd)
+            counts_h.copy_(torch.bincount(idx_e.reshape(-1), minlength=E), non_blocking=True)
+            xd = xd.detach()
+        e2.record()
+        torch.cuda.synchronize(device)
+        e2e_ms = s2.elapsed_time(e2) / n_e2e
+        te = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(world * T / (float(te.item()) / 1e3), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": 2 * T * H * 2, "d2h_bytes_per_step": E * 8,
+               "ms_per_step": round(float(te.item()), 4)}
+
+    peak_burst, peak_src = load_peaks()
+    peak = peak_burst
+    try:
+        peak = float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"])
+        peak_src = "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    except Exception:
+        pass
+    if rank == 0:
+        line = {
+            "metric": "MoE-layer tokens/s",
+            "value": round(world * T / (step_ms / 1e3), 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
+            "config": {"workload": args.workload, "description": cfg["desc"], "tokens_per_rank": T,
+                       "comm_sms": args.comm_sms, "l2": "working set (weights 1 GiB, activations) > L2",
+                       "parallelism": "replicas" if world > 1 else "single"},
+            "expert_load_cv": round(stats.load_cv, 4),
+            "router_entropy": round(stats.entropy, 4),
+            "roofline": {"bound": "tensor", "scope": "whole step, expert GEMM FLOPs only",
+                         "achieved": round(tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_source": peak_src, "traffic": None},
+            "phase_ms": phases,
+            "e2e": e2e,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -477,6 +637,9 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "layer_train":
+        run_layer_train(args, rank, world, local_rank)
         return
     if args.workload in LAYER_WORKLOADS:
         run_layer(args, rank, world, local_rank)

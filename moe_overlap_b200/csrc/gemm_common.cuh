@@ -74,28 +74,56 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const v
   return __all_sync(0xffffffffu, ok);
 }
 
-// Epilogue of one 128-row x 256-column fp32 accumulator held in TMEM lanes
-// [32*quad, 32*quad+32) of this warp, for rows [0, rows) of the tile starting at
-// global row `row0`, columns n0.. (< n): v = acc (* row_scale), optionally saved
-// to aux_out, then C = act(v) with act none, GELU or v * gelu'(aux_in), rounded
-// and written with 16-byte stores.
+// Epilogue of one 128-row fp32 accumulator held in TMEM lanes [32*quad, 32*quad+32)
+// of this warp: the 32-column chunks [ch0, ch0 + nch) of the tile, for rows
+// [0, rows) of the tile starting at global row `row0`, columns n0.. (< n).
+// v = acc (* row_scale), optionally saved to aux_out, then C = act(v) with act
+// none, GELU or v * gelu'(aux_in), rounded and written with 16-byte stores.
+// aux_in for chunk c+1 is loaded while chunk c is computed, so the epilogue of
+// the backward GEMM does not wait a full memory latency per chunk.
 template <bool BF16>
 __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int lane, int row0,
-                                                  int rows, int n0, const Params& p) {
+                                                  int rows, int n0, const Params& p, int ch0 = 0,
+                                                  int nch = 8) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int row_in_tile = quad * 32 + lane;
   const bool row_ok = row_in_tile < rows;
   const int64_t grow = int64_t(row0) + row_in_tile;
   T* crow = reinterpret_cast<T*>(p.c) + grow * p.ldc;
   const float rs = (p.row_scale != nullptr && row_ok) ? p.row_scale[grow] : 1.0f;
+  const bool dgelu = p.activation == MOE_ACT_DGELU;
+  const T* arow = dgelu ? reinterpret_cast<const T*>(p.aux_in) + grow * p.ld_aux : nullptr;
+  // 16-byte vectors of chunk c that lie inside the matrix (0 when the row or chunk is outside).
+  auto vecs = [&](int c) {
+    const int col = n0 + c * 32;
+    return (row_ok && col < p.n) ? min(4, (p.n - col) / 8) : 0;
+  };
+  uint4 anext[4] = {};
+  if (dgelu) {
+    const int nv = vecs(ch0);
+    const uint4* ai = reinterpret_cast<const uint4*>(arow + n0 + ch0 * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (q < nv) anext[q] = ai[q];
+  }
 #pragma unroll 1
-  for (int ch = 0; ch < 256 / 32; ++ch) {
+  for (int ch = ch0; ch < ch0 + nch; ++ch) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_base + ch * 32, r);
+    uint4 acur[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acur[q] = anext[q];
+    if (dgelu && ch + 1 < ch0 + nch) {
+      const int nv = vecs(ch + 1);
+      const uint4* ai = reinterpret_cast<const uint4*>(arow + n0 + (ch + 1) * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (q < nv) anext[q] = ai[q];
+    }
     tmem_wait_ld();
     const int col = n0 + ch * 32;
-    if (row_ok && col < p.n) {
-      const int nvec = min(4, (p.n - col) / 8);  // 16-byte vectors inside the matrix
+    const int nvec = vecs(ch);  // 16-byte vectors inside the matrix
+    if (nvec > 0) {
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
@@ -111,14 +139,11 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
       if (p.activation == MOE_ACT_GELU) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-      } else if (p.activation == MOE_ACT_DGELU) {
-        const uint4* ai =
-            reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux_in) + grow * p.ld_aux + col);
+      } else if (dgelu) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           if (q < nvec) {
-            const uint4 a = ai[q];
-            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+            const uint32_t w[4] = {acur[q].x, acur[q].y, acur[q].z, acur[q].w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
               const float2 f = unpack2<BF16>(w[h]);

@@ -9,7 +9,7 @@
 // tensor work), so six stages fit in shared memory, and each CTA receives its
 // 128 rows of the accumulator in its own TMEM.
 //
-// Roles per CTA (192 threads):
+// Roles per CTA (320 threads):
 //   warp 0   producer.  Leader: takes the next tile (striped over the pairs, or
 //            from the global atomic counter), posts it to both CTAs' tile rings,
 //            loads its halves.  Follower: reads the posted tile, loads its halves.
@@ -17,7 +17,10 @@
 //   warp 1   TMEM (both CTAs allocate the pair's 512 columns); in the leader it
 //            also issues the MMAs and commits stage/accumulator completion to the
 //            barriers of both CTAs.
-//   warps 2-5 epilogue of this CTA's 128 rows (see store_accumulator).
+//   warps 2-9 epilogue of this CTA's 128 rows (see store_accumulator): warp w
+//            reads TMEM lanes 32*(w%4).. (the lanes its warp slot may access) and
+//            columns 128*((w-2)/4).. of the tile, so two warps share each lane
+//            quadrant and every SM sub-partition runs two epilogue warps.
 // No load uses cluster multicast; the pair exchanges only barrier arrivals and
 // the tile ring entries through shared::cluster addresses.
 #include <algorithm>
@@ -40,8 +43,8 @@ constexpr int BK = 64;
 constexpr int UMMA_K = 16;
 constexpr int STAGES = 6;
 constexpr int QDEPTH = 8;
-constexpr int NUM_THREADS = 192;
-constexpr int NUM_EPI_WARPS = 4;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int A_STAGE_BYTES = BM_CTA * BK * 2;  // 16 KiB
 constexpr int B_STAGE_BYTES = BK * BN_CTA * 2;  // 16 KiB
 constexpr int B_SLAB_BYTES = BK * 64 * 2;       // one 64-column slab of an N-major B stage
@@ -287,6 +290,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue --
     const int quad = warp & 3;
+    const int col_half = (warp - 2) >> 2;  // 0 or 1: which 128 columns of the tile
     int q = 0;
     uint32_t qphase = 0;
     int acc = 0;
@@ -314,7 +318,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int rows_here = min(int(BM_CTA), max(0, s.y - static_cast<int>(crank) * int(BM_CTA)));
       store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
-                              lane, s.x + static_cast<int>(crank) * BM_CTA, rows_here, s.z, p);
+                              lane, s.x + static_cast<int>(crank) * BM_CTA, rows_here, s.z, p,
+                              col_half * 4, 4);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->tempty[acc]), 0));

@@ -174,7 +174,7 @@ class DeepEPDispatcher:
     def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
                  previous_event: Optional[object] = None, *,
                  exact_size: Optional[bool] = None, expert_alignment: int = 1,
-                 scale_rows: bool = False) -> DispatchResult:
+                 scale_rows: bool = False, num_sms: Optional[int] = None) -> DispatchResult:
         if x.dtype != torch.bfloat16:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
@@ -199,7 +199,7 @@ class DeepEPDispatcher:
             wc = topk_weights.to(torch.float32).contiguous()
             if xc.data_ptr() % 16 != 0:
                 xc = xc.clone()
-            self._ep.dispatch(xc, ic, wc, slot, epoch, self.num_sms, not exact, self.wait_ns,
+            self._ep.dispatch(xc, ic, wc, slot, epoch, num_sms or self.num_sms, not exact, self.wait_ns,
                               self._status, expert_alignment, scale_rows)
             offs = self._ep.slots[slot].expert_offsets
             per_expert = offs[1:] - offs[:-1]
@@ -232,7 +232,8 @@ class DeepEPDispatcher:
         if self._epoch - handle.epoch >= 2:
             raise RuntimeError("the dispatch's exchange slot has been reused by a later dispatch")
 
-    def topk_weight_grad(self, grad_out: torch.Tensor, handle: DispatchHandle) -> torch.Tensor:
+    def topk_weight_grad(self, grad_out: torch.Tensor, handle: DispatchHandle,
+                         num_sms: Optional[int] = None) -> torch.Tensor:
         """d loss / d topk_weights of a combined dispatch: <grad_out[t], y(t, j)> (float32 [T, k]).
 
         Reads the expert outputs that ``handle``'s combine summed, so call it before
@@ -243,7 +244,7 @@ class DeepEPDispatcher:
             raise ValueError(f"grad_out must be [{handle.num_tokens}, {self.hidden_size}]")
         out = torch.empty(handle.num_tokens, handle.topk, dtype=torch.float32, device=self.device)
         g = grad_out.to(torch.bfloat16).contiguous()
-        self._ep.topk_weight_grad(g, handle.topk_idx, handle.slot, out, 2 * self.num_sms)
+        self._ep.topk_weight_grad(g, handle.topk_idx, handle.slot, out, 2 * (num_sms or self.num_sms))
         return out
 
     def expert_out_buffer(self, handle: DispatchHandle) -> torch.Tensor:
@@ -254,7 +255,8 @@ class DeepEPDispatcher:
     def combine(self, expert_out: torch.Tensor, handle: DispatchHandle,
                 previous_event: Optional[object] = None, *,
                 weighted: bool = False,
-                out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, object]:
+                out: Optional[torch.Tensor] = None,
+                num_sms: Optional[int] = None) -> Tuple[torch.Tensor, object]:
         if not isinstance(handle, DispatchHandle) or handle.combined:
             raise RuntimeError("combine needs the handle of an outstanding dispatch")
         if expert_out.dtype != torch.bfloat16 or expert_out.dim() != 2 or \
@@ -278,7 +280,7 @@ class DeepEPDispatcher:
                     raise ValueError("expert_out has more rows than the receive buffer")
                 views.expert_out[:rows].copy_(expert_out)
             self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot, handle.epoch,
-                             weighted, out, self.num_sms, self.wait_ns, self._status)
+                             weighted, out, num_sms or self.num_sms, self.wait_ns, self._status)
             event = torch.cuda.Event()
             event.record(self.comm_stream)
         expert_out.record_stream(self.comm_stream)

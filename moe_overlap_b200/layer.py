@@ -93,6 +93,9 @@ class MoELayer:
         self.gemm_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self.h = torch.empty(self.dispatcher.max_recv_rows, ffn_size, dtype=bf16, device=dev)
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        # When a list, the training path appends (phase, event) pairs recorded on
+        # the compute stream at each phase boundary (for per-phase device times).
+        self.trace: Optional[list] = None
 
     # ----------------------------------------------------------------- weights --
     def init_random(self, std: float = 0.02, seed: int = 0) -> "MoELayer":
@@ -216,7 +219,7 @@ class MoELayer:
             dist.all_reduce(counts, group=self.group)
         mean = counts.mean().clamp_min(1e-6)
         entropy = (-probs * probs.clamp_min(1e-9).log()).sum(dim=-1).mean()
-        return RouterStats(float(entropy), float(counts.std()), float(counts.std() / mean))
+        return RouterStats(float(entropy.detach()), float(counts.std()), float(counts.std() / mean))
 
     # ---------------------------------------------------------------- training --
     def forward_autograd(self, x: torch.Tensor):
@@ -228,7 +231,9 @@ class MoELayer:
         weighted combine; backward: top-k weight gradient, weighted dispatch of the
         output gradient, dgrad GEMMs with GELU' fused, combine, weight-gradient
         GEMMs).  ``router_w``, ``w1`` and ``w2`` receive ``.grad`` when they
-        require it.  The whole batch is one chunk (micro_batch_size must cover it).
+        require it.  The whole batch is one chunk (micro_batch_size must cover it),
+        and nothing runs beside the exchange kernels in this path (each phase waits
+        for the one before), so they get a grid of one block per SM.
         """
         logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t()).float()
         if self.router_b is not None:
@@ -240,23 +245,35 @@ class MoELayer:
         out = RoutedExperts.apply(x, w, self.w1, self.w2, idx.to(torch.int64), self)
         return out, probs, idx
 
+    def _mark(self, phase: str) -> None:
+        if self.trace is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.trace.append((phase, ev))
+
     def _train_forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor):
         disp = self.dispatcher
+        self._mark("start")
         if x.shape[0] > self.micro:
             raise ValueError("training forward runs the batch as one chunk: raise micro_batch_size")
         x = x.to(torch.bfloat16).contiguous()
-        res = disp.dispatch(x, idx, w.float(), exact_size=False, expert_alignment=TRAIN_ALIGNMENT)
+        res = disp.dispatch(x, idx, w.float(), exact_size=False, expert_alignment=TRAIN_ALIGNMENT,
+                            num_sms=self.gemm_sms)
         res.event.current_stream_wait()
+        self._mark("fwd_dispatch")
         rows = res.recv_x.shape[0]
         pre = torch.empty(rows, self.ffn, dtype=torch.bfloat16, device=self.device)
         h = torch.empty_like(pre)
         kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
         grouped_gemm(res.recv_x, self.w1.detach().transpose(1, 2), res.expert_offsets, out=h,
                      activation="gelu", aux_out=pre, **kw)
+        self._mark("fwd_gemm1")
         y = disp.expert_out_buffer(res.handle)
         grouped_gemm(h, self.w2.detach().transpose(1, 2), res.expert_offsets, out=y, **kw)
-        out, ev = disp.combine(y, res.handle, weighted=True)
+        self._mark("fwd_gemm2")
+        out, ev = disp.combine(y, res.handle, weighted=True, num_sms=self.gemm_sms)
         ev.current_stream_wait()
+        self._mark("fwd_combine")
         return out, dict(res=res, pre=pre, h=h, idx=idx, w=w.float())
 
     def _train_backward(self, state: dict, dout: torch.Tensor):
@@ -267,24 +284,33 @@ class MoELayer:
             # dispatch may run in between.
             raise RuntimeError("another dispatch ran on this layer between its forward and backward; "
                                "run backward before the layer's next forward")
+        self._mark("bwd_start")
         dout = dout.to(torch.bfloat16).contiguous()
         kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
         # d/d topk weight: <dout[t], y(t, j)>, read from the forward's expert outputs.
-        dw = disp.topk_weight_grad(dout, res.handle)
+        dw = disp.topk_weight_grad(dout, res.handle, num_sms=self.gemm_sms)
+        self._mark("bwd_topk_weight_grad")
         # The output gradient goes back to the experts weighted: dY = w * dout rows,
         # laid out exactly like the forward rows (same routing and alignment).
         rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False,
-                           expert_alignment=TRAIN_ALIGNMENT, scale_rows=True)
+                           expert_alignment=TRAIN_ALIGNMENT, scale_rows=True, num_sms=self.gemm_sms)
         rb.event.current_stream_wait()
+        self._mark("bwd_dispatch")
         d_pre = torch.empty_like(state["pre"])
         grouped_gemm(rb.recv_x, self.w2.detach(), rb.expert_offsets, out=d_pre, activation="dgelu",
                      aux_in=state["pre"], **kw)
+        self._mark("bwd_dgrad2")
         dx_rows = disp.expert_out_buffer(rb.handle)
         grouped_gemm(d_pre, self.w1.detach(), rb.expert_offsets, out=dx_rows, **kw)
+        self._mark("bwd_dgrad1")
+        # The combine of dx runs on the exchange stream under the weight gradients.
         dx, ev = disp.combine(dx_rows, rb.handle, weighted=False)
         dw2 = grouped_gemm_wgrad(rb.recv_x, state["h"], rb.expert_offsets, num_sms=self.gemm_sms)
+        self._mark("bwd_wgrad2")
         dw1 = grouped_gemm_wgrad(d_pre, res.recv_x, rb.expert_offsets, num_sms=self.gemm_sms)
+        self._mark("bwd_wgrad1")
         ev.current_stream_wait()
+        self._mark("bwd_combine_tail")
         return dx, dw, dw1, dw2
 
     def close(self) -> None:
