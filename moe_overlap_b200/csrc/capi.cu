@@ -46,7 +46,8 @@ int current_device_info(int* dev, DeviceInfo* info) {
 }
 
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
-                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -67,7 +68,7 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void*
     if (i + 1 < rank) s[i] = strides_bytes[i];
   }
   const CUresult r = g_encode(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d,
-                              s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MOE_OK : MOE_ERR_INVALID_ARG;

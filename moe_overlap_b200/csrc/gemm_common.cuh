@@ -34,6 +34,7 @@ struct Params {
   const void* aux_in;      // MOE_ACT_DGELU: C = v * gelu'(aux_in[row, col])
   void* aux_out;           // aux_out[row, col] = v (before the activation)
   int64_t ld_aux;
+  int c_tma;               // the CTA-pair kernel may store C through its TMA store map
 };
 
 __device__ __forceinline__ float gelu_erf(float x) {
@@ -81,10 +82,21 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const v
 // none, GELU or v * gelu'(aux_in), rounded and written with 16-byte stores.
 // aux_in for chunk c+1 is loaded while chunk c is computed, so the epilogue of
 // the backward GEMM does not wait a full memory latency per chunk.
+//
+// With `tmap_c` (a 2-D {N, rows} or, when e3 >= 0, 3-D {N, rows, E} tensor map of C
+// with 32x32 boxes and 64-byte swizzle) a warp whose 32 rows may all be written
+// stages each bf16 chunk in its 2 KiB of shared memory at `stage` and stores it with
+// one TMA bulk store instead of 32 scattered 16-byte stores per instruction.  A warp
+// may use it when all its rows belong to the tile (rows >= 32*quad + 32) or, with
+// `rows_clipped_by_map`, when the map's row extent is the tile's own bound (rows past
+// it are dropped by the TMA unit).  Other warps store directly.  The caller drains
+// its bulk stores (bulk_wait_group0) before the CTA exits.
 template <bool BF16>
 __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int lane, int row0,
                                                   int rows, int n0, const Params& p, int ch0 = 0,
-                                                  int nch = 8) {
+                                                  int nch = 8, const void* tmap_c = nullptr,
+                                                  uint32_t stage = 0, bool rows_clipped_by_map = false,
+                                                  int e3 = -1) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int row_in_tile = quad * 32 + lane;
   const bool row_ok = row_in_tile < rows;
@@ -123,11 +135,13 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
     tmem_wait_ld();
     const int col = n0 + ch * 32;
     const int nvec = vecs(ch);  // 16-byte vectors inside the matrix
-    if (nvec > 0) {
+    const bool tma = tmap_c != nullptr && col < p.n &&
+                     (rows_clipped_by_map ? quad * 32 < rows : quad * 32 + 32 <= rows);  // warp-uniform
+    if (tma || nvec > 0) {
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
-      if (p.aux_out != nullptr) {
+      if (p.aux_out != nullptr && nvec > 0) {
         uint4* ad = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.aux_out) + grow * p.ld_aux + col);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
@@ -153,13 +167,33 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
           }
         }
       }
-      uint4* dst = reinterpret_cast<uint4*>(crow + col);
+      if (tma) {
+        if (lane == 0) bulk_wait_group_read0();  // the previous chunk's store has read the buffer
+        __syncwarp();
+        // Row `lane` is 64 bytes; 16-byte unit q sits at unit q ^ ((lane >> 1) & 3) (64-byte swizzle).
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (q < nvec)
-          dst[q] = make_uint4(pack2<BF16>(v[8 * q], v[8 * q + 1]), pack2<BF16>(v[8 * q + 2], v[8 * q + 3]),
-                              pack2<BF16>(v[8 * q + 4], v[8 * q + 5]),
-                              pack2<BF16>(v[8 * q + 6], v[8 * q + 7]));
+        for (int q = 0; q < 4; ++q)
+          st_shared_v4(stage + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4), pack2<BF16>(v[8 * q], v[8 * q + 1]),
+                       pack2<BF16>(v[8 * q + 2], v[8 * q + 3]), pack2<BF16>(v[8 * q + 4], v[8 * q + 5]),
+                       pack2<BF16>(v[8 * q + 6], v[8 * q + 7]));
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (e3 >= 0)
+            tma_store_3d(tmap_c, stage, col, row0 + quad * 32, e3);
+          else
+            tma_store_2d(tmap_c, stage, col, row0 + quad * 32);
+          bulk_commit_group();
+        }
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (q < nvec)
+            dst[q] = make_uint4(pack2<BF16>(v[8 * q], v[8 * q + 1]), pack2<BF16>(v[8 * q + 2], v[8 * q + 3]),
+                                pack2<BF16>(v[8 * q + 4], v[8 * q + 5]),
+                                pack2<BF16>(v[8 * q + 6], v[8 * q + 7]));
+      }
     }
   }
 }
@@ -177,9 +211,11 @@ __device__ __forceinline__ void zero_output(const Params& p, int nthreads) {
   }
 }
 
-// Launches the 2-SM (CTA pair) kernel; grid must be even.  Returns a MOE_* code.
+// Launches the 2-SM (CTA pair) kernel; grid must be even.  `tc` is the 2-D {N, m_total}
+// store map of C (32x32 boxes, 64-byte swizzle), used when p.c_tma is set.
+// Returns a MOE_* code.
 int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                       const Params& p, int grid, cudaStream_t stream);
+                       const CUtensorMap& tc, const Params& p, int grid, cudaStream_t stream);
 
 }  // namespace gg
 }  // namespace moe

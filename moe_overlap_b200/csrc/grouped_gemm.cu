@@ -26,6 +26,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
 #include <cstdlib>
 #include <mutex>
 
@@ -331,6 +332,16 @@ static int gemm_kernel_choice() {
   return v;
 }
 
+// MOE_B200_GEMM_TMA_STORE=0 makes the pair kernel write C with direct 16-byte
+// stores instead of staged TMA bulk stores (default 1).
+static bool gemm_tma_store() {
+  static const bool v = [] {
+    const char* e = std::getenv("MOE_B200_GEMM_TMA_STORE");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return v;
+}
+
 // Tile walk order: 0 (default) = the reference's expert, tile_m, tile_n fastest
 // (measured ~1 % faster on BASELINE configs 2/3 than 1 = expert, tile_n, tile_m
 // fastest).  MOE_B200_GEMM_ORDER overrides.
@@ -462,11 +473,24 @@ extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b
   p.aux_out = aux_out;
   p.ld_aux = ld_aux;
 
+  // The pair kernel stores C through a {N, m_total} map in 32x32 boxes (64-byte swizzle).
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  p.c_tma = 0;
+  if (use_pair && gemm_tma_store()) {
+    const uint64_t dims[2] = {uint64_t(n), uint64_t(m_total)};
+    const uint64_t strides[1] = {uint64_t(ldc) * 2};
+    const uint32_t box[2] = {32, 32};
+    if (int rc = encode_tiled(&tc, dt, 2, c, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B); rc != MOE_OK)
+      return rc;
+    p.c_tma = 1;
+  }
+
   if (p.use_atomic &&
       cudaMemsetAsync(work_counter, 0, sizeof(int32_t), stream) != cudaSuccess)
     return MOE_ERR_CUDA;
   const bool bf16 = dtype == MOE_DTYPE_BF16;
-  if (use_pair) return launch_pair_kernel(bf16, b_mn, ta, tb, p, grid, stream);
+  if (use_pair) return launch_pair_kernel(bf16, b_mn, ta, tb, tc, p, grid, stream);
   if (bf16 && b_mn) return launch<true, true>(ta, tb, p, grid, stream);
   if (bf16 && !b_mn) return launch<true, false>(ta, tb, p, grid, stream);
   if (!bf16 && b_mn) return launch<false, true>(ta, tb, p, grid, stream);

@@ -20,7 +20,9 @@
 //   warps 2-9 epilogue of this CTA's 128 rows (see store_accumulator): warp w
 //            reads TMEM lanes 32*(w%4).. (the lanes its warp slot may access) and
 //            columns 128*((w-2)/4).. of the tile, so two warps share each lane
-//            quadrant and every SM sub-partition runs two epilogue warps.
+//            quadrant and every SM sub-partition runs two epilogue warps.  Each
+//            warp stages 32x32 bf16 chunks in its own 2 KiB of shared memory and
+//            writes them with TMA bulk stores (rows inside the tile's expert only).
 // No load uses cluster multicast; the pair exchanges only barrier arrivals and
 // the tile ring entries through shared::cluster addresses.
 #include <algorithm>
@@ -49,6 +51,7 @@ constexpr int A_STAGE_BYTES = BM_CTA * BK * 2;  // 16 KiB
 constexpr int B_STAGE_BYTES = BK * BN_CTA * 2;  // 16 KiB
 constexpr int B_SLAB_BYTES = BK * 64 * 2;       // one 64-column slab of an N-major B stage
 constexpr uint32_t PAIR_TX_BYTES = 2 * (A_STAGE_BYTES + B_STAGE_BYTES);
+constexpr int EPI_STAGE_BYTES = 32 * 32 * 2;  // one 32x32 bf16 chunk per epilogue warp
 constexpr uint32_t TMEM_COLS = 2 * BN;
 
 struct Ctrl {
@@ -65,20 +68,22 @@ struct Ctrl {
 };
 
 __host__ __device__ constexpr size_t smem_bytes(int num_experts) {
-  return 1024 + size_t(STAGES) * (A_STAGE_BYTES + B_STAGE_BYTES) + ((sizeof(Ctrl) + 15) / 16) * 16 +
-         size_t(3) * 4 * (num_experts + 1);
+  return 1024 + size_t(STAGES) * (A_STAGE_BYTES + B_STAGE_BYTES) + size_t(NUM_EPI_WARPS) * EPI_STAGE_BYTES +
+         ((sizeof(Ctrl) + 15) / 16) * 16 + size_t(3) * 4 * (num_experts + 1);
 }
 
 template <bool BF16, bool B_MN_MAJOR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                             const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+                             const __grid_constant__ CUtensorMap tmap_b,
+                             const __grid_constant__ CUtensorMap tmap_c, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  Ctrl* ctrl = reinterpret_cast<Ctrl*>(sB + STAGES * B_STAGE_BYTES);
+  uint8_t* sEpi = sB + STAGES * B_STAGE_BYTES;  // 1024-aligned, EPI_STAGE_BYTES per epilogue warp
+  Ctrl* ctrl = reinterpret_cast<Ctrl*>(sEpi + NUM_EPI_WARPS * EPI_STAGE_BYTES);
   int* tile_prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ctrl) +
                                             ((sizeof(Ctrl) + 15) / 16) * 16);
   int* seg_start = tile_prefix + (p.num_experts + 1);
@@ -319,7 +324,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int rows_here = min(int(BM_CTA), max(0, s.y - static_cast<int>(crank) * int(BM_CTA)));
       store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
                               lane, s.x + static_cast<int>(crank) * BM_CTA, rows_here, s.z, p,
-                              col_half * 4, 4);
+                              col_half * 4, 4, p.c_tma ? &tmap_c : nullptr,
+                              smem_u32(sEpi + (warp - 2) * EPI_STAGE_BYTES));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->tempty[acc]), 0));
@@ -332,6 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       record_status(p.status, MOE_ERR_TIMEOUT);
       *abort_flag = 1;
     }
+    if (lane == 0) bulk_wait_group0();  // this warp's C stores are complete before the CTA exits
   }
 
   tc_fence_before();
@@ -345,8 +352,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 }
 
 template <bool BF16, bool B_MN>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
-           cudaStream_t stream) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
+           int grid, cudaStream_t stream) {
   auto kern = grouped_gemm_pair_kernel<BF16, B_MN>;
   static std::once_flag once[kMaxDevices];
   int dev = 0;
@@ -357,19 +364,19 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int gr
                                     static_cast<int>(smem_bytes(kMaxExperts)));
   });
   if (attr_err != cudaSuccess) return MOE_ERR_CUDA;
-  kern<<<grid, NUM_THREADS, smem_bytes(p.num_experts), stream>>>(ta, tb, p);
+  kern<<<grid, NUM_THREADS, smem_bytes(p.num_experts), stream>>>(ta, tb, tc, p);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
 }  // namespace pair
 
 int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                       const Params& p, int grid, cudaStream_t stream) {
+                       const CUtensorMap& tc, const Params& p, int grid, cudaStream_t stream) {
   if (grid < 2 || grid % 2 != 0) return MOE_ERR_INVALID_ARG;
-  if (bf16 && b_mn) return pair::launch<true, true>(ta, tb, p, grid, stream);
-  if (bf16 && !b_mn) return pair::launch<true, false>(ta, tb, p, grid, stream);
-  if (!bf16 && b_mn) return pair::launch<false, true>(ta, tb, p, grid, stream);
-  return pair::launch<false, false>(ta, tb, p, grid, stream);
+  if (bf16 && b_mn) return pair::launch<true, true>(ta, tb, tc, p, grid, stream);
+  if (bf16 && !b_mn) return pair::launch<true, false>(ta, tb, tc, p, grid, stream);
+  if (!bf16 && b_mn) return pair::launch<false, true>(ta, tb, tc, p, grid, stream);
+  return pair::launch<false, false>(ta, tb, tc, p, grid, stream);
 }
 
 }  // namespace gg

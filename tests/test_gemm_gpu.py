@@ -194,8 +194,10 @@ def test_epilogue_row_scale_aux_out_and_dgelu(cuda_device):
     assert_matches_oracle(c2, want2, defined, "bf16")
 
 
-@pytest.mark.parametrize("m,n", [(256, 512), (192, 136)])
-def test_wgrad_matches_oracle(cuda_device, m, n):
+@pytest.mark.parametrize("m,n,num_sms", [(256, 512, 148), (192, 136, 148), (192, 136, 1),
+                                         (384, 264, 7), (256, 512, 1)])
+def test_wgrad_matches_oracle(cuda_device, m, n, num_sms):
+    """num_sms >= 2 runs the CTA-pair kernel (7 -> 3 pairs), 1 the 1-SM kernel."""
     counts = [128, 0, 64, 384, 192]  # 64-row aligned segments, one empty expert
     g = torch.Generator().manual_seed(m + n)
     rows = sum(counts)
@@ -208,7 +210,7 @@ def test_wgrad_matches_oracle(cuda_device, m, n):
     da, db, doff = a.to(cuda_device), b.to(cuda_device), off.to(cuda_device)
     rc = lib.moe_grouped_gemm_wgrad(da.data_ptr(), m, db.data_ptr(), n, c.data_ptr(), n, m * n,
                                     doff.data_ptr(), 0, rows, m, n, len(counts),
-                                    _lib.MOE_DTYPE_BF16, 148, status.data_ptr(),
+                                    _lib.MOE_DTYPE_BF16, num_sms, status.data_ptr(),
                                     torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     torch.cuda.synchronize()
