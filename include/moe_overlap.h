@@ -47,6 +47,8 @@ extern "C" {
 #define MOE_ACT_NONE 0
 #define MOE_ACT_GELU 1  /* exact GELU, 0.5*x*(1+erf(x/sqrt(2))), on the fp32 accumulator */
 #define MOE_ACT_DGELU 2 /* acc * gelu'(aux_in): the GELU backward fused into a dgrad GEMM  */
+#define MOE_ACT_GELU_SAVE_GRAD 3 /* GELU(acc); aux_out receives gelu'(acc) instead of acc      */
+#define MOE_ACT_MUL_AUX 4        /* acc * aux_in: the backward against a saved gelu'           */
 
 /* Human-readable text for a status code (static storage). */
 MOE_API const char* moe_status_string(int32_t code);
@@ -104,6 +106,10 @@ MOE_API int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int6
  *   aux_in     m_total x n (row stride ld_aux), dtype: with activation
  *              MOE_ACT_DGELU the result is v * gelu'(aux_in), the GELU backward
  *              fused into a dgrad GEMM
+ * Two more activations split that work between the passes: MOE_ACT_GELU_SAVE_GRAD
+ * writes C = GELU(v) and aux_out = gelu'(v) (required), both from one erf of v, and
+ * MOE_ACT_MUL_AUX writes C = v * aux_in (required), so the backward epilogue
+ * multiplies instead of evaluating erf and exp again.
  * then C = act(v) as in moe_grouped_gemm.  No counterpart in the reference, which
  * runs inference only (src/train_moe_baseline.py:524-552); these serve the
  * forward-with-saved-activations and backward of the routed experts.

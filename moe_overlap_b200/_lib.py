@@ -35,6 +35,8 @@ MOE_DTYPE_F16 = 1
 MOE_ACT_NONE = 0
 MOE_ACT_GELU = 1
 MOE_ACT_DGELU = 2
+MOE_ACT_GELU_SAVE_GRAD = 3
+MOE_ACT_MUL_AUX = 4
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32

@@ -103,7 +103,9 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
   const int64_t grow = int64_t(row0) + row_in_tile;
   T* crow = reinterpret_cast<T*>(p.c) + grow * p.ldc;
   const float rs = (p.row_scale != nullptr && row_ok) ? p.row_scale[grow] : 1.0f;
-  const bool dgelu = p.activation == MOE_ACT_DGELU;
+  // DGELU and MUL_AUX read aux_in; DGELU maps it through gelu', MUL_AUX uses it as is.
+  const bool dgelu = p.activation == MOE_ACT_DGELU || p.activation == MOE_ACT_MUL_AUX;
+  const bool aux_is_grad = p.activation == MOE_ACT_MUL_AUX;
   const T* arow = dgelu ? reinterpret_cast<const T*>(p.aux_in) + grow * p.ld_aux : nullptr;
   // 16-byte vectors of chunk c that lie inside the matrix (0 when the row or chunk is outside).
   auto vecs = [&](int c) {
@@ -141,7 +143,27 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
-      if (p.aux_out != nullptr && nvec > 0) {
+      if (p.activation == MOE_ACT_GELU_SAVE_GRAD) {
+        // One erf per element: C = v * Phi(v), aux_out = Phi(v) + v * phi(v).
+        uint4* ad = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.aux_out) + grow * p.ld_aux + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t g[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float gg2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float x = v[8 * q + 2 * h + u];
+              const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+              gg2[u] = cdf + x * (0.39894228040143267794f * expf(-0.5f * x * x));
+              v[8 * q + 2 * h + u] = x * cdf;
+            }
+            g[h] = pack2<BF16>(gg2[0], gg2[1]);
+          }
+          if (q < nvec) ad[q] = make_uint4(g[0], g[1], g[2], g[3]);
+        }
+      } else if (p.aux_out != nullptr && nvec > 0) {
         uint4* ad = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.aux_out) + grow * p.ld_aux + col);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
@@ -161,8 +183,8 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
               const float2 f = unpack2<BF16>(w[h]);
-              v[8 * q + 2 * h] *= gelu_erf_grad(f.x);
-              v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
+              v[8 * q + 2 * h] *= aux_is_grad ? f.x : gelu_erf_grad(f.x);
+              v[8 * q + 2 * h + 1] *= aux_is_grad ? f.y : gelu_erf_grad(f.y);
             }
           }
         }

@@ -388,9 +388,10 @@ extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b
   using namespace moe::gg;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_F16) return MOE_ERR_INVALID_ARG;
-  if (activation != MOE_ACT_NONE && activation != MOE_ACT_GELU && activation != MOE_ACT_DGELU)
+  if (activation < MOE_ACT_NONE || activation > MOE_ACT_MUL_AUX) return MOE_ERR_INVALID_ARG;
+  if ((activation == MOE_ACT_DGELU || activation == MOE_ACT_MUL_AUX) && aux_in == nullptr)
     return MOE_ERR_INVALID_ARG;
-  if (activation == MOE_ACT_DGELU && aux_in == nullptr) return MOE_ERR_INVALID_ARG;
+  if (activation == MOE_ACT_GELU_SAVE_GRAD && aux_out == nullptr) return MOE_ERR_INVALID_ARG;
   if ((aux_in != nullptr || aux_out != nullptr) &&
       (ld_aux < n || ld_aux % 8 != 0 || (aux_in && !aligned16(aux_in)) ||
        (aux_out && !aligned16(aux_out))))
@@ -504,7 +505,8 @@ extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, i
                                     int32_t dtype, int32_t activation, int32_t num_sms,
                                     int32_t use_atomic_queue, int32_t* work_counter,
                                     int32_t* status, void* stream) {
-  if (activation == MOE_ACT_DGELU) return MOE_ERR_INVALID_ARG;  // needs aux_in: use _ex
+  // the activations with auxiliary operands need moe_grouped_gemm_ex
+  if (activation != MOE_ACT_NONE && activation != MOE_ACT_GELU) return MOE_ERR_INVALID_ARG;
   return moe_grouped_gemm_ex(a, lda, b, b_stride_e, b_stride_k, b_stride_n, c, ldc,
                              expert_offsets, offsets_int64, m_total, k, n, num_experts, dtype,
                              activation, num_sms, use_atomic_queue, work_counter, nullptr,

@@ -26,7 +26,8 @@ __all__ = [
 
 _DTYPE_CODE = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_F16}
 _ACT_CODE = {None: _lib.MOE_ACT_NONE, "none": _lib.MOE_ACT_NONE, "gelu": _lib.MOE_ACT_GELU,
-             "dgelu": _lib.MOE_ACT_DGELU}
+             "dgelu": _lib.MOE_ACT_DGELU, "gelu_save_grad": _lib.MOE_ACT_GELU_SAVE_GRAD,
+             "mul_aux": _lib.MOE_ACT_MUL_AUX}
 
 
 def _aligned(t: torch.Tensor) -> bool:
@@ -73,6 +74,9 @@ def grouped_gemm(
     row of the product), ``aux_out`` (``[M, N]``, receives the product before
     the activation) and ``aux_in`` (``[M, N]``; with ``activation="dgelu"`` the
     result is the product times gelu'(aux_in), the fused GELU backward).
+    ``activation="gelu_save_grad"`` writes GELU(product) and puts gelu'(product)
+    in ``aux_out`` (one erf per element); ``activation="mul_aux"`` multiplies the
+    product by ``aux_in`` (the backward against that saved derivative).
 
     The extended entry point behind ``persistent_grouped_gemm``: optional fused
     exact GELU (``activation="gelu"``), caller-provided output, and ``num_sms``

@@ -227,10 +227,10 @@ class MoELayer:
 
         The router, softmax, top-k and optional renormalisation run in torch
         autograd; the routed experts run on this package's kernels through
-        RoutedExperts (dispatch, GEMM1+GELU with the pre-activation saved, GEMM2,
-        weighted combine; backward: top-k weight gradient, weighted dispatch of the
-        output gradient, dgrad GEMMs with GELU' fused, combine, weight-gradient
-        GEMMs).  ``router_w``, ``w1`` and ``w2`` receive ``.grad`` when they
+        RoutedExperts (dispatch, GEMM1+GELU saving gelu'(a) from the same erf,
+        GEMM2, weighted combine; backward: top-k weight gradient, weighted
+        dispatch of the output gradient, dgrad GEMMs with the saved gelu'
+        multiplied in, combine, weight-gradient GEMMs).  ``router_w``, ``w1`` and ``w2`` receive ``.grad`` when they
         require it.  The whole batch is one chunk (micro_batch_size must cover it),
         and nothing runs beside the exchange kernels in this path (each phase waits
         for the one before), so they get a grid of one block per SM.
@@ -262,11 +262,12 @@ class MoELayer:
         res.event.current_stream_wait()
         self._mark("fwd_dispatch")
         rows = res.recv_x.shape[0]
-        pre = torch.empty(rows, self.ffn, dtype=torch.bfloat16, device=self.device)
+        pre = torch.empty(rows, self.ffn, dtype=torch.bfloat16, device=self.device)  # gelu'(a)
         h = torch.empty_like(pre)
         kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
+        # h = GELU(a) and, from the same erf, gelu'(a) for the backward.
         grouped_gemm(res.recv_x, self.w1.detach().transpose(1, 2), res.expert_offsets, out=h,
-                     activation="gelu", aux_out=pre, **kw)
+                     activation="gelu_save_grad", aux_out=pre, **kw)
         self._mark("fwd_gemm1")
         y = disp.expert_out_buffer(res.handle)
         grouped_gemm(h, self.w2.detach().transpose(1, 2), res.expert_offsets, out=y, **kw)
@@ -297,7 +298,7 @@ class MoELayer:
         rb.event.current_stream_wait()
         self._mark("bwd_dispatch")
         d_pre = torch.empty_like(state["pre"])
-        grouped_gemm(rb.recv_x, self.w2.detach(), rb.expert_offsets, out=d_pre, activation="dgelu",
+        grouped_gemm(rb.recv_x, self.w2.detach(), rb.expert_offsets, out=d_pre, activation="mul_aux",
                      aux_in=state["pre"], **kw)
         self._mark("bwd_dgrad2")
         dx_rows = disp.expert_out_buffer(rb.handle)

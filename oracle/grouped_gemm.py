@@ -112,16 +112,23 @@ def gelu_erf_grad(x: np.ndarray) -> np.ndarray:
 
 
 def grouped_gemm_ex(a, b, offsets, dtype: str, activation=None, row_scale=None, aux_in=None):
-    """Extended epilogue: v = acc * row_scale; returns (C, aux_out=v) as storage arrays
-    and the defined-row mask.  activation None / "gelu" / "dgelu" (v * gelu'(aux_in))."""
+    """Extended epilogue: v = acc * row_scale; returns (C, aux_out) as storage arrays
+    and the defined-row mask.  aux_out = v, except gelu'(v) for "gelu_save_grad".
+    activation None / "gelu" / "gelu_save_grad" (GELU(v)) / "dgelu" (v * gelu'(aux_in))
+    / "mul_aux" (v * aux_in)."""
     acc, defined = grouped_gemm_f32(a, b, offsets, dtype)
     if row_scale is not None:
         acc = (acc * np.asarray(row_scale, np.float32)[:, None]).astype(np.float32)
     aux = from_f32(acc, dtype)
     if activation == "gelu":
         out = gelu_erf(acc).astype(np.float32)
+    elif activation == "gelu_save_grad":
+        out = gelu_erf(acc).astype(np.float32)
+        aux = from_f32(gelu_erf_grad(acc).astype(np.float32), dtype)
     elif activation == "dgelu":
         out = (acc * gelu_erf_grad(to_f32(aux_in, dtype))).astype(np.float32)
+    elif activation == "mul_aux":
+        out = (acc * to_f32(aux_in, dtype)).astype(np.float32)
     else:
         out = acc
     return from_f32(out, dtype), aux, defined

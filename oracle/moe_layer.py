@@ -160,8 +160,8 @@ def experts_backward_bf16(x_bits, idx, w, w1_bits, w2_bits, dout_bits):
     """Routed-expert gradients at the build's rounding points, for a given routing.
 
     Per (token, slot) with expert e (numpy fp32 matmuls, bf16 where the pipeline
-    stores):  pre = bf16(x W1[e]^T), h = bf16(gelu(x W1[e]^T)), y = bf16(h W2[e]^T);
-    dy = bf16(w * dout); dpre = bf16((dy W2[e]) * gelu'(pre)); dxr = bf16(dpre W1[e]).
+    stores):  a = x W1[e]^T (fp32), g = bf16(gelu'(a)), h = bf16(gelu(a)), y = bf16(h W2[e]^T);
+    dy = bf16(w * dout); dpre = bf16((dy W2[e]) * g); dxr = bf16(dpre W1[e]).
     Returns a dict of
       ``dx``   bf16 bits [T, H]: the slot sum of dxr in fp32, rounded once;
       ``dw``   float64 [T, k]:  <dout, y>;
@@ -186,12 +186,12 @@ def experts_backward_bf16(x_bits, idx, w, w1_bits, w2_bits, dout_bits):
         toks, slots = sel[:, 0], sel[:, 1]
         w1f, w2f = bf16_bits_to_f32(w1_bits[e]), bf16_bits_to_f32(w2_bits[e])
         acc = xf[toks] @ w1f.T
-        pre = rnd(acc)
+        gsave = rnd(gelu_erf_grad(acc))
         h = rnd(gelu_erf(acc))
         y = rnd(h @ w2f.T)
         dw[toks, slots] = (dof[toks].astype(np.float64) * y).sum(axis=1)
         dy = rnd(w[toks, slots][:, None].astype(np.float32) * dof[toks])
-        dpre = rnd((dy @ w2f) * gelu_erf_grad(pre))
+        dpre = rnd((dy @ w2f) * gsave)
         dxr = rnd(dpre @ w1f)
         np.add.at(dx, toks, dxr)
         np.add.at(mag_dx, toks, np.abs(dxr))

@@ -235,3 +235,27 @@ def test_wgrad_rejects_misaligned_segments(cuda_device):
     assert rc == 0
     torch.cuda.synchronize()
     assert int(status.item()) == _lib.MOE_ERR_OFFSETS
+
+
+@pytest.mark.parametrize("num_sms", [148, 1])
+def test_epilogue_gelu_save_grad_and_mul_aux(cuda_device, num_sms):
+    """GELU with gelu'(v) saved to aux_out, then v * aux_in: the split GELU backward."""
+    counts = [70, 0, 130, 64]
+    a, b, off = gemm_inputs(counts, 256, 384, "bf16", seed=33, w_std=0.05)
+    m = a.shape[0]
+    g = torch.Generator().manual_seed(34)
+    aux_in = (torch.rand(m, 384, generator=g) * 1.2).to(torch.bfloat16)
+    da, db, doff = a.to(cuda_device), b.to(cuda_device), off.to(cuda_device)
+    aux_out = torch.empty(m, 384, dtype=torch.bfloat16, device=cuda_device)
+    c = mo.grouped_gemm(da, db, doff, activation="gelu_save_grad", aux_out=aux_out, num_sms=num_sms)
+    c2 = mo.grouped_gemm(da, db, doff, activation="mul_aux", aux_in=aux_in.to(cuda_device),
+                         num_sms=num_sms)
+    mo.check_status(cuda_device, sync=True)
+    sa, sb = to_storage(a), to_storage(b)
+    want, want_aux, defined = og.grouped_gemm_ex(sa, sb, off.numpy(), "bf16", "gelu_save_grad")
+    assert_matches_oracle(c, want, defined, "bf16")
+    assert_matches_oracle(aux_out, want_aux, defined, "bf16")
+    want2, _, _ = og.grouped_gemm_ex(sa, sb, off.numpy(), "bf16", "mul_aux", aux_in=to_storage(aux_in))
+    assert_matches_oracle(c2, want2, defined, "bf16")
+    with pytest.raises(mo.MoeError):
+        mo.grouped_gemm(da, db, doff, activation="gelu_save_grad")  # aux_out is required
