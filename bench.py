@@ -792,7 +792,9 @@ def main() -> None:
                 "frac": round(achieved / peak, 4),
                 "peak_source": peak_src,
                 "traffic": profiled_traffic(args.workload),
-                "kernel": "moe::gg::grouped_gemm_kernel",
+                "kernel": ("moe::gg::grouped_gemm_kernel (1 SM)" if sm_count < 2 or
+                           os.environ.get("MOE_B200_GEMM_KERNEL") == "1"
+                           else "moe::gg::pair::grouped_gemm_pair_kernel (CTA pairs, TMA-store epilogue)"),
                 "algorithmic_work": f"2*M*K*N = {flops / 1e9:.2f} GFLOP per launch (M={m_rows} real rows)",
             },
             "cpu_baseline": cpu,
