@@ -90,10 +90,12 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(LAYER_WORKLOADS),
                     default="gemm_cfg2")
-    ap.add_argument("--comm-sms", type=int, default=24,
+    ap.add_argument("--comm-sms", type=int, default=48,
                     help="layer workloads: SM budget (grid) of the dispatch/combine kernels")
     ap.add_argument("--micro-batch", type=int, default=4096,
                     help="layer workloads: tokens per pipelined chunk")
+    ap.add_argument("--taper", action="store_true",
+                    help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     return ap.parse_args()
@@ -368,7 +370,8 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     T, H, Fd, E, K = cfg["tokens"], cfg["hidden"], cfg["ffn"], cfg["experts"], cfg["top_k"]
     layer = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
                      router_bias=cfg["zipf_bias"], num_comm_sms=args.comm_sms,
-                     micro_batch_size=args.micro_batch).init_random(std=0.02, seed=0)
+                     micro_batch_size=args.micro_batch,
+                     taper_chunks=args.taper).init_random(std=0.02, seed=0)
     bias_info = None
     if cfg["zipf_bias"]:
         rw, _, _ = random_weights(E, H, Fd, 0.02, 0)
@@ -448,6 +451,7 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
             "config": {"workload": args.workload, "description": cfg["desc"],
                        "tokens_per_rank": T, "micro_batch": args.micro_batch,
+                       "chunks": [e - s for s, e in layer.chunk_plan(T)],
                        "comm_sms": args.comm_sms, "gate_bias": bias_info,
                        "realised_expert_share": [round(v, 4) for v in realised_share],
                        "rows_received_per_rank": [int(v) for v in recv_rows.tolist()],
