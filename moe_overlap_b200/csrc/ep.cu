@@ -44,8 +44,14 @@ constexpr int kMaxRanks = MOE_EP_MAX_RANKS;
 constexpr int kMaxExperts = 1024;
 constexpr int kAssignPerLayoutBlock = 2048;  // 8 warps x 8 chunks x 32 lanes
 constexpr int kLayoutThreads = 256;
-constexpr int kCommThreads = 512;
-constexpr int kPullThreads = 256;
+// The scatter and pull blocks are sized to run beside a resident CTA of the
+// CTA-pair grouped GEMM (320 threads x 168 registers, ~215 KB shared memory),
+// which leaves ~11.7K registers and ~17 KB of shared memory per SM: 128 threads
+// at <= 64 registers and the 12 KB CountView fit, so the exchange runs during the
+// expert GEMMs instead of waiting for their persistent CTAs to exit.
+constexpr int kCommThreads = 128;
+constexpr int kPullThreads = 128;
+constexpr int kCommMinBlocks = 8;  // __launch_bounds__ minimum: caps registers at 64
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -291,7 +297,7 @@ __device__ __forceinline__ bool wait_all_flags(const Params& p, uint64_t off, in
   return *fail == 0;
 }
 
-__global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(Params p) {
   __shared__ CountView cv;
   if (threadIdx.x == 0) {
     cv.overflow = 0;
@@ -357,9 +363,9 @@ __global__ void __launch_bounds__(kCommThreads) scatter_kernel(Params p) {
           p.send_pos[a] = row;
         }
       }
-      // Each lane loads 8 x 16 B per pass (a 4 KB row per warp for H = 2048)
+      // Each lane loads 4 x 16 B per pass (2 KB of a row per warp)
       // before storing anything, so every load of the pass is in flight at once.
-      constexpr int U = 8;
+      constexpr int U = 4;
       for (int base = 0; base < nvec; base += 32 * U) {
         uint4 v[U];
 #pragma unroll
@@ -492,7 +498,7 @@ __device__ __forceinline__ void pull_token(const uint4* const* srcs, const float
 }
 
 template <int U, int MAXR>
-__global__ void __launch_bounds__(kPullThreads, 2) pull_kernel(Params p) {
+__global__ void __launch_bounds__(kPullThreads, kCommMinBlocks) pull_kernel(Params p) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
   __syncthreads();
@@ -871,11 +877,11 @@ extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int grid = num_blocks;
   if (topk <= 2)
-    pull_kernel<8, 2><<<grid, kPullThreads, 0, stream>>>(p);
+    pull_kernel<4, 2><<<grid, kPullThreads, 0, stream>>>(p);
   else if (topk <= 4)
-    pull_kernel<4, 4><<<grid, kPullThreads, 0, stream>>>(p);
+    pull_kernel<2, 4><<<grid, kPullThreads, 0, stream>>>(p);
   else
-    pull_kernel<2, 8><<<grid, kPullThreads, 0, stream>>>(p);
+    pull_kernel<1, 8><<<grid, kPullThreads, 0, stream>>>(p);
   return check_launch();
 }
 

@@ -47,6 +47,7 @@ constexpr int STAGES = 6;
 constexpr int QDEPTH = 8;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr int kMaxRegs = 144;
 constexpr int A_STAGE_BYTES = BM_CTA * BK * 2;  // 16 KiB
 constexpr int B_STAGE_BYTES = BK * BN_CTA * 2;  // 16 KiB
 constexpr int B_SLAB_BYTES = BK * 64 * 2;       // one 64-column slab of an N-major B stage
@@ -73,7 +74,11 @@ __host__ __device__ constexpr size_t smem_bytes(int num_experts) {
 }
 
 template <bool BF16, bool B_MN_MAJOR>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+// 144 registers: with 10 warps, SM sub-partitions 0 and 1 hold three of them
+// (3 x 32 x 144 = 13,824 of their 16,384 registers), which leaves room for one
+// warp per sub-partition of a 4-warp exchange block at <= 80 registers, so the
+// dispatch/combine kernels run beside this persistent kernel.
+__global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                              const __grid_constant__ CUtensorMap tmap_b,
                              const __grid_constant__ CUtensorMap tmap_c, const Params p) {

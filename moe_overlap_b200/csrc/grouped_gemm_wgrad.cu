@@ -366,8 +366,10 @@ struct Ctrl {
 constexpr size_t kSmem = 1024 + size_t(STAGES) * (A_STAGE_BYTES + B_STAGE_BYTES) +
                          size_t(NUM_EPI_WARPS) * EPI_STAGE_BYTES + ((sizeof(Ctrl) + 15) / 16) * 16;
 
+// 144 registers leave room for a 4-warp exchange block beside this kernel (see
+// the forward pair kernel): the backward's combine runs during the weight gradients.
 template <bool BF16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __maxnreg__(144)
     wgrad_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_c, const WParams wp) {

@@ -174,7 +174,8 @@ class DeepEPDispatcher:
     def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
                  previous_event: Optional[object] = None, *,
                  exact_size: Optional[bool] = None, expert_alignment: int = 1,
-                 scale_rows: bool = False, num_sms: Optional[int] = None) -> DispatchResult:
+                 scale_rows: bool = False, num_sms: Optional[int] = None,
+                 pad_rows: Optional[bool] = None) -> DispatchResult:
         if x.dtype != torch.bfloat16:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
@@ -199,7 +200,11 @@ class DeepEPDispatcher:
             wc = topk_weights.to(torch.float32).contiguous()
             if xc.data_ptr() % 16 != 0:
                 xc = xc.clone()
-            self._ep.dispatch(xc, ic, wc, slot, epoch, num_sms or self.num_sms, not exact, self.wait_ns,
+            # Without an exact size the receive views span the whole slot; pad_rows
+            # marks the rows past the received count (-1 ids, zero weights) so the
+            # views read like DeepEP's.  Callers that use expert_offsets can skip it.
+            pad = (not exact) if pad_rows is None else bool(pad_rows)
+            self._ep.dispatch(xc, ic, wc, slot, epoch, num_sms or self.num_sms, pad, self.wait_ns,
                               self._status, expert_alignment, scale_rows)
             offs = self._ep.slots[slot].expert_offsets
             per_expert = offs[1:] - offs[:-1]

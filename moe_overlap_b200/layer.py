@@ -169,7 +169,7 @@ class MoELayer:
         chunks = self.chunk_plan(t_total)
         disp = self.dispatcher
         cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
-                            w[chunks[0][0]:chunks[0][1]])
+                            w[chunks[0][0]:chunks[0][1]], pad_rows=False)
         for i, (s, e) in enumerate(chunks):
             # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
             # starts them as soon as this chunk's rows have landed, and the host
@@ -182,7 +182,7 @@ class MoELayer:
             nxt = None
             if i + 1 < len(chunks):
                 ns, ne = chunks[i + 1]
-                nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne])
+                nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
             disp.combine(y, cur.handle, previous_event=done, weighted=True, out=out[s:e])
             cur = nxt
         torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
@@ -220,7 +220,7 @@ class MoELayer:
             return r
 
         for s, e in chunks:
-            res = timed("dispatch_ms", lambda: disp.dispatch(x[s:e], idx[s:e], w[s:e]))
+            res = timed("dispatch_ms", lambda: disp.dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False))
             res.event.current_stream_wait()
             y = timed("experts_ms", lambda: self._experts(res))
             timed("combine_ms", lambda: disp.combine(y, res.handle, weighted=True, out=out[s:e]))
@@ -280,7 +280,8 @@ class MoELayer:
         if x.shape[0] > self.micro:
             raise ValueError("training forward runs the batch as one chunk: raise micro_batch_size")
         x = x.to(torch.bfloat16).contiguous()
-        res = disp.dispatch(x, idx, w.float(), exact_size=False, expert_alignment=TRAIN_ALIGNMENT,
+        res = disp.dispatch(x, idx, w.float(), exact_size=False, pad_rows=False,
+                            expert_alignment=TRAIN_ALIGNMENT,
                             num_sms=self.gemm_sms)
         res.event.current_stream_wait()
         self._mark("fwd_dispatch")
@@ -316,7 +317,7 @@ class MoELayer:
         self._mark("bwd_topk_weight_grad")
         # The output gradient goes back to the experts weighted: dY = w * dout rows,
         # laid out exactly like the forward rows (same routing and alignment).
-        rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False,
+        rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False, pad_rows=False,
                            expert_alignment=TRAIN_ALIGNMENT, scale_rows=True, num_sms=self.gemm_sms)
         rb.event.current_stream_wait()
         self._mark("bwd_dispatch")
