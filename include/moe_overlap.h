@@ -42,6 +42,7 @@ extern "C" {
 /* ----------------------------------------------------------------- dtypes -- */
 #define MOE_DTYPE_BF16 0
 #define MOE_DTYPE_F16 1
+#define MOE_DTYPE_F32 2 /* router logits only */
 
 /* ------------------------------------------------------------ activations -- */
 #define MOE_ACT_NONE 0
@@ -333,6 +334,34 @@ MOE_API int32_t moe_ep_combine(moe_ep_t ep, const int64_t* topk_idx, const float
 MOE_API int32_t moe_ep_topk_weight_grad(moe_ep_t ep, const void* grad_out, const int64_t* topk_idx,
                                         int32_t num_tokens, int32_t topk, int32_t slot, float* out,
                                         int32_t num_blocks, void* stream);
+
+/*
+ * Router top-k: softmax / top-k / renormalisation after the gate's linear layer
+ * (src/train_moe_baseline.py:316-318; the bias and renormalisation are the
+ * BASELINE configs' options).  One warp per token, E <= 256, top_k <= 16.
+ *   logits          [T, E] bf16 (MOE_DTYPE_BF16) or fp32 (MOE_DTYPE_F32)
+ *   bias            [E] fp32 or NULL, added to the logits
+ *   probs           [T, E] fp32 out: softmax(logits + bias)
+ *   topk_idx        [T, k] int64 out: the k largest probabilities, ties to the
+ *                   lower expert id, in descending order
+ *   topk_weights    [T, k] fp32 out: those probabilities, divided by their sum
+ *                   when renormalize != 0
+ */
+MOE_API int32_t moe_router_topk(const void* logits, int32_t logits_dtype, const float* bias,
+                                int32_t num_tokens, int32_t num_experts, int32_t topk,
+                                int32_t renormalize, float* probs, int64_t* topk_idx,
+                                float* topk_weights, void* stream);
+
+/*
+ * Backward of moe_router_topk's topk_weights with respect to the logits:
+ * grad_logits [T, E] fp32 = softmax-backward of the gradient scattered from
+ * grad_topk_weights [T, k] (through the renormalisation when renormalize != 0).
+ * No counterpart in the reference, which runs inference only.
+ */
+MOE_API int32_t moe_router_topk_backward(const float* probs, const int64_t* topk_idx,
+                                         const float* grad_topk_weights, int32_t num_tokens,
+                                         int32_t num_experts, int32_t topk, int32_t renormalize,
+                                         float* grad_logits, void* stream);
 
 /*
  * DeepEP's get_dispatch_layout (thirdParty/DeepEP/deep_ep/buffer.py:293-319,

@@ -32,6 +32,7 @@ MOE_ERR_CAPACITY = 6
 
 MOE_DTYPE_BF16 = 0
 MOE_DTYPE_F16 = 1
+MOE_DTYPE_F32 = 2
 MOE_ACT_NONE = 0
 MOE_ACT_GELU = 1
 MOE_ACT_DGELU = 2
@@ -130,6 +131,16 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_combine": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _c_void_p, _i32,
                _u64, _c_void_p, _c_void_p]),
+    "moe_router_topk": (
+        _i32,
+        [_c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32,  # logits, dtype, bias, T, E, k, renorm
+         _c_void_p, _c_void_p, _c_void_p, _c_void_p],  # probs, idx, weights, stream
+    ),
+    "moe_router_topk_backward": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32,  # probs, idx, dw, T, E, k, renorm
+         _c_void_p, _c_void_p],  # grad_logits, stream
+    ),
     "moe_ep_dispatch_layout": (
         _i32, [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "moe_ipc_export": (_i32, [_c_void_p, _c_void_p]),

@@ -24,10 +24,10 @@ from typing import Optional
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 
 from .deep_ep_comm import DeepEPDispatcher
 from .gemm import grouped_gemm, grouped_gemm_wgrad
+from .router import router_topk
 
 # Expert segments of a training dispatch are padded to this many rows so the
 # weight-gradient GEMM's 64-row k-blocks never straddle two experts.
@@ -61,7 +61,7 @@ class MoELayer:
 
     def __init__(self, hidden_size: int, ffn_size: int, num_experts: int, top_k: int, *,
                  group: Optional[dist.ProcessGroup] = None, renormalize: bool = False,
-                 router_bias: bool = False, num_comm_sms: int = 24,
+                 router_bias: bool = False, num_comm_sms: int = 148,
                  micro_batch_size: int = 4096, use_atomic_queue: bool = True,
                  max_recv_rows: Optional[int] = None, training: bool = False,
                  taper_chunks: bool = False):
@@ -120,15 +120,14 @@ class MoELayer:
 
     # ----------------------------------------------------------------- forward --
     def route(self, x: torch.Tensor):
-        """softmax router and top-k (src/train_moe_baseline.py:316-318); float32 weights."""
-        logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t()).float()
-        if self.router_b is not None:
-            logits = logits + self.router_b
-        probs = F.softmax(logits, dim=-1)
-        w, idx = torch.topk(probs, k=self.top_k, dim=-1)
-        if self.renormalize:
-            w = w / w.sum(dim=-1, keepdim=True)
-        return probs, idx.to(torch.int64), w.contiguous()
+        """softmax router and top-k (src/train_moe_baseline.py:316-318); float32 weights.
+
+        The gate's linear layer is one bf16 matmul (bf16 logits, as under the
+        reference's autocast); softmax, bias, top-k and renormalisation are one
+        kernel (router.router_topk)."""
+        with torch.no_grad():
+            logits = torch.matmul(x.to(torch.bfloat16), self.router_w.detach().t())
+            return router_topk(logits, self.top_k, bias=self.router_b, renormalize=self.renormalize)
 
     def _experts(self, res) -> torch.Tensor:
         """GEMM1 (+GELU) and GEMM2 on the current stream; returns the expert-output rows."""
@@ -248,8 +247,8 @@ class MoELayer:
     def forward_autograd(self, x: torch.Tensor):
         """Differentiable forward: returns (out, probs, topk_idx).
 
-        The router, softmax, top-k and optional renormalisation run in torch
-        autograd; the routed experts run on this package's kernels through
+        The gate's linear layer runs in torch autograd, softmax / top-k /
+        renormalisation in router.RouterTopK (forward and backward kernels); the routed experts run on this package's kernels through
         RoutedExperts (dispatch, GEMM1+GELU saving gelu'(a) from the same erf,
         GEMM2, weighted combine; backward: top-k weight gradient, weighted
         dispatch of the output gradient, dgrad GEMMs with the saved gelu'
@@ -258,14 +257,10 @@ class MoELayer:
         and nothing runs beside the exchange kernels in this path (each phase waits
         for the one before), so they get a grid of one block per SM.
         """
-        logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t()).float()
-        if self.router_b is not None:
-            logits = logits + self.router_b
-        probs = F.softmax(logits, dim=-1)
-        w, idx = torch.topk(probs, k=self.top_k, dim=-1)
-        if self.renormalize:
-            w = w / w.sum(dim=-1, keepdim=True)
-        out = RoutedExperts.apply(x, w, self.w1, self.w2, idx.to(torch.int64), self)
+        logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t())
+        probs, idx, w = router_topk(logits, self.top_k, bias=self.router_b,
+                                    renormalize=self.renormalize)
+        out = RoutedExperts.apply(x, w, self.w1, self.w2, idx, self)
         return out, probs, idx
 
     def _mark(self, phase: str) -> None:

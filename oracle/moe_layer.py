@@ -201,3 +201,32 @@ def experts_backward_bf16(x_bits, idx, w, w1_bits, w2_bits, dout_bits):
         mag1[e] = np.abs(dpre).T @ np.abs(xf[toks])
     return dict(dx=f32_to_bf16_bits(dx), dw=dw, dw1=f32_to_bf16_bits(dw1),
                 dw2=f32_to_bf16_bits(dw2), mag_dx=mag_dx, mag_dw1=mag1, mag_dw2=mag2)
+
+
+def topk_from_logits(logits, top_k: int, router_b=None, renormalize: bool = False):
+    """(probs, topk_idx, topk_w) of given logits [T, E] (fp32 arithmetic, ties to the
+    lower expert id): the steps after the gate's linear layer in route()."""
+    z = np.asarray(logits, np.float32)
+    if router_b is not None:
+        z = z + np.asarray(router_b, np.float32)
+    probs = softmax(z).astype(np.float32)
+    idx = np.argsort(-probs, axis=-1, kind="stable")[:, :top_k].astype(np.int64)
+    w = np.take_along_axis(probs, idx, axis=-1)
+    if renormalize:
+        w = w / w.sum(axis=-1, keepdims=True)
+    return probs, idx, w.astype(np.float32)
+
+
+def topk_backward(probs, idx, dw, renormalize: bool = False):
+    """d loss / d logits for the upstream gradient dw [T, k] of topk_from_logits'
+    weights (float64): through the renormalisation, scattered to the selected
+    experts, then the softmax backward p * (dp - <p, dp>)."""
+    p = np.asarray(probs, np.float64)
+    d = np.asarray(dw, np.float64)
+    sel = np.take_along_axis(p, idx, axis=-1)
+    if renormalize:
+        s = sel.sum(axis=-1, keepdims=True)
+        d = (d - (d * (sel / s)).sum(axis=-1, keepdims=True)) / s
+    dp = np.zeros_like(p)
+    np.put_along_axis(dp, idx, d, axis=-1)
+    return p * (dp - (p * dp).sum(axis=-1, keepdims=True))
