@@ -93,6 +93,9 @@ class MoELayer:
                                            max_recv_rows=max_recv_rows, exact_size=False)
         self.compute_stream = torch.cuda.Stream(dev)
         self.gemm_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        # Exchange blocks when nothing runs beside them (the training path waits for
+        # each exchange phase): four 128-thread blocks per SM.
+        self.solo_comm_blocks = 4 * self.gemm_sms
         self.h = torch.empty(self.dispatcher.max_recv_rows, ffn_size, dtype=bf16, device=dev)
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
         # When a list, the training path appends (phase, event) pairs recorded on
@@ -255,7 +258,7 @@ class MoELayer:
         multiplied in, combine, weight-gradient GEMMs).  ``router_w``, ``w1`` and ``w2`` receive ``.grad`` when they
         require it.  The whole batch is one chunk (micro_batch_size must cover it),
         and nothing runs beside the exchange kernels in this path (each phase waits
-        for the one before), so they get a grid of one block per SM.
+        for the one before), so they get four blocks per SM.
         """
         logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t())
         probs, idx, w = router_topk(logits, self.top_k, bias=self.router_b,
@@ -277,7 +280,7 @@ class MoELayer:
         x = x.to(torch.bfloat16).contiguous()
         res = disp.dispatch(x, idx, w.float(), exact_size=False, pad_rows=False,
                             expert_alignment=TRAIN_ALIGNMENT,
-                            num_sms=self.gemm_sms)
+                            num_sms=self.solo_comm_blocks)
         res.event.current_stream_wait()
         self._mark("fwd_dispatch")
         rows = res.recv_x.shape[0]
@@ -291,7 +294,7 @@ class MoELayer:
         y = disp.expert_out_buffer(res.handle)
         grouped_gemm(h, self.w2.detach().transpose(1, 2), res.expert_offsets, out=y, **kw)
         self._mark("fwd_gemm2")
-        out, ev = disp.combine(y, res.handle, weighted=True, num_sms=self.gemm_sms)
+        out, ev = disp.combine(y, res.handle, weighted=True, num_sms=self.solo_comm_blocks)
         ev.current_stream_wait()
         self._mark("fwd_combine")
         return out, dict(res=res, pre=pre, h=h, idx=idx, w=w.float())
@@ -308,12 +311,13 @@ class MoELayer:
         dout = dout.to(torch.bfloat16).contiguous()
         kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
         # d/d topk weight: <dout[t], y(t, j)>, read from the forward's expert outputs.
-        dw = disp.topk_weight_grad(dout, res.handle, num_sms=self.gemm_sms)
+        dw = disp.topk_weight_grad(dout, res.handle, num_sms=self.solo_comm_blocks)
         self._mark("bwd_topk_weight_grad")
         # The output gradient goes back to the experts weighted: dY = w * dout rows,
         # laid out exactly like the forward rows (same routing and alignment).
         rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False, pad_rows=False,
-                           expert_alignment=TRAIN_ALIGNMENT, scale_rows=True, num_sms=self.gemm_sms)
+                           expert_alignment=TRAIN_ALIGNMENT, scale_rows=True,
+                           num_sms=self.solo_comm_blocks)
         rb.event.current_stream_wait()
         self._mark("bwd_dispatch")
         d_pre = torch.empty_like(state["pre"])
