@@ -148,14 +148,19 @@ class DeepEPDispatcher:
         self._status = _lib.status_word(self.device)
 
     # ------------------------------------------------------------------------
-    def _enter_comm(self, previous_event) -> None:
-        # Wait for the caller's stream as well as previous_event: the expert
-        # outputs handed to combine are produced there.
+    def _enter_comm(self, previous_event, inline: bool = False) -> torch.cuda.Stream:
+        """The stream the exchange runs on: the dispatcher's own, after the caller's
+        stream and previous_event (the expert outputs handed to combine are produced
+        there), or, with ``inline``, the caller's current stream itself."""
+        cur = torch.cuda.current_stream(self.device)
+        stream = cur if inline else self.comm_stream
         if previous_event is not None:
             ev = getattr(previous_event, "event", previous_event)
             if ev is not None:
-                self.comm_stream.wait_event(ev)
-        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+                stream.wait_event(ev)
+        if not inline:
+            self.comm_stream.wait_stream(cur)
+        return stream
 
     def get_dispatch_layout(self, topk_idx: torch.Tensor, num_experts: int):
         """(num_tokens_per_rank, None, num_tokens_per_expert, is_token_in_rank) as DeepEP returns."""
@@ -175,7 +180,7 @@ class DeepEPDispatcher:
                  previous_event: Optional[object] = None, *,
                  exact_size: Optional[bool] = None, expert_alignment: int = 1,
                  scale_rows: bool = False, num_sms: Optional[int] = None,
-                 pad_rows: Optional[bool] = None) -> DispatchResult:
+                 pad_rows: Optional[bool] = None, inline: bool = False) -> DispatchResult:
         if x.dtype != torch.bfloat16:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
@@ -193,8 +198,8 @@ class DeepEPDispatcher:
         _lib.check_status(self.device)
         self._epoch += 1
         epoch, slot = self._epoch, self._epoch % 2
-        self._enter_comm(previous_event)
-        with torch.cuda.stream(self.comm_stream):
+        stream = self._enter_comm(previous_event, inline)
+        with torch.cuda.stream(stream):
             xc = x.contiguous()
             ic = topk_idx.to(torch.int64).contiguous()
             wc = topk_weights.to(torch.float32).contiguous()
@@ -209,9 +214,10 @@ class DeepEPDispatcher:
             offs = self._ep.slots[slot].expert_offsets
             per_expert = offs[1:] - offs[:-1]
             event = torch.cuda.Event()
-            event.record(self.comm_stream)
-        for t in (x, topk_idx, topk_weights):
-            t.record_stream(self.comm_stream)
+            event.record(stream)
+        if not inline:
+            for t in (x, topk_idx, topk_weights):
+                t.record_stream(self.comm_stream)
         views = self._ep.slots[slot]
         rows = self._ep.received_rows(slot, epoch) if exact else views.recv_x.shape[0]
         handle = DispatchHandle(slot, epoch, num_tokens, topk, ic, wc, xc, rows if exact else None)
@@ -261,7 +267,7 @@ class DeepEPDispatcher:
                 previous_event: Optional[object] = None, *,
                 weighted: bool = False,
                 out: Optional[torch.Tensor] = None,
-                num_sms: Optional[int] = None) -> Tuple[torch.Tensor, object]:
+                num_sms: Optional[int] = None, inline: bool = False) -> Tuple[torch.Tensor, object]:
         if not isinstance(handle, DispatchHandle) or handle.combined:
             raise RuntimeError("combine needs the handle of an outstanding dispatch")
         if expert_out.dtype != torch.bfloat16 or expert_out.dim() != 2 or \
@@ -271,14 +277,14 @@ class DeepEPDispatcher:
             raise RuntimeError("combine the oldest outstanding dispatch first")
         _lib.check_status(self.device)
         views = self._ep.slots[handle.slot]
-        self._enter_comm(previous_event)
+        stream = self._enter_comm(previous_event, inline)
         if out is None:
             out = torch.empty((handle.num_tokens, self.hidden_size), dtype=torch.bfloat16,
                               device=self.device)
         elif (out.shape != (handle.num_tokens, self.hidden_size) or out.dtype != torch.bfloat16
               or not out.is_contiguous() or out.data_ptr() % 16 != 0):
             raise ValueError("out must be a contiguous, 16-byte aligned bf16 [num_tokens, hidden]")
-        with torch.cuda.stream(self.comm_stream):
+        with torch.cuda.stream(stream):
             if expert_out.data_ptr() != views.expert_out.data_ptr():
                 rows = expert_out.shape[0]
                 if rows > views.expert_out.shape[0]:
@@ -287,9 +293,10 @@ class DeepEPDispatcher:
             self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot, handle.epoch,
                              weighted, out, num_sms or self.num_sms, self.wait_ns, self._status)
             event = torch.cuda.Event()
-            event.record(self.comm_stream)
-        expert_out.record_stream(self.comm_stream)
-        out.record_stream(self.comm_stream)
+            event.record(stream)
+        if not inline:
+            expert_out.record_stream(self.comm_stream)
+            out.record_stream(self.comm_stream)
         handle.combined = True
         self._outstanding.popleft()
         return out, EventOverlap(event)

@@ -258,7 +258,9 @@ class MoELayer:
         multiplied in, combine, weight-gradient GEMMs).  ``router_w``, ``w1`` and ``w2`` receive ``.grad`` when they
         require it.  The whole batch is one chunk (micro_batch_size must cover it),
         and nothing runs beside the exchange kernels in this path (each phase waits
-        for the one before), so they get four blocks per SM.
+        for the one before), so they run on the caller's stream (no stream switch)
+        with four blocks per SM; only the backward's combine of dx runs on the
+        exchange stream, beside the weight-gradient GEMMs.
         """
         logits = torch.matmul(x.to(torch.bfloat16), self.router_w.t())
         probs, idx, w = router_topk(logits, self.top_k, bias=self.router_b,
@@ -278,7 +280,7 @@ class MoELayer:
         if x.shape[0] > self.micro:
             raise ValueError("training forward runs the batch as one chunk: raise micro_batch_size")
         x = x.to(torch.bfloat16).contiguous()
-        res = disp.dispatch(x, idx, w.float(), exact_size=False, pad_rows=False,
+        res = disp.dispatch(x, idx, w.float(), exact_size=False, pad_rows=False, inline=True,
                             expert_alignment=TRAIN_ALIGNMENT,
                             num_sms=self.solo_comm_blocks)
         res.event.current_stream_wait()
@@ -294,7 +296,8 @@ class MoELayer:
         y = disp.expert_out_buffer(res.handle)
         grouped_gemm(h, self.w2.detach().transpose(1, 2), res.expert_offsets, out=y, **kw)
         self._mark("fwd_gemm2")
-        out, ev = disp.combine(y, res.handle, weighted=True, num_sms=self.solo_comm_blocks)
+        out, ev = disp.combine(y, res.handle, weighted=True, num_sms=self.solo_comm_blocks,
+                               inline=True)
         ev.current_stream_wait()
         self._mark("fwd_combine")
         return out, dict(res=res, pre=pre, h=h, idx=idx, w=w.float())
@@ -315,7 +318,7 @@ class MoELayer:
         self._mark("bwd_topk_weight_grad")
         # The output gradient goes back to the experts weighted: dY = w * dout rows,
         # laid out exactly like the forward rows (same routing and alignment).
-        rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False, pad_rows=False,
+        rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False, pad_rows=False, inline=True,
                            expert_alignment=TRAIN_ALIGNMENT, scale_rows=True,
                            num_sms=self.solo_comm_blocks)
         rb.event.current_stream_wait()

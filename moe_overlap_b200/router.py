@@ -55,6 +55,7 @@ class RouterTopK(torch.autograd.Function):
         ctx.logits_dtype = logits.dtype
         ctx.has_bias = bias is not None
         ctx.mark_non_differentiable(idx)
+        ctx.set_materialize_grads(False)  # unused outputs get None, not zero tensors
         return probs, w, idx
 
     @staticmethod
@@ -62,6 +63,8 @@ class RouterTopK(torch.autograd.Function):
         probs, idx = ctx.saved_tensors
         t, e = probs.shape
         k = idx.shape[1]
+        if grad_w is None and grad_probs is None:
+            return None, None, None, None
         if grad_w is None:
             grad_w = torch.zeros(t, k, dtype=torch.float32, device=probs.device)
         dlogits = torch.empty(t, e, dtype=torch.float32, device=probs.device)
