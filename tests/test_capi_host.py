@@ -152,3 +152,40 @@ def test_library_missing_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "missing.so")
     with pytest.raises(RuntimeError, match="is not built"):
         _lib.load()
+
+
+def test_router_entry_points_reject_bad_arguments_on_host():
+    """Argument checks that return before any CUDA call (runs without a GPU)."""
+    lib = _lib.load()
+    bf16 = _lib.MOE_DTYPE_BF16
+    # more than 256 experts, top_k above the experts, top_k above 16, bad dtype
+    assert lib.moe_router_topk(None, bf16, None, 4, 300, 2, 0, None, None, None, None) == \
+        _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_router_topk(None, bf16, None, 4, 8, 9, 0, None, None, None, None) == \
+        _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_router_topk(None, bf16, None, 4, 64, 17, 0, None, None, None, None) == \
+        _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_router_topk(None, 7, None, 4, 8, 2, 0, None, None, None, None) == \
+        _lib.MOE_ERR_INVALID_ARG
+    # missing buffers with tokens to route
+    assert lib.moe_router_topk(None, bf16, None, 4, 8, 2, 0, None, None, None, None) == \
+        _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_router_topk_backward(None, None, None, 4, 8, 2, 1, None, None) == \
+        _lib.MOE_ERR_INVALID_ARG
+    # no tokens: nothing to do
+    assert lib.moe_router_topk(None, bf16, None, 0, 8, 2, 0, None, None, None, None) == _lib.MOE_OK
+    assert lib.moe_router_topk_backward(None, None, None, 0, 8, 2, 0, None, None) == _lib.MOE_OK
+
+
+def test_grouped_gemm_activation_codes_checked_on_host():
+    """GELU_SAVE_GRAD needs aux_out and MUL_AUX/DGELU need aux_in; the plain entry point
+    takes none of them; unknown codes are rejected - all before any CUDA call."""
+    lib = _lib.load()
+    common = (None, 64, None, 64 * 64, 64, 1, None, 64, None, 0, 64, 64, 64, 1,
+              _lib.MOE_DTYPE_BF16)
+    for act in (_lib.MOE_ACT_DGELU, _lib.MOE_ACT_GELU_SAVE_GRAD, _lib.MOE_ACT_MUL_AUX, 5, -1):
+        assert lib.moe_grouped_gemm(*common, act, 1, 0, None, None, None) == \
+            _lib.MOE_ERR_INVALID_ARG, act
+    ex_tail = (None, None, None, None, 64, None, None)
+    for act in (_lib.MOE_ACT_DGELU, _lib.MOE_ACT_MUL_AUX, _lib.MOE_ACT_GELU_SAVE_GRAD):
+        assert lib.moe_grouped_gemm_ex(*common, act, 1, 0, *ex_tail) == _lib.MOE_ERR_INVALID_ARG, act

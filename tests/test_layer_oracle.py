@@ -38,3 +38,38 @@ def test_oracle_layer_backward_matches_reference_autograd():
                                              int(G["top_k"]), G["dout"])
     for got, want in ((dx, G["dx"]), (dr, G["d_router_w"]), (dw1, G["d_w1"]), (dw2, G["d_w2"])):
         np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-5)
+
+
+def test_oracle_router_topk_backward_matches_torch_autograd():
+    """oracle.topk_backward against torch autograd of softmax -> gather -> (renormalise)
+    on the CPU, with and without renormalisation and a bias."""
+    import torch
+    rng = np.random.default_rng(3)
+    for renorm in (False, True):
+        z = rng.standard_normal((64, 16)).astype(np.float32) * 2
+        bias = rng.standard_normal(16).astype(np.float32) * 0.3
+        probs, idx, _ = ol.topk_from_logits(z, 3, bias, renorm)
+        dw = rng.standard_normal((64, 3))
+        zt = torch.tensor(z, dtype=torch.float64, requires_grad=True)
+        p = torch.softmax(zt + torch.tensor(bias, dtype=torch.float64), dim=-1)
+        sel = p.gather(1, torch.tensor(idx))
+        w = sel / sel.sum(dim=-1, keepdim=True) if renorm else sel
+        w.backward(torch.tensor(dw))
+        got = ol.topk_backward(probs, idx, dw, renorm)
+        np.testing.assert_allclose(got, zt.grad.numpy(), rtol=1e-5, atol=1e-7)
+
+
+def test_layer_chunk_plan_covers_the_batch():
+    from moe_overlap_b200.layer import MoELayer
+
+    class _L:
+        pass
+    for micro in (64, 300, 1000, 4096):
+        for taper in (False, True):
+            lay = _L()
+            lay.micro, lay.taper = micro, taper
+            for t in (0, 1, 63, 64, 65, 999, 1000, 8192, 8193):
+                plan = MoELayer.chunk_plan(lay, t)
+                assert plan[0][0] == 0 and plan[-1][1] == t
+                assert all(a[1] == b[0] for a, b in zip(plan[:-1], plan[1:]))
+                assert all(0 < e - s <= micro for s, e in plan) or t == 0
