@@ -6,17 +6,20 @@
 // which the reference does not have (it runs inference only,
 // src/train_moe_baseline.py:524-552).  The contraction runs over the token rows,
 // so both operands are MN-major in shared memory, straight from their row-major
-// storage: the MMA is tcgen05 kind::f16 128x256x16 with A and B MN-major.
+// storage: tcgen05 kind::f16 MMAs with A and B MN-major.
 //
 // Every expert segment must start and end on a multiple of 64 rows (the
 // exchange's expert_alignment provides that, with zero padding rows), so a
 // 64-row k-block never straddles two experts; a misaligned segment is reported
 // as MOE_ERR_OFFSETS.  An expert without rows gets a zero gradient.
 //
-// One CTA per SM, 192 threads: warp 0 schedules (striped over a fixed tile grid
-// of E x ceil(M/128) x ceil(N/256)) and TMA-loads, warp 1 owns TMEM and issues
-// MMAs, warps 2-5 run the epilogue; two TMEM accumulators overlap the epilogue
-// of one tile with the main loop of the next.
+// Two kernels.  Grids of two or more SMs run wgrad_pair_kernel (CTA pairs,
+// cta_group::2, 256x256 tiles, TMA-store epilogue; see its comment below).  The
+// 1-SM wgrad_kernel (for num_sms == 1 or MOE_B200_GEMM_KERNEL=1): one CTA per SM,
+// 192 threads: warp 0 schedules (striped over a fixed tile grid of
+// E x ceil(M/128) x ceil(N/256)) and TMA-loads, warp 1 owns TMEM and issues
+// 128x256x16 MMAs, warps 2-5 run the epilogue; two TMEM accumulators overlap the
+// epilogue of one tile with the main loop of the next.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
