@@ -170,8 +170,11 @@ class MoELayer:
         out = torch.empty_like(x)
         chunks = self.chunk_plan(t_total)
         disp = self.dispatcher
+        # The first dispatch and the last combine have no GEMM beside them: they get
+        # the solo grid; the others run one block per SM beside the GEMMs.
         cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
-                            w[chunks[0][0]:chunks[0][1]], pad_rows=False)
+                            w[chunks[0][0]:chunks[0][1]], pad_rows=False,
+                            num_sms=self.solo_comm_blocks)
         for i, (s, e) in enumerate(chunks):
             # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
             # starts them as soon as this chunk's rows have landed, and the host
@@ -185,7 +188,9 @@ class MoELayer:
             if i + 1 < len(chunks):
                 ns, ne = chunks[i + 1]
                 nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
-            disp.combine(y, cur.handle, previous_event=done, weighted=True, out=out[s:e])
+            last = i + 1 == len(chunks)
+            disp.combine(y, cur.handle, previous_event=done, weighted=True, out=out[s:e],
+                         num_sms=self.solo_comm_blocks if last else None)
             cur = nxt
         torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
         stats = self.stats(probs, idx) if return_stats else None
