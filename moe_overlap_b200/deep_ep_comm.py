@@ -71,9 +71,21 @@ class DispatchResult:
     handle: object
     event: object
     expert_offsets: Optional[torch.Tensor] = None
-    num_recv_tokens_per_expert: Optional[torch.Tensor] = None
     recv_src: Optional[torch.Tensor] = None
     extra: dict = field(default_factory=dict)
+    _per_expert: Optional[torch.Tensor] = field(default=None, repr=False)
+
+    @property
+    def num_recv_tokens_per_expert(self) -> Optional[torch.Tensor]:
+        """Rows per local expert (int32), computed on first access on the caller's
+        current stream, after it has waited for the dispatch (no launch otherwise)."""
+        if self._per_expert is None and self.expert_offsets is not None:
+            ev = getattr(self.event, "event", None)
+            if ev is not None:
+                torch.cuda.current_stream(self.expert_offsets.device).wait_event(ev)
+            offs = self.expert_offsets
+            self._per_expert = offs[1:] - offs[:-1]
+        return self._per_expert
 
 
 def exchange_buffers(group, rank: int, world: int, own_base: int, export_handle,
@@ -212,7 +224,6 @@ class DeepEPDispatcher:
             self._ep.dispatch(xc, ic, wc, slot, epoch, num_sms or self.num_sms, pad, self.wait_ns,
                               self._status, expert_alignment, scale_rows)
             offs = self._ep.slots[slot].expert_offsets
-            per_expert = offs[1:] - offs[:-1]
             event = torch.cuda.Event()
             event.record(stream)
         if not inline:
@@ -230,7 +241,6 @@ class DeepEPDispatcher:
             handle=handle,
             event=EventOverlap(event),
             expert_offsets=offs,
-            num_recv_tokens_per_expert=per_expert,
             recv_src=views.recv_src[:rows],
         )
 

@@ -64,6 +64,8 @@ def main() -> None:
             if exact:
                 assert res.recv_x.shape[0] == n, (res.recv_x.shape, n)
             assert np.array_equal(res.expert_offsets.cpu().numpy(), mine["offsets"])
+            assert np.array_equal(res.num_recv_tokens_per_expert.cpu().numpy(),
+                                  np.diff(mine["offsets"]))
             assert np.array_equal(to_storage(res.recv_x[:n]), mine["x"])
             assert np.array_equal(res.recv_topk_idx[:n].cpu().numpy(), mine["topk_idx"])
             assert np.array_equal(res.recv_topk_weights[:n].cpu().numpy(), mine["topk_weights"])
