@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this directory from the reference's own code.
 
-Run in a container where the reference checkout is available (default
-``/root/reference``; override with ``MOE_REFERENCE_SRC``):
+Run where a checkout of the reference is available, with MOE_REFERENCE_SRC
+naming its ``src`` directory:
 
-    python tests/golden/make_golden.py
+    MOE_REFERENCE_SRC=<checkout>/src python tests/golden/make_golden.py
 
 It imports ``src/triton_grouped_gemm.py`` of Hongyu15/moe-overlap and records,
 on the CPU:
@@ -33,10 +33,12 @@ sys.dont_write_bytecode = True
 
 from tests._inputs import gemm_inputs, to_storage  # noqa: E402
 
-REF_SRC = Path(os.environ.get("MOE_REFERENCE_SRC", "/root/reference/src"))
+REF_SRC = Path(os.environ["MOE_REFERENCE_SRC"]) if "MOE_REFERENCE_SRC" in os.environ else None
 
 
 def _import_reference():
+    if REF_SRC is None:
+        raise SystemExit("set MOE_REFERENCE_SRC to the reference checkout's src directory")
     sys.path.insert(0, str(REF_SRC))
     import triton_grouped_gemm as tg  # noqa: PLC0415
 

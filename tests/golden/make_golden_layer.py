@@ -1,9 +1,9 @@
 """Golden vectors for the MoE layer, produced by the reference's own SimpleMoE.
 
-Run where the reference checkout is available (default /root/reference;
-override with MOE_REFERENCE_SRC):
+Run where a checkout of the reference is available, with MOE_REFERENCE_SRC
+naming its ``src`` directory:
 
-    python tests/golden/make_golden_layer.py
+    MOE_REFERENCE_SRC=<checkout>/src python tests/golden/make_golden_layer.py
 
 Records, on the CPU in fp32:
   * the single-process routed path (src/train_moe_baseline.py:342-348,
@@ -28,11 +28,13 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF_SRC = Path(os.environ.get("MOE_REFERENCE_SRC", "/root/reference/src"))
+REF_SRC = Path(os.environ["MOE_REFERENCE_SRC"]) if "MOE_REFERENCE_SRC" in os.environ else None
 H, F, E, TOPK, T = 32, 64, 8, 2, 128
 
 
 def _import_ref():
+    if REF_SRC is None:
+        raise SystemExit("set MOE_REFERENCE_SRC to the reference checkout's src directory")
     sys.path.insert(0, str(REF_SRC))
     sys.dont_write_bytecode = True
     import train_moe_baseline as tmb  # noqa: PLC0415
