@@ -90,10 +90,13 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(LAYER_WORKLOADS),
                     default="gemm_cfg2")
-    ap.add_argument("--comm-sms", type=int, default=48,
-                    help="layer workloads: SM budget (grid) of the dispatch/combine kernels")
+    ap.add_argument("--comm-sms", type=int, default=148,
+                    help="layer workloads: blocks of the dispatch/combine kernels (one per SM "
+                         "by default; they run beside the persistent GEMM CTAs)")
     ap.add_argument("--micro-batch", type=int, default=4096,
                     help="layer workloads: tokens per pipelined chunk")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="layer_train: time eager steps instead of a captured CUDA graph")
     ap.add_argument("--taper", action="store_true",
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
@@ -525,26 +528,7 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize(device)
     mo.check_status(device, sync=True)
 
-    sampler = ClockSampler(device)
-    sampler.start()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        probs, idx = step(x, dout)
-    end.record()
-    torch.cuda.synchronize(device)
-    clocks = sampler.stop()
-    mo.check_status(device, sync=True)
-    step_ms = start.elapsed_time(end) / args.steps
-    t = torch.tensor([step_ms], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms = float(t.item())
-
-    # Per-phase device times of one more step (phase boundaries on the compute stream).
+    # Per-phase device times of one eager step (phase boundaries on the compute stream).
     def mark(name):
         ev = torch.cuda.Event(enable_timing=True)
         ev.record()
@@ -559,6 +543,48 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
     phases = {}
     for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
         phases["router_fwd" if name == "start" else name] = round(a.elapsed_time(b), 4)
+
+    # The timed steps replay the whole step as one CUDA graph (device-drawn exchange
+    # epochs), unless --no-graph; a failed capture falls back to eager steps.
+    graph, graph_note = None, None
+    if not args.no_graph:
+        try:
+            from moe_overlap_b200.layer import TrainStepGraph
+
+            graph = TrainStepGraph(layer, x, dout)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize(device)
+            mo.check_status(device, sync=True)
+        except Exception as exc:  # report and time eager steps instead
+            graph = None
+            graph_note = f"capture failed ({type(exc).__name__}: {exc})"[:240]
+            torch.cuda.synchronize(device)
+
+    def timed_step():
+        if graph is not None:
+            graph.replay()
+            return graph.probs, graph.topk_idx
+        return step(x, dout)
+
+    sampler = ClockSampler(device)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        probs, idx = timed_step()
+    end.record()
+    torch.cuda.synchronize(device)
+    clocks = sampler.stop()
+    mo.check_status(device, sync=True)
+    step_ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([step_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
 
     stats = layer.stats(probs, idx)
     rows = T * K
@@ -578,12 +604,19 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for _ in range(n_e2e):
-            xd.copy_(xh, non_blocking=True)
-            gd.copy_(gh, non_blocking=True)
-            xd.requires_grad_(True)
-            _, idx_e = step(xd, gd)
+            if graph is not None:
+                with torch.no_grad():
+                    x.copy_(xh, non_blocking=True)
+                    dout.copy_(gh, non_blocking=True)
+                graph.replay()
+                idx_e = graph.topk_idx
+            else:
+                xd.copy_(xh, non_blocking=True)
+                gd.copy_(gh, non_blocking=True)
+                xd.requires_grad_(True)
+                _, idx_e = step(xd, gd)
+                xd = xd.detach()
             counts_h.copy_(torch.bincount(idx_e.reshape(-1), minlength=E), non_blocking=True)
-            xd = xd.detach()
         e2.record()
         torch.cuda.synchronize(device)
         e2e_ms = s2.elapsed_time(e2) / n_e2e
@@ -617,6 +650,7 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
             "config": {"workload": args.workload, "description": cfg["desc"], "tokens_per_rank": T,
                        "comm_sms": args.comm_sms, "l2": "working set (weights 1 GiB, activations) > L2",
+                       "cuda_graph": graph is not None, "cuda_graph_note": graph_note,
                        "parallelism": "replicas" if world > 1 else "single"},
             "expert_load_cv": round(stats.load_cv, 4),
             "router_entropy": round(stats.entropy, 4),

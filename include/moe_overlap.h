@@ -231,7 +231,13 @@ MOE_API int32_t moe_expert_offsets_host(const void* counts, int32_t counts_int64
  * expert_offsets on the device.  Two slots alternate between consecutive
  * dispatches; at most two dispatches may be outstanding (not yet combined).
  * Every call takes an `epoch` (1, 2, 3, ... in call order, the same on every
- * rank) and a `slot` (the epoch's parity, by convention).
+ * rank) and a `slot` (the epoch's parity, by convention).  Epoch 0 means "draw
+ * it on the device": the dispatch's first kernel takes the endpoint's device
+ * counter + 1 and every later kernel of that dispatch and of its combine reads
+ * it, so a captured CUDA graph replays with fresh epochs.  Set the counter to the
+ * last host epoch with moe_ep_set_device_epoch before the first such call, keep
+ * the host's slot alternation, and capture an even number of dispatches so that
+ * every replay leaves the slot parity unchanged.
  */
 #define MOE_EP_MAX_RANKS 64
 
@@ -301,6 +307,9 @@ MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_
                                 int32_t slot, uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
                                 int32_t expert_alignment, int32_t scale_rows, uint64_t wait_ns,
                                 int32_t* status, void* stream);
+
+/* Sets the endpoint's device epoch counter (stream-ordered; see epoch 0 above). */
+MOE_API int32_t moe_ep_set_device_epoch(moe_ep_t ep, uint64_t epoch, void* stream);
 
 /*
  * Combine, in two phases (moe_ep_combine runs both):

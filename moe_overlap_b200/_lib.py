@@ -131,6 +131,7 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_combine": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _c_void_p, _i32,
                _u64, _c_void_p, _c_void_p]),
+    "moe_ep_set_device_epoch": (_i32, [_c_void_p, ctypes.c_uint64, _c_void_p]),
     "moe_router_topk": (
         _i32,
         [_c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32,  # logits, dtype, bias, T, E, k, renorm

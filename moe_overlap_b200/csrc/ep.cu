@@ -106,6 +106,8 @@ struct Endpoint {
   int32_t* offsets[2] = {};         // [per_rank+1] receiver expert offsets
   int32_t* my_counts = nullptr;     // [E]
   unsigned int* done_ctr = nullptr; // blocks finished in the current scatter
+  uint64_t* epoch_ctr = nullptr;    // device-side epoch counter (epoch 0 = use it)
+  uint64_t* slot_epoch = nullptr;   // [2] epoch the last dispatch into each slot drew
   int max_blocks = 0;
   int64_t* host_info = nullptr;     // mapped pinned: [2][2] {epoch, total rows}
   int device = 0;
@@ -131,6 +133,8 @@ struct Params {
   int32_t* offsets_out;
   int32_t* my_counts;
   unsigned int* done_ctr;
+  uint64_t* epoch_ctr;
+  uint64_t* slot_epoch;
   int num_layout_blocks;
   int pad_rows;  // fill recv_topk_idx rows past the received count with -1
   int align;     // receive segments of each local expert rounded up to this many rows
@@ -144,6 +148,13 @@ struct Params {
 template <typename T>
 __device__ __forceinline__ T* at(uint8_t* base, uint64_t off) {
   return reinterpret_cast<T*>(base + off);
+}
+
+// The epoch of the dispatch a kernel belongs to: the host's, or with host epoch 0
+// the one that dispatch's count kernel drew from this endpoint's device counter,
+// so that a captured CUDA graph replays with fresh epochs.
+__device__ __forceinline__ uint64_t kernel_epoch(const Params& p) {
+  return p.epoch != 0 ? p.epoch : *reinterpret_cast<const volatile uint64_t*>(p.slot_epoch + p.slot);
 }
 
 // Bounded wait until flag >= epoch.  Returns false on timeout.
@@ -213,6 +224,16 @@ __global__ void __launch_bounds__(kLayoutThreads) layout_kernel(Params p) {
 // count matrix for this slot), then raise this rank's count flag there.
 __global__ void count_kernel(Params p) {
   const int E = p.num_experts;
+  __shared__ uint64_t epoch_sh;
+  if (threadIdx.x == 0) {
+    uint64_t e = p.epoch;
+    if (e == 0) {  // draw this dispatch's epoch on the device
+      e = *p.epoch_ctr + 1;
+      *p.epoch_ctr = e;
+      p.slot_epoch[p.slot] = e;
+    }
+    epoch_sh = e;
+  }
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int run = 0;
     for (int b = 0; b < p.num_layout_blocks; ++b) {
@@ -232,7 +253,7 @@ __global__ void count_kernel(Params p) {
   __syncthreads();
   if (threadIdx.x < p.world) {
     uint64_t* f = at<uint64_t>(p.peers[threadIdx.x], p.lay.count_flag) + p.slot * p.world + p.rank;
-    st_release_sys(f, p.epoch);
+    st_release_sys(f, epoch_sh);
   }
 }
 
@@ -291,7 +312,7 @@ __device__ void build_count_view(const Params& p, CountView& cv) {
 __device__ __forceinline__ bool wait_all_flags(const Params& p, uint64_t off, int* fail) {
   if (threadIdx.x < p.world) {
     const uint64_t* f = at<uint64_t>(p.peers[p.rank], off) + p.slot * p.world + threadIdx.x;
-    if (!wait_flag(f, p.epoch, p.wait_ns)) atomicOr(fail, 1);
+    if (!wait_flag(f, kernel_epoch(p), p.wait_ns)) atomicOr(fail, 1);
   }
   __syncthreads();
   return *fail == 0;
@@ -323,7 +344,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
       volatile int64_t* hi = p.host_info + 2 * p.slot;
       hi[1] = overflow ? -1 : cv.recv_total;
       __threadfence_system();
-      hi[0] = static_cast<int64_t>(p.epoch);
+      hi[0] = static_cast<int64_t>(kernel_epoch(p));
     }
   }
 
@@ -429,7 +450,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
       __threadfence_system();
       for (int d = 0; d < p.world; ++d)
         st_release_sys(at<uint64_t>(p.peers[d], p.lay.data_flag) + p.slot * p.world + p.rank,
-                       p.epoch);
+                       kernel_epoch(p));
     }
   }
 }
@@ -448,7 +469,7 @@ __global__ void ready_kernel(Params p) {
   __syncthreads();
   if (threadIdx.x < p.world)
     st_release_sys(at<uint64_t>(p.peers[threadIdx.x], p.lay.ready_flag) + p.slot * p.world + p.rank,
-                   p.epoch);
+                   kernel_epoch(p));
 }
 
 __device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, float s) {
@@ -634,6 +655,8 @@ static Params base_params(const Endpoint* ep, int slot, uint64_t epoch, uint64_t
   p.cap_rows = ep->cap_rows;
   p.slot = slot;
   p.epoch = epoch;
+  p.epoch_ctr = ep->epoch_ctr;
+  p.slot_epoch = ep->slot_epoch;
   p.wait_ns = wait_ns;
   p.status = status;
   return p;
@@ -723,8 +746,22 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   }
   ep->my_counts = reinterpret_cast<int32_t*>(ep->scratch + o_cnt);
   ep->done_ctr = reinterpret_cast<unsigned int*>(ep->scratch + o_done);
+  ep->epoch_ctr = reinterpret_cast<uint64_t*>(ep->scratch + o_done + 8);
+  ep->slot_epoch = reinterpret_cast<uint64_t*>(ep->scratch + o_done + 16);
   *out = ep;
   return MOE_OK;
+}
+
+namespace moe {
+namespace ep {
+__global__ void set_epoch_kernel(uint64_t* ctr, uint64_t epoch) { *ctr = epoch; }
+}  // namespace ep
+}  // namespace moe
+
+extern "C" int32_t moe_ep_set_device_epoch(moe_ep_t ep, uint64_t epoch, void* stream) {
+  if (ep == nullptr) return MOE_ERR_INVALID_ARG;
+  moe::ep::set_epoch_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(ep->epoch_ctr, epoch);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
 extern "C" int32_t moe_ep_destroy(moe_ep_t ep) {
@@ -778,7 +815,7 @@ extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64
                                          int32_t topk, int32_t slot, uint64_t epoch,
                                          int32_t* status, void* stream_) {
   using namespace moe::ep;
-  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
+  if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk ||
       (num_tokens > 0 && (x == nullptr || topk_idx == nullptr || topk_weights == nullptr)) ||
       !moe::aligned16(x))
@@ -810,7 +847,7 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
                                            int32_t expert_alignment, int32_t scale_rows,
                                            uint64_t wait_ns, int32_t* status, void* stream_) {
   using namespace moe::ep;
-  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
+  if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
       expert_alignment < 1 || expert_alignment > 4096)
     return MOE_ERR_INVALID_ARG;
@@ -840,7 +877,7 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
 extern "C" int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch, uint64_t wait_ns,
                                        int32_t* status, void* stream_) {
   using namespace moe::ep;
-  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0) return MOE_ERR_INVALID_ARG;
+  if (ep == nullptr || slot < 0 || slot > 1) return MOE_ERR_INVALID_ARG;
   Params p = base_params(ep, slot, epoch, wait_ns, status);
   wait_data_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream_)>>>(p);
   return check_launch();
@@ -848,7 +885,7 @@ extern "C" int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch
 
 extern "C" int32_t moe_ep_combine_begin(moe_ep_t ep, int32_t slot, uint64_t epoch, void* stream_) {
   using namespace moe::ep;
-  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0) return MOE_ERR_INVALID_ARG;
+  if (ep == nullptr || slot < 0 || slot > 1) return MOE_ERR_INVALID_ARG;
   Params p = base_params(ep, slot, epoch, 0, nullptr);
   ready_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream_)>>>(p);
   return check_launch();
@@ -860,7 +897,7 @@ extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
                                       int32_t num_blocks, uint64_t wait_ns, int32_t* status,
                                       void* stream_) {
   using namespace moe::ep;
-  if (ep == nullptr || slot < 0 || slot > 1 || epoch == 0 || num_tokens < 0 ||
+  if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
       (num_tokens > 0 && (out == nullptr || topk_idx == nullptr)) || !moe::aligned16(out) ||
       (weighted && num_tokens > 0 && topk_weights == nullptr))

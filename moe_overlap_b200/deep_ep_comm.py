@@ -156,6 +156,7 @@ class DeepEPDispatcher:
             dist.barrier(group=group)
         self.comm_stream = torch.cuda.Stream(self.device)
         self._epoch = 0
+        self._device_epochs = False
         self._outstanding: collections.deque[DispatchHandle] = collections.deque()
         self._status = _lib.status_word(self.device)
 
@@ -207,6 +208,8 @@ class DeepEPDispatcher:
         if len(self._outstanding) >= 2:
             raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
         exact = self.exact_size if exact_size is None else exact_size
+        if exact and self._device_epochs:
+            raise ValueError("exact_size needs host epochs; with device epochs use expert_offsets")
         _lib.check_status(self.device)
         self._epoch += 1
         epoch, slot = self._epoch, self._epoch % 2
@@ -221,12 +224,13 @@ class DeepEPDispatcher:
             # marks the rows past the received count (-1 ids, zero weights) so the
             # views read like DeepEP's.  Callers that use expert_offsets can skip it.
             pad = (not exact) if pad_rows is None else bool(pad_rows)
-            self._ep.dispatch(xc, ic, wc, slot, epoch, num_sms or self.num_sms, pad, self.wait_ns,
+            self._ep.dispatch(xc, ic, wc, slot, 0 if self._device_epochs else epoch,
+                              num_sms or self.num_sms, pad, self.wait_ns,
                               self._status, expert_alignment, scale_rows)
             offs = self._ep.slots[slot].expert_offsets
             event = torch.cuda.Event()
             event.record(stream)
-        if not inline:
+        if not inline and not torch.cuda.is_current_stream_capturing():
             for t in (x, topk_idx, topk_weights):
                 t.record_stream(self.comm_stream)
         views = self._ep.slots[slot]
@@ -243,6 +247,27 @@ class DeepEPDispatcher:
             expert_offsets=offs,
             recv_src=views.recv_src[:rows],
         )
+
+    def use_device_epochs(self) -> None:
+        """Switch the exchange kernels to epochs drawn on the device (graph-capturable).
+
+        Collective in effect: every rank must switch before the same dispatch.  The
+        device counter starts at the last host epoch, the host keeps alternating
+        slots, and a captured region must hold an even number of dispatches so that
+        replays leave the slot parity unchanged (layer.TrainStepGraph checks this).
+        Receive sizes then come only from ``expert_offsets`` (``exact_size`` is not
+        available: the host cannot know a replayed dispatch's epoch).
+        """
+        if self._device_epochs:
+            return
+        torch.cuda.synchronize(self.device)
+        self._ep.set_device_epoch(self._epoch)
+        torch.cuda.synchronize(self.device)
+        self._device_epochs = True
+
+    @property
+    def device_epochs(self) -> bool:
+        return self._device_epochs
 
     @property
     def last_epoch(self) -> int:
@@ -300,11 +325,13 @@ class DeepEPDispatcher:
                 if rows > views.expert_out.shape[0]:
                     raise ValueError("expert_out has more rows than the receive buffer")
                 views.expert_out[:rows].copy_(expert_out)
-            self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot, handle.epoch,
+            self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot,
+                             0 if self._device_epochs else handle.epoch,
                              weighted, out, num_sms or self.num_sms, self.wait_ns, self._status)
             event = torch.cuda.Event()
             event.record(stream)
-        if not inline:
+        # (under CUDA-graph capture the graph keeps its memory; nothing to record)
+        if not inline and not torch.cuda.is_current_stream_capturing():
             expert_out.record_stream(self.comm_stream)
             out.record_stream(self.comm_stream)
         handle.combined = True

@@ -215,6 +215,12 @@ class Endpoint:
                                     wait_ns, status.data_ptr(), self._stream()),
             "moe_ep_combine")
 
+    def set_device_epoch(self, epoch: int) -> None:
+        """Sets the device epoch counter (on the current stream): kernels called with
+        epoch 0 draw epoch + 1, + 2, ... on the device."""
+        _lib.check_call(self.lib.moe_ep_set_device_epoch(self.handle, int(epoch), self._stream()),
+                        "moe_ep_set_device_epoch")
+
     def received_rows(self, slot: int, epoch: int, timeout_s: float = 60.0) -> int:
         """Rows received in ``slot`` for ``epoch``, read from mapped host memory.
 
@@ -262,10 +268,19 @@ class LocalGroup:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.eps[0].device)
         self.wait_ns = default_wait_ns()
 
+    def use_device_epochs(self) -> None:
+        """Later phases pass epoch 0: every endpoint draws its epochs on the device."""
+        for ep in self.eps:
+            ep.set_device_epoch(self.epoch)
+        self.device_epochs = True
+
+    def _kernel_epoch(self, epoch: int) -> int:
+        return 0 if getattr(self, "device_epochs", False) else epoch
+
     def dispatch(self, xs, idxs, ws, pad_rows: bool = False, expert_alignment: int = 1,
                  scale_rows: bool = False):
         self.epoch += 1
-        slot, epoch = self.epoch % 2, self.epoch
+        slot, epoch = self.epoch % 2, self._kernel_epoch(self.epoch)
         for r, ep in enumerate(self.eps):
             ep.dispatch_begin(xs[r], idxs[r], ws[r], slot, epoch, self.status)
         for r, ep in enumerate(self.eps):
@@ -276,6 +291,7 @@ class LocalGroup:
         return slot, epoch
 
     def combine(self, idxs, ws, slot, epoch, weighted, outs):
+        epoch = self._kernel_epoch(epoch)
         for ep in self.eps:
             ep.combine_begin(slot, epoch)
         for r, ep in enumerate(self.eps):

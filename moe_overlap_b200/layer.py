@@ -363,3 +363,51 @@ class RoutedExperts(torch.autograd.Function):
         dx, dw, dw1, dw2 = ctx.layer._train_backward(ctx.state, dout)
         ctx.state = None
         return dx, dw, dw1, dw2, None, None
+
+
+class TrainStepGraph:
+    """One training step of ``layer`` (forward_autograd + backward) as a CUDA graph.
+
+    ``x`` and ``dout`` are the static inputs: copy each step's data into them
+    (under ``torch.no_grad()``) and call ``replay()``.  After a replay ``out``,
+    ``probs``, ``topk_idx``, ``x.grad`` and the parameters' ``.grad`` hold that
+    step's results (written in place, not accumulated).  The exchange switches to
+    device-drawn epochs (DeepEPDispatcher.use_device_epochs) so that every replay
+    runs with fresh ones; a step holds two dispatches, which keeps the slot
+    alternation aligned across replays.  With a process group, every rank must
+    build and replay its graph in step.
+    """
+
+    def __init__(self, layer: MoELayer, x: torch.Tensor, dout: torch.Tensor, warmup: int = 2):
+        self.layer, self.x, self.dout = layer, x, dout
+        disp = layer.dispatcher
+        disp.use_device_epochs()
+        self.params = [p for p in (layer.router_w, layer.router_b, layer.w1, layer.w2)
+                       if p is not None and p.requires_grad]
+        cur = torch.cuda.current_stream(layer.device)
+        side = torch.cuda.Stream(layer.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                self._clear_grads()
+                out, _, _ = layer.forward_autograd(x)
+                out.backward(dout)
+        cur.wait_stream(side)
+        torch.cuda.synchronize(layer.device)
+        self._clear_grads()
+        e0 = disp.last_epoch
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out, self.probs, self.topk_idx = layer.forward_autograd(x)
+            self.out.backward(dout)
+        if (disp.last_epoch - e0) % 2 != 0:
+            raise RuntimeError("a captured training step must hold an even number of dispatches")
+
+    def _clear_grads(self) -> None:
+        for p in self.params:
+            p.grad = None
+        if self.x.requires_grad:
+            self.x.grad = None
+
+    def replay(self) -> None:
+        self.graph.replay()

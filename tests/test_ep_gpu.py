@@ -233,3 +233,39 @@ def test_scale_rows_and_topk_weight_grad_match_oracle(cuda_device, world):
             assert np.all(got[send_pos[r] < 0] == 0.0)
     finally:
         grp.close()
+
+
+def test_device_epochs_match_the_oracle(cuda_device):
+    """Epoch 0 (drawn on the device, the graph-capturable mode): after two host-epoch
+    dispatches, three more with device epochs move the same rows and combine bit-exactly."""
+    world, tokens, topk, hidden, E = 4, 211, 2, 128, 8
+    grp = LocalGroup(world, E, hidden, tokens, topk, world * tokens * topk, num_blocks=5)
+    try:
+        for it in range(5):
+            if it == 2:
+                grp.use_device_epochs()
+            xs, idxs, ws = routing(world, tokens, E, topk, seed=300 + it, hidden=hidden)
+            di = [i.to(cuda_device) for i in idxs]
+            dw = [w.to(cuda_device) for w in ws]
+            slot, epoch = grp.dispatch([x.to(cuda_device) for x in xs], di, dw)
+            recv, send_pos = oep.dispatch([to_storage(x) for x in xs], [i.numpy() for i in idxs],
+                                          [w.numpy() for w in ws], E)
+            ys = []
+            for d, ep in enumerate(grp.eps):
+                n = int(recv[d]["offsets"][-1])
+                assert np.array_equal(ep.slots[slot].expert_offsets.cpu().numpy(), recv[d]["offsets"])
+                assert np.array_equal(to_storage(ep.slots[slot].recv_x[:n]), recv[d]["x"])
+                y = (ep.slots[slot].recv_x[:n].float() * 2.0 + 1.0).to(torch.bfloat16)
+                ep.slots[slot].expert_out[:n].copy_(y)
+                ys.append(to_storage(y))
+            outs = [torch.empty(tokens, hidden, dtype=torch.bfloat16, device=cuda_device)
+                    for _ in range(world)]
+            grp.combine(di, dw, slot, epoch, True, outs)
+            torch.cuda.synchronize()
+            assert int(grp.status.item()) == 0, it
+            want = oep.combine(ys, [i.numpy() for i in idxs], send_pos, E,
+                               weights=[w.numpy() for w in ws])
+            for r in range(world):
+                assert np.array_equal(to_storage(outs[r]), want[r]), (it, r)
+    finally:
+        grp.close()

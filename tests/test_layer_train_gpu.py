@@ -150,3 +150,44 @@ def test_backward_after_another_dispatch_is_rejected(cuda_device):
     torch.cuda.synchronize()
     assert layer.w1.grad is not None and torch.isfinite(layer.w1.grad.float()).all()
     layer.close()
+
+
+def test_train_step_graph_replays_the_eager_step(cuda_device):
+    """A training step captured as a CUDA graph (device-drawn exchange epochs) gives the
+    eager step's results on the same data, replay after replay and for new data."""
+    from moe_overlap_b200.layer import TrainStepGraph
+
+    tokens, hidden, ffn, experts, topk = 1024, 256, 512, 8, 2
+    layer = _trainable(MoELayer(hidden, ffn, experts, topk, renormalize=True, micro_batch_size=tokens,
+                                num_comm_sms=8, training=True).init_random(std=0.05, seed=13))
+    g = torch.Generator().manual_seed(31)
+    batches = [(torch.randn(tokens, hidden, generator=g).to(torch.bfloat16),
+                torch.randn(tokens, hidden, generator=g).to(torch.bfloat16)) for _ in range(2)]
+
+    def eager(xh, dh):
+        for p in (layer.router_w, layer.w1, layer.w2):
+            p.grad = None
+        x = xh.to(cuda_device).requires_grad_(True)
+        out, _, idx = layer.forward_autograd(x)
+        out.backward(dh.to(cuda_device))
+        torch.cuda.synchronize()
+        return [t.detach().clone() for t in (out, idx, x.grad, layer.router_w.grad, layer.w1.grad,
+                                             layer.w2.grad)]
+
+    want = [eager(xh, dh) for xh, dh in batches]
+    xs = batches[0][0].to(cuda_device).requires_grad_(True)
+    ds = batches[0][1].to(cuda_device)
+    step = TrainStepGraph(layer, xs, ds)
+    for rep, (xh, dh) in enumerate([batches[0], batches[1], batches[0]]):
+        with torch.no_grad():
+            xs.copy_(xh.to(cuda_device))
+            ds.copy_(dh.to(cuda_device))
+        step.replay()
+        torch.cuda.synchronize()
+        w = want[0 if rep != 1 else 1]
+        got = [step.out, step.topk_idx, xs.grad, layer.router_w.grad, layer.w1.grad, layer.w2.grad]
+        assert torch.equal(got[0], w[0]) and torch.equal(got[1], w[1]), rep
+        for gt, wt in zip(got[2:], w[2:]):
+            assert torch.allclose(gt.float(), wt.float(), rtol=1e-2, atol=1e-3), rep
+        assert torch.equal(got[4], w[4]) and torch.equal(got[5], w[5]), rep  # our GEMMs: bitwise
+    layer.close()
