@@ -308,6 +308,32 @@ MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_
                                 int32_t expert_alignment, int32_t scale_rows, uint64_t wait_ns,
                                 int32_t* status, void* stream);
 
+/*
+ * Fused down-projection + combine push: the grouped GEMM C = A @ B[e] over this
+ * rank's received rows (expert_offsets of `slot`, experts = num_experts/world,
+ * n = hidden, bf16), whose epilogue writes each result row straight into the
+ * combine rows of the token's source rank (peer memory, row src_token * max_topk +
+ * slot) instead of a local buffer; then this rank raises its ready flag in every
+ * rank.  A = the expert hidden rows [m_total, k] (the receive layout), B as in
+ * moe_grouped_gemm.  With moe_ep_combine_pushed this replaces expert_out +
+ * moe_ep_combine: the all-to-all back overlaps the GEMM tile by tile, and the
+ * combine becomes a local reduce (src/deep_ep_comm.py:107-115 moves the same rows).
+ */
+MOE_API int32_t moe_ep_push_gemm(moe_ep_t ep, const void* a, int64_t lda, const void* b,
+                                 int64_t b_stride_e, int64_t b_stride_k, int64_t b_stride_n,
+                                 int64_t m_total, int64_t k, int32_t dtype, int32_t num_sms,
+                                 int32_t use_atomic_queue, int32_t* work_counter, int32_t slot,
+                                 uint64_t epoch, int32_t* status, void* stream);
+
+/* The combine of rows pushed by moe_ep_push_gemm: waits for every owner's ready
+ * flag, then reduces this rank's combine rows as moe_ep_combine_end does (same
+ * arguments, same fp32 slot-order sum, bit-identical result). */
+MOE_API int32_t moe_ep_combine_pushed(moe_ep_t ep, const int64_t* topk_idx,
+                                      const float* topk_weights, int32_t num_tokens,
+                                      int32_t topk, int32_t slot, uint64_t epoch,
+                                      int32_t weighted, void* out, int32_t num_blocks,
+                                      uint64_t wait_ns, int32_t* status, void* stream);
+
 /* Sets the endpoint's device epoch counter (stream-ordered; see epoch 0 above). */
 MOE_API int32_t moe_ep_set_device_epoch(moe_ep_t ep, uint64_t epoch, void* stream);
 

@@ -132,6 +132,17 @@ SIGNATURES: dict[str, tuple] = {
         _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _c_void_p, _i32,
                _u64, _c_void_p, _c_void_p]),
     "moe_ep_set_device_epoch": (_i32, [_c_void_p, ctypes.c_uint64, _c_void_p]),
+    "moe_ep_push_gemm": (
+        _i32,
+        [_c_void_p, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64,  # ep, a, lda, b, strides e/k/n
+         _i64, _i64, _i32, _i32, _i32, _c_void_p,  # m_total, k, dtype, num_sms, atomic, counter
+         _i32, ctypes.c_uint64, _c_void_p, _c_void_p],  # slot, epoch, status, stream
+    ),
+    "moe_ep_combine_pushed": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, ctypes.c_uint64,  # ep, idx, w, T, k, slot, epoch
+         _i32, _c_void_p, _i32, ctypes.c_uint64, _c_void_p, _c_void_p],  # weighted, out, blocks, wait, status, stream
+    ),
     "moe_router_topk": (
         _i32,
         [_c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32,  # logits, dtype, bias, T, E, k, renorm

@@ -35,6 +35,7 @@
 #include <new>
 
 #include "../../include/moe_overlap.h"
+#include "gemm_common.cuh"
 #include "host_common.h"
 
 namespace moe {
@@ -80,7 +81,10 @@ struct SlotLayout {
   uint64_t topk_idx;   // [cap][max_topk] int64
   uint64_t topk_w;     // [cap][max_topk] float
   uint64_t src;        // [cap] int2 {src_rank, src_token}
+  uint64_t dst;        // [cap] int32: src_token * max_topk + slot (-1 for padding rows)
   uint64_t counts;     // [world][num_experts] int32
+  uint64_t cb;         // [max_tokens * max_topk][hidden] bf16: this rank's tokens' expert
+                       // outputs, pushed here by their owners' GEMM epilogue
 };
 
 struct SymLayout {
@@ -143,6 +147,7 @@ struct Params {
   // combine
   __nv_bfloat16* out;
   int weighted;
+  int pushed;  // combine reads the rows the owners pushed here instead of pulling them
 };
 
 template <typename T>
@@ -381,6 +386,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
         }
         if (lane == 0) {
           at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
+          at<int32_t>(peer, sl.dst)[row] = t * p.max_topk + j;
           p.send_pos[a] = row;
         }
       }
@@ -420,6 +426,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
               at<float>(me, sl.topk_w)[r * p.max_topk + j] = 0.0f;
             }
             at<int2>(me, sl.src)[r] = make_int2(-1, -1);
+            at<int32_t>(me, sl.dst)[r] = -1;
           }
         }
       }
@@ -539,8 +546,14 @@ __global__ void __launch_bounds__(kPullThreads, kCommMinBlocks) pull_kernel(Para
       const int a = t * p.topk + j;
       const int row = p.send_pos[a];
       if (row < 0) continue;
-      const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
-      srcs[ns] = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
+      if (p.pushed) {
+        // The owner's GEMM pushed this (token, slot) row into our combine rows.
+        srcs[ns] = at<const uint4>(p.peers[p.rank], sl.cb) +
+                   (static_cast<int64_t>(t) * p.max_topk + j) * nvec;
+      } else {
+        const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
+        srcs[ns] = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
+      }
       scale[ns] = p.weighted ? p.topk_w[a] : 1.0f;
       ++ns;
     }
@@ -613,7 +626,8 @@ __global__ void expert_count_kernel(const int64_t* topk_idx, int64_t assigns, in
 // -------------------------------------------------------------------- host --
 static uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
-static SymLayout plan(int world, int num_experts, int hidden, int max_topk, int64_t cap) {
+static SymLayout plan(int world, int num_experts, int hidden, int max_topk, int64_t cap,
+                      int max_tokens) {
   SymLayout L{};
   uint64_t off = 0;
   for (int s = 0; s < 2; ++s) {
@@ -628,8 +642,12 @@ static SymLayout plan(int world, int num_experts, int hidden, int max_topk, int6
     off = align_up(off + uint64_t(cap) * max_topk * 4, 256);
     sl.src = off;
     off = align_up(off + uint64_t(cap) * 8, 256);
+    sl.dst = off;
+    off = align_up(off + uint64_t(cap) * 4, 256);
     sl.counts = off;
     off = align_up(off + uint64_t(world) * num_experts * 4, 256);
+    sl.cb = off;
+    off = align_up(off + uint64_t(max_tokens) * max_topk * hidden * 2, 256);
   }
   L.count_flag = off;
   off = align_up(off + 2ull * world * 8, 256);
@@ -693,7 +711,7 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   ep->max_tokens = max_tokens;
   ep->max_topk = max_topk;
   ep->cap_rows = max_recv_rows;
-  ep->lay = plan(world, num_experts, hidden, max_topk, max_recv_rows);
+  ep->lay = plan(world, num_experts, hidden, max_topk, max_recv_rows, max_tokens);
   if (cudaGetDevice(&ep->device) != cudaSuccess) {
     delete ep;
     return MOE_ERR_CUDA;
@@ -891,11 +909,10 @@ extern "C" int32_t moe_ep_combine_begin(moe_ep_t ep, int32_t slot, uint64_t epoc
   return check_launch();
 }
 
-extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
-                                      const float* topk_weights, int32_t num_tokens, int32_t topk,
-                                      int32_t slot, uint64_t epoch, int32_t weighted, void* out,
-                                      int32_t num_blocks, uint64_t wait_ns, int32_t* status,
-                                      void* stream_) {
+static int32_t combine_reduce(moe_ep_t ep, const int64_t* topk_idx, const float* topk_weights,
+                              int32_t num_tokens, int32_t topk, int32_t slot, uint64_t epoch,
+                              int32_t weighted, void* out, int32_t num_blocks, uint64_t wait_ns,
+                              int32_t* status, void* stream_, int pushed) {
   using namespace moe::ep;
   if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
@@ -910,6 +927,7 @@ extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
   p.send_pos = ep->send_pos[slot];
   p.out = static_cast<__nv_bfloat16*>(out);
   p.weighted = weighted ? 1 : 0;
+  p.pushed = pushed;
   // The pass width bounds the registers a lane needs for all of a token's rows.
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int grid = num_blocks;
@@ -919,6 +937,53 @@ extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
     pull_kernel<2, 4><<<grid, kPullThreads, 0, stream>>>(p);
   else
     pull_kernel<1, 8><<<grid, kPullThreads, 0, stream>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_combine_end(moe_ep_t ep, const int64_t* topk_idx,
+                                      const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                      int32_t slot, uint64_t epoch, int32_t weighted, void* out,
+                                      int32_t num_blocks, uint64_t wait_ns, int32_t* status,
+                                      void* stream) {
+  return combine_reduce(ep, topk_idx, topk_weights, num_tokens, topk, slot, epoch, weighted, out,
+                        num_blocks, wait_ns, status, stream, 0);
+}
+
+extern "C" int32_t moe_ep_combine_pushed(moe_ep_t ep, const int64_t* topk_idx,
+                                         const float* topk_weights, int32_t num_tokens,
+                                         int32_t topk, int32_t slot, uint64_t epoch,
+                                         int32_t weighted, void* out, int32_t num_blocks,
+                                         uint64_t wait_ns, int32_t* status, void* stream) {
+  return combine_reduce(ep, topk_idx, topk_weights, num_tokens, topk, slot, epoch, weighted, out,
+                        num_blocks, wait_ns, status, stream, 1);
+}
+
+extern "C" int32_t moe_ep_push_gemm(moe_ep_t ep, const void* a, int64_t lda, const void* b,
+                                    int64_t b_stride_e, int64_t b_stride_k, int64_t b_stride_n,
+                                    int64_t m_total, int64_t k, int32_t dtype, int32_t num_sms,
+                                    int32_t use_atomic_queue, int32_t* work_counter, int32_t slot,
+                                    uint64_t epoch, int32_t* status, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || dtype != MOE_DTYPE_BF16 || m_total < 0 ||
+      m_total > ep->cap_rows)
+    return MOE_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const SlotLayout& sl = ep->lay.slot[slot];
+  moe::gg::PushTarget push;
+  push.src = reinterpret_cast<const int2*>(ep->sym + sl.src);
+  push.dst = reinterpret_cast<const int32_t*>(ep->sym + sl.dst);
+  push.peers = ep->d_peers;
+  push.cb = sl.cb;
+  if (m_total > 0) {
+    const int rc = moe::gg::grouped_gemm_launch(
+        a, lda, b, b_stride_e, b_stride_k, b_stride_n, nullptr, ep->hidden, ep->offsets[slot], 0,
+        m_total, k, ep->hidden, ep->per_rank, dtype, MOE_ACT_NONE, num_sms, use_atomic_queue,
+        work_counter, nullptr, nullptr, nullptr, 0, status, stream, &push);
+    if (rc != MOE_OK) return rc;
+  }
+  // Every owner raises its ready flag in every rank once its pushes have landed.
+  Params p = base_params(ep, slot, epoch, 0, nullptr);
+  ready_kernel<<<1, 64, 0, stream>>>(p);
   return check_launch();
 }
 

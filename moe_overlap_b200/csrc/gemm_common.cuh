@@ -15,6 +15,16 @@ namespace gg {
 
 constexpr int kMaxExperts = 1024;
 
+// Expert-parallel combine push: instead of C, row r of the result goes to
+// peers[src[r].x] + cb + dst[r] * ldc elements (the source rank's combine rows);
+// rows with src[r].x < 0 or dst[r] < 0 (alignment padding) are not stored.
+struct PushTarget {
+  const int2* src;         // [m_total] {source rank, token}; null = ordinary C stores
+  const int32_t* dst;      // [m_total] row index in the source rank's combine rows
+  uint8_t* const* peers;   // [world] every rank's symmetric buffer, as mapped here
+  uint64_t cb;             // byte offset of the combine rows in each buffer
+};
+
 struct Params {
   void* c;
   int64_t ldc;
@@ -35,6 +45,7 @@ struct Params {
   void* aux_out;           // aux_out[row, col] = v (before the activation)
   int64_t ld_aux;
   int c_tma;               // the CTA-pair kernel may store C through its TMA store map
+  PushTarget push;         // combine push instead of C (push.src != null)
 };
 
 __device__ __forceinline__ float gelu_erf(float x) {
@@ -91,7 +102,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const v
 // `rows_clipped_by_map`, when the map's row extent is the tile's own bound (rows past
 // it are dropped by the TMA unit).  Other warps store directly.  The caller drains
 // its bulk stores (bulk_wait_group0) before the CTA exits.
-template <bool BF16>
+template <bool BF16, bool PUSH = false>
 __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int lane, int row0,
                                                   int rows, int n0, const Params& p, int ch0 = 0,
                                                   int nch = 8, const void* tmap_c = nullptr,
@@ -99,9 +110,23 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
                                                   int e3 = -1) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int row_in_tile = quad * 32 + lane;
-  const bool row_ok = row_in_tile < rows;
+  bool row_ok = row_in_tile < rows;
   const int64_t grow = int64_t(row0) + row_in_tile;
-  T* crow = reinterpret_cast<T*>(p.c) + grow * p.ldc;
+  T* crow;
+  if constexpr (PUSH) {
+    // Combine push: this row's destination on its source rank (peer memory).
+    crow = nullptr;
+    if (row_ok) {
+      const int2 src = p.push.src[grow];
+      const int32_t dst = p.push.dst[grow];
+      if (src.x >= 0 && dst >= 0)
+        crow = reinterpret_cast<T*>(p.push.peers[src.x] + p.push.cb) + int64_t(dst) * p.ldc;
+      else
+        row_ok = false;
+    }
+  } else {
+    crow = reinterpret_cast<T*>(p.c) + grow * p.ldc;
+  }
   const float rs = (p.row_scale != nullptr && row_ok) ? p.row_scale[grow] : 1.0f;
   // DGELU and MUL_AUX read aux_in; DGELU maps it through gelu', MUL_AUX uses it as is.
   const bool dgelu = p.activation == MOE_ACT_DGELU || p.activation == MOE_ACT_MUL_AUX;
@@ -224,6 +249,7 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
 template <bool BF16>
 __device__ __forceinline__ void zero_output(const Params& p, int nthreads) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  if (p.push.src != nullptr) return;  // combine push: no expert rows, nothing to push
   const int64_t chunks_per_row = p.n / 8;
   const int64_t total_chunks = int64_t(p.m_total) * chunks_per_row;
   for (int64_t i = int64_t(blockIdx.x) * nthreads + threadIdx.x; i < total_chunks;
@@ -232,6 +258,18 @@ __device__ __forceinline__ void zero_output(const Params& p, int nthreads) {
     *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.c) + r * p.ldc + cc * 8) = make_uint4(0, 0, 0, 0);
   }
 }
+
+// The grouped GEMM with the extended epilogue (moe_grouped_gemm_ex's contract) and,
+// when push is non-null, the combine push instead of C (c may then be null and ldc
+// is the combine row stride).  Returns a MOE_* code.
+int grouped_gemm_launch(const void* a, int64_t lda, const void* b, int64_t b_stride_e,
+                        int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                        const void* expert_offsets, int32_t offsets_int64, int64_t m_total,
+                        int64_t k, int64_t n, int32_t num_experts, int32_t dtype,
+                        int32_t activation, int32_t num_sms, int32_t use_atomic_queue,
+                        int32_t* work_counter, const float* row_scale, const void* aux_in,
+                        void* aux_out, int64_t ld_aux, int32_t* status, cudaStream_t stream,
+                        const PushTarget* push);
 
 // Launches the 2-SM (CTA pair) kernel; grid must be even.  `tc` is the 2-D {N, m_total}
 // store map of C (32x32 boxes, 64-byte swizzle), used when p.c_tma is set.

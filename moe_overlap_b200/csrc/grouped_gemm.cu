@@ -297,8 +297,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
-                              lane, s.x, s.y, s.z, p);
+      if (p.push.src != nullptr)
+        store_accumulator<BF16, true>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN),
+                                      quad, lane, s.x, s.y, s.z, p);
+      else
+        store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
+                                lane, s.x, s.y, s.z, p);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->tempty[acc]));
@@ -376,17 +380,16 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
 
 using namespace moe;
 
-extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b,
-                                       int64_t b_stride_e, int64_t b_stride_k, int64_t b_stride_n,
-                                       void* c, int64_t ldc, const void* expert_offsets,
-                                       int32_t offsets_int64, int64_t m_total, int64_t k,
-                                       int64_t n, int32_t num_experts, int32_t dtype,
-                                       int32_t activation, int32_t num_sms,
-                                       int32_t use_atomic_queue, int32_t* work_counter,
-                                       const float* row_scale, const void* aux_in, void* aux_out,
-                                       int64_t ld_aux, int32_t* status, void* stream_) {
+int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int64_t b_stride_e,
+                                 int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                                 const void* expert_offsets, int32_t offsets_int64, int64_t m_total,
+                                 int64_t k, int64_t n, int32_t num_experts, int32_t dtype,
+                                 int32_t activation, int32_t num_sms, int32_t use_atomic_queue,
+                                 int32_t* work_counter, const float* row_scale, const void* aux_in,
+                                 void* aux_out, int64_t ld_aux, int32_t* status, cudaStream_t stream,
+                                 const PushTarget* push) {
   using namespace moe::gg;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const bool pushing = push != nullptr && push->src != nullptr;
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_F16) return MOE_ERR_INVALID_ARG;
   if (activation < MOE_ACT_NONE || activation > MOE_ACT_MUL_AUX) return MOE_ERR_INVALID_ARG;
   if ((activation == MOE_ACT_DGELU || activation == MOE_ACT_MUL_AUX) && aux_in == nullptr)
@@ -401,8 +404,15 @@ extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b
   if (num_experts > MAX_EXPERTS) return MOE_ERR_UNSUPPORTED;
   if (expert_offsets == nullptr) return MOE_ERR_INVALID_ARG;
   if (m_total == 0 || n == 0) return MOE_OK;
-  if (c == nullptr || !aligned16(c) || ldc < n || ldc % 8 != 0 || n % 8 != 0)
+  if (pushing) {
+    // Combine push: rows go to the source ranks' combine rows (stride ldc), not C.
+    if (push->dst == nullptr || push->peers == nullptr || ldc < n || ldc % 8 != 0 ||
+        n % 8 != 0 || k == 0 || num_experts == 0 || aux_out != nullptr ||
+        activation == MOE_ACT_GELU_SAVE_GRAD)
+      return MOE_ERR_INVALID_ARG;
+  } else if (c == nullptr || !aligned16(c) || ldc < n || ldc % 8 != 0 || n % 8 != 0) {
     return MOE_ERR_INVALID_ARG;
+  }
   if (k == 0 || num_experts == 0) {
     // Empty contraction or no experts: every computed row is zero, and with no
     // experts at all the reference zero-fills the whole output.
@@ -473,12 +483,13 @@ extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b
   p.aux_in = aux_in;
   p.aux_out = aux_out;
   p.ld_aux = ld_aux;
+  p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0};
 
   // The pair kernel stores C through a {N, m_total} map in 32x32 boxes (64-byte swizzle).
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   p.c_tma = 0;
-  if (use_pair && gemm_tma_store()) {
+  if (use_pair && gemm_tma_store() && !pushing) {
     const uint64_t dims[2] = {uint64_t(n), uint64_t(m_total)};
     const uint64_t strides[1] = {uint64_t(ldc) * 2};
     const uint32_t box[2] = {32, 32};
@@ -496,6 +507,22 @@ extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b
   if (bf16 && !b_mn) return launch<true, false>(ta, tb, p, grid, stream);
   if (!bf16 && b_mn) return launch<false, true>(ta, tb, p, grid, stream);
   return launch<false, false>(ta, tb, p, grid, stream);
+}
+
+extern "C" int32_t moe_grouped_gemm_ex(const void* a, int64_t lda, const void* b,
+                                       int64_t b_stride_e, int64_t b_stride_k, int64_t b_stride_n,
+                                       void* c, int64_t ldc, const void* expert_offsets,
+                                       int32_t offsets_int64, int64_t m_total, int64_t k,
+                                       int64_t n, int32_t num_experts, int32_t dtype,
+                                       int32_t activation, int32_t num_sms,
+                                       int32_t use_atomic_queue, int32_t* work_counter,
+                                       const float* row_scale, const void* aux_in, void* aux_out,
+                                       int64_t ld_aux, int32_t* status, void* stream) {
+  return moe::gg::grouped_gemm_launch(a, lda, b, b_stride_e, b_stride_k, b_stride_n, c, ldc,
+                                      expert_offsets, offsets_int64, m_total, k, n, num_experts,
+                                      dtype, activation, num_sms, use_atomic_queue, work_counter,
+                                      row_scale, aux_in, aux_out, ld_aux, status,
+                                      static_cast<cudaStream_t>(stream), nullptr);
 }
 
 extern "C" int32_t moe_grouped_gemm(const void* a, int64_t lda, const void* b, int64_t b_stride_e,

@@ -73,11 +73,12 @@ __host__ __device__ constexpr size_t smem_bytes(int num_experts) {
          ((sizeof(Ctrl) + 15) / 16) * 16 + size_t(3) * 4 * (num_experts + 1);
 }
 
-template <bool BF16, bool B_MN_MAJOR>
 // 144 registers: with 10 warps, SM sub-partitions 0 and 1 hold three of them
 // (3 x 32 x 144 = 13,824 of their 16,384 registers), which leaves room for one
 // warp per sub-partition of a 4-warp exchange block at <= 80 registers, so the
-// dispatch/combine kernels run beside this persistent kernel.
+// dispatch/combine kernels run beside this persistent kernel.  PUSH compiles the
+// expert-parallel combine push into the epilogue (rows go to their source ranks).
+template <bool BF16, bool B_MN_MAJOR, bool PUSH>
 __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                              const __grid_constant__ CUtensorMap tmap_b,
@@ -327,7 +328,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
       }
       tc_fence_after();
       const int rows_here = min(int(BM_CTA), max(0, s.y - static_cast<int>(crank) * int(BM_CTA)));
-      store_accumulator<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
+      store_accumulator<BF16, PUSH>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
                               lane, s.x + static_cast<int>(crank) * BM_CTA, rows_here, s.z, p,
                               col_half * 4, 4, p.c_tma ? &tmap_c : nullptr,
                               smem_u32(sEpi + (warp - 2) * EPI_STAGE_BYTES));
@@ -356,10 +357,10 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
   }
 }
 
-template <bool BF16, bool B_MN>
+template <bool BF16, bool B_MN, bool PUSH = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
            int grid, cudaStream_t stream) {
-  auto kern = grouped_gemm_pair_kernel<BF16, B_MN>;
+  auto kern = grouped_gemm_pair_kernel<BF16, B_MN, PUSH>;
   static std::once_flag once[kMaxDevices];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MOE_ERR_CUDA;
@@ -378,6 +379,11 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
 int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                        const CUtensorMap& tc, const Params& p, int grid, cudaStream_t stream) {
   if (grid < 2 || grid % 2 != 0) return MOE_ERR_INVALID_ARG;
+  if (p.push.src != nullptr) {  // combine push (bf16 only)
+    if (!bf16) return MOE_ERR_INVALID_ARG;
+    return b_mn ? pair::launch<true, true, true>(ta, tb, tc, p, grid, stream)
+                : pair::launch<true, false, true>(ta, tb, tc, p, grid, stream);
+  }
   if (bf16 && b_mn) return pair::launch<true, true>(ta, tb, tc, p, grid, stream);
   if (bf16 && !b_mn) return pair::launch<true, false>(ta, tb, tc, p, grid, stream);
   if (!bf16 && b_mn) return pair::launch<false, true>(ta, tb, tc, p, grid, stream);

@@ -338,6 +338,60 @@ class DeepEPDispatcher:
         self._outstanding.popleft()
         return out, EventOverlap(event)
 
+    def expert_gemm_push(self, h: torch.Tensor, weight: torch.Tensor, handle: DispatchHandle, *,
+                         num_sms: Optional[int] = None, use_atomic_queue: bool = True,
+                         work_counter: Optional[torch.Tensor] = None) -> None:
+        """Down-projection fused with the combine's transfer, on the caller's stream.
+
+        ``h`` [rows, K] are the expert hidden rows in ``handle``'s receive layout and
+        ``weight`` [E_local, K, hidden] (strided views accepted, e.g. ``w2.transpose(1, 2)``
+        of nn.Linear weights).  Each result row is written by the GEMM epilogue straight
+        into the combine rows of the token's source rank; finish with
+        ``combine_pushed(handle, ...)``.
+        """
+        self._check_slot_live(handle)
+        if h.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+            raise ValueError("expert_gemm_push expects bf16 rows and weights")
+        if weight.dim() != 3 or weight.shape[0] != self.experts_per_rank or \
+                weight.shape[2] != self.hidden_size or weight.shape[1] != h.shape[1]:
+            raise ValueError(f"weight must be [{self.experts_per_rank}, {h.shape[1]}, {self.hidden_size}]")
+        _lib.check_status(self.device)
+        if use_atomic_queue and work_counter is None:
+            work_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        sms = num_sms or torch.cuda.get_device_properties(self.device).multi_processor_count
+        hc = h if (h.stride(1) == 1 and h.stride(0) % 8 == 0 and h.data_ptr() % 16 == 0) else h.contiguous()
+        self._ep.push_gemm(hc, weight, handle.slot, 0 if self._device_epochs else handle.epoch, sms,
+                           use_atomic_queue, work_counter, self._status)
+
+    def combine_pushed(self, handle: DispatchHandle, previous_event: Optional[object] = None, *,
+                       weighted: bool = False, out: Optional[torch.Tensor] = None,
+                       num_sms: Optional[int] = None, inline: bool = False):
+        """combine() for rows pushed by ``expert_gemm_push``: a local reduce after every
+        owner's GEMM has landed its rows here.  Returns (combined_x, event)."""
+        if not isinstance(handle, DispatchHandle) or handle.combined:
+            raise RuntimeError("combine needs the handle of an outstanding dispatch")
+        if self._outstanding and self._outstanding[0] is not handle:
+            raise RuntimeError("combine the oldest outstanding dispatch first")
+        _lib.check_status(self.device)
+        stream = self._enter_comm(previous_event, inline)
+        if out is None:
+            out = torch.empty((handle.num_tokens, self.hidden_size), dtype=torch.bfloat16,
+                              device=self.device)
+        elif (out.shape != (handle.num_tokens, self.hidden_size) or out.dtype != torch.bfloat16
+              or not out.is_contiguous() or out.data_ptr() % 16 != 0):
+            raise ValueError("out must be a contiguous, 16-byte aligned bf16 [num_tokens, hidden]")
+        with torch.cuda.stream(stream):
+            self._ep.combine_pushed(handle.topk_idx, handle.topk_weights, handle.slot,
+                                    0 if self._device_epochs else handle.epoch, weighted, out,
+                                    num_sms or self.num_sms, self.wait_ns, self._status)
+            event = torch.cuda.Event()
+            event.record(stream)
+        if not inline and not torch.cuda.is_current_stream_capturing():
+            out.record_stream(self.comm_stream)
+        handle.combined = True
+        self._outstanding.popleft()
+        return out, EventOverlap(event)
+
     def close(self) -> None:
         """Collective: every rank unmaps its peers' buffers before any rank frees its own."""
         if self._ep is not None:

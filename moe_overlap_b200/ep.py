@@ -215,6 +215,28 @@ class Endpoint:
                                     wait_ns, status.data_ptr(), self._stream()),
             "moe_ep_combine")
 
+    def push_gemm(self, a, b, slot, epoch, num_sms, use_atomic, work_counter, status) -> None:
+        """Fused down-projection + combine push of ``a`` rows (this rank's receive
+        layout of ``slot``) by ``b`` [E_local, K, hidden] (any strides that
+        moe_grouped_gemm accepts); see moe_ep_push_gemm."""
+        _lib.check_call(
+            self.lib.moe_ep_push_gemm(self.handle, a.data_ptr(), a.stride(0), b.data_ptr(),
+                                      b.stride(0), b.stride(1), b.stride(2), a.shape[0], a.shape[1],
+                                      _lib.MOE_DTYPE_BF16, int(num_sms), 1 if use_atomic else 0,
+                                      work_counter.data_ptr() if work_counter is not None else None,
+                                      slot, epoch, status.data_ptr(), self._stream()),
+            "moe_ep_push_gemm")
+
+    def combine_pushed(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns,
+                       status) -> None:
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_combine_pushed(self.handle, topk_idx.data_ptr(),
+                                           topk_w.data_ptr() if topk_w is not None else None, t, k,
+                                           slot, epoch, 1 if weighted else 0, out.data_ptr(),
+                                           num_blocks, wait_ns, status.data_ptr(), self._stream()),
+            "moe_ep_combine_pushed")
+
     def set_device_epoch(self, epoch: int) -> None:
         """Sets the device epoch counter (on the current stream): kernels called with
         epoch 0 draw epoch + 1, + 2, ... on the device."""
@@ -289,6 +311,19 @@ class LocalGroup:
         for ep in self.eps:
             ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
         return slot, epoch
+
+    def push_gemm(self, hs, ws_b, slot, epoch, num_sms=148, work_counter=None):
+        """Each rank's fused GEMM + push (rank r: rows hs[r] by weights ws_b[r])."""
+        epoch = self._kernel_epoch(epoch)
+        for r, ep in enumerate(self.eps):
+            ep.push_gemm(hs[r], ws_b[r], slot, epoch, num_sms, work_counter is not None,
+                         work_counter, self.status)
+
+    def combine_pushed(self, idxs, ws, slot, epoch, weighted, outs):
+        epoch = self._kernel_epoch(epoch)
+        for r, ep in enumerate(self.eps):
+            ep.combine_pushed(idxs[r], ws[r], slot, epoch, weighted, outs[r], self.num_blocks,
+                              self.wait_ns, self.status)
 
     def combine(self, idxs, ws, slot, epoch, weighted, outs):
         epoch = self._kernel_epoch(epoch)

@@ -64,7 +64,7 @@ class MoELayer:
                  router_bias: bool = False, num_comm_sms: int = 148,
                  micro_batch_size: int = 4096, use_atomic_queue: bool = True,
                  max_recv_rows: Optional[int] = None, training: bool = False,
-                 taper_chunks: bool = False):
+                 taper_chunks: bool = False, fused_combine: bool = True):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         self.group = group
         self.world = group.size() if group is not None else 1
@@ -76,6 +76,7 @@ class MoELayer:
         self.renormalize = renormalize
         self.micro = max(1, int(micro_batch_size))
         self.taper = taper_chunks
+        self.fused_combine = fused_combine
         self.use_atomic = use_atomic_queue
         self.device = torch.device("cuda", torch.cuda.current_device())
         dev, bf16 = self.device, torch.bfloat16
@@ -132,14 +133,26 @@ class MoELayer:
             logits = torch.matmul(x.to(torch.bfloat16), self.router_w.detach().t())
             return router_topk(logits, self.top_k, bias=self.router_b, renormalize=self.renormalize)
 
-    def _experts(self, res) -> torch.Tensor:
-        """GEMM1 (+GELU) and GEMM2 on the current stream; returns the expert-output rows."""
-        y = self.dispatcher.expert_out_buffer(res.handle)
+    def _experts(self, res) -> Optional[torch.Tensor]:
+        """GEMM1 (+GELU) and GEMM2 on the current stream.
+
+        With ``fused_combine`` GEMM2's epilogue pushes each row straight to its
+        source rank (DeepEPDispatcher.expert_gemm_push) and None is returned;
+        otherwise the expert-output rows are written locally and returned."""
         kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
         grouped_gemm(res.recv_x, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
                      activation="gelu", **kw)
+        if self.fused_combine:
+            self.dispatcher.expert_gemm_push(self.h, self.w2.transpose(1, 2), res.handle, **kw)
+            return None
+        y = self.dispatcher.expert_out_buffer(res.handle)
         grouped_gemm(self.h, self.w2.transpose(1, 2), res.expert_offsets, out=y, **kw)
         return y
+
+    def _combine(self, y, handle, **kw):
+        if y is None:
+            return self.dispatcher.combine_pushed(handle, weighted=True, **kw)
+        return self.dispatcher.combine(y, handle, weighted=True, **kw)
 
     def chunk_plan(self, t_total: int) -> list:
         """Token ranges of the pipelined chunks (each at most micro_batch_size tokens).
@@ -189,8 +202,8 @@ class MoELayer:
                 ns, ne = chunks[i + 1]
                 nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
             last = i + 1 == len(chunks)
-            disp.combine(y, cur.handle, previous_event=done, weighted=True, out=out[s:e],
-                         num_sms=self.solo_comm_blocks if last else None)
+            self._combine(y, cur.handle, previous_event=done, out=out[s:e],
+                          num_sms=self.solo_comm_blocks if last else None)
             cur = nxt
         torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
         stats = self.stats(probs, idx) if return_stats else None
@@ -230,7 +243,7 @@ class MoELayer:
             res = timed("dispatch_ms", lambda: disp.dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False))
             res.event.current_stream_wait()
             y = timed("experts_ms", lambda: self._experts(res))
-            timed("combine_ms", lambda: disp.combine(y, res.handle, weighted=True, out=out[s:e]))
+            timed("combine_ms", lambda: self._combine(y, res.handle, out=out[s:e]))
         if self.world > 1:
             t = torch.tensor([times[k] for k in sorted(times)], dtype=torch.float64, device=self.device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)

@@ -269,3 +269,60 @@ def test_device_epochs_match_the_oracle(cuda_device):
                 assert np.array_equal(to_storage(outs[r]), want[r]), (it, r)
     finally:
         grp.close()
+
+
+@pytest.mark.parametrize("world,topk", [(1, 2), (2, 2), (4, 3)])
+def test_push_gemm_combine_equals_pull_combine(cuda_device, world, topk):
+    """The fused down-projection + combine push (moe_ep_push_gemm + moe_ep_combine_pushed)
+    gives bit-for-bit the result of the GEMM into expert_out + the pull combine, and both
+    match the oracle (the GEMM within bf16 rounding, the reduction bit-exact)."""
+    from moe_overlap_b200.gemm import grouped_gemm
+    from oracle import grouped_gemm as og
+
+    tokens, hidden, ffn, E = 257, 128, 192, 8
+    per = E // world
+    xs, idxs, ws = routing(world, tokens, E, topk, seed=500 + world, hidden=hidden)
+    g = torch.Generator().manual_seed(41)
+    w1 = [(torch.randn(per, ffn, hidden, generator=g) * 0.05).to(torch.bfloat16) for _ in range(world)]
+    w2 = [(torch.randn(per, hidden, ffn, generator=g) * 0.05).to(torch.bfloat16) for _ in range(world)]
+    cap = world * tokens * topk
+    grp = LocalGroup(world, E, hidden, tokens, topk, cap, num_blocks=6)
+    try:
+        di = [i.to(cuda_device) for i in idxs]
+        dw = [w.to(cuda_device) for w in ws]
+        slot, epoch = grp.dispatch([x.to(cuda_device) for x in xs], di, dw)
+        torch.cuda.synchronize()
+        hs, w2t, ys = [], [], []
+        for r, ep in enumerate(grp.eps):
+            v = ep.slots[slot]
+            n = int(v.expert_offsets[-1])
+            h = grouped_gemm(v.recv_x, w1[r].to(cuda_device).transpose(1, 2), v.expert_offsets,
+                             activation="gelu")
+            hs.append(h)
+            w2t.append(w2[r].to(cuda_device).transpose(1, 2))
+            grouped_gemm(h, w2t[-1], v.expert_offsets, out=v.expert_out)
+            ys.append(to_storage(v.expert_out[:n]))
+        outs_pull = [torch.empty(tokens, hidden, dtype=torch.bfloat16, device=cuda_device)
+                     for _ in range(world)]
+        grp.combine(di, dw, slot, epoch, True, outs_pull)
+        grp.push_gemm(hs, w2t, slot, epoch)
+        outs_push = [torch.empty(tokens, hidden, dtype=torch.bfloat16, device=cuda_device)
+                     for _ in range(world)]
+        grp.combine_pushed(di, dw, slot, epoch, True, outs_push)
+        torch.cuda.synchronize()
+        assert int(grp.status.item()) == 0
+        recv, send_pos = oep.dispatch([to_storage(x) for x in xs], [i.numpy() for i in idxs],
+                                      [w.numpy() for w in ws], E)
+        want = oep.combine(ys, [i.numpy() for i in idxs], send_pos, E, weights=[w.numpy() for w in ws])
+        for r in range(world):
+            assert torch.equal(outs_push[r], outs_pull[r]), r
+            assert np.array_equal(to_storage(outs_pull[r]), want[r]), r
+            # the expert rows themselves against the oracle GEMM (bf16 rounding)
+            n = int(recv[r]["offsets"][-1])
+            yo, _ = og.grouped_gemm(to_storage(hs[r][:n]), to_storage(w2t[r].contiguous()),
+                                    recv[r]["offsets"], "bf16")
+            from oracle.numerics import bf16_bits_to_f32
+            diff = np.abs(bf16_bits_to_f32(ys[r]) - bf16_bits_to_f32(yo))
+            assert float(diff.max()) <= 2 ** -7 * float(np.abs(bf16_bits_to_f32(yo)).max()) + 1e-2
+    finally:
+        grp.close()
