@@ -97,6 +97,9 @@ def parse_args() -> argparse.Namespace:
                     help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-graph", action="store_true",
                     help="layer_train: time eager steps instead of a captured CUDA graph")
+    ap.add_argument("--combine", choices=["auto", "push", "pull"], default="auto",
+                    help="layer workloads: GEMM-fused combine push, or GEMM into expert_out + pull "
+                         "combine (auto: push when the layer spans several GPUs)")
     ap.add_argument("--taper", action="store_true",
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
@@ -374,7 +377,9 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     layer = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
                      router_bias=cfg["zipf_bias"], num_comm_sms=args.comm_sms,
                      micro_batch_size=args.micro_batch,
-                     taper_chunks=args.taper).init_random(std=0.02, seed=0)
+                     taper_chunks=args.taper,
+                     fused_combine=None if args.combine == "auto" else args.combine == "push",
+                     ).init_random(std=0.02, seed=0)
     bias_info = None
     if cfg["zipf_bias"]:
         rw, _, _ = random_weights(E, H, Fd, 0.02, 0)
@@ -455,6 +460,8 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": args.workload, "description": cfg["desc"],
                        "tokens_per_rank": T, "micro_batch": args.micro_batch,
                        "chunks": [e - s for s, e in layer.chunk_plan(T)],
+                       "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
+                       else "pull",
                        "comm_sms": args.comm_sms, "gate_bias": bias_info,
                        "realised_expert_share": [round(v, 4) for v in realised_share],
                        "rows_received_per_rank": [int(v) for v in recv_rows.tolist()],
