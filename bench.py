@@ -99,7 +99,7 @@ def parse_args() -> argparse.Namespace:
                     help="layer_train: time eager steps instead of a captured CUDA graph")
     ap.add_argument("--combine", choices=["auto", "push", "pull"], default="auto",
                     help="layer workloads: GEMM-fused combine push, or GEMM into expert_out + pull "
-                         "combine (auto: push when the layer spans several GPUs)")
+                         "combine (auto: the layer's default, pull)")
     ap.add_argument("--taper", action="store_true",
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")

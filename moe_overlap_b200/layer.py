@@ -76,10 +76,11 @@ class MoELayer:
         self.renormalize = renormalize
         self.micro = max(1, int(micro_batch_size))
         self.taper = taper_chunks
-        # The GEMM-fused combine push pays off when rows cross NVLink; on one GPU the
-        # local TMA-stored GEMM plus a local pull is faster (2.42 vs 2.55 ms, config 4).
-        self.fused_combine = (group is not None and group.size() > 1) if fused_combine is None \
-            else bool(fused_combine)
+        # The GEMM-fused combine push (expert_gemm_push + combine_pushed) is off by
+        # default: its epilogue stores rows one by one to their source ranks, which
+        # costs more GEMM time than the separate combine it removes (config 5 on
+        # 2 B200s: 1.70 vs 1.60 ms per step; config 4 on one: 2.55 vs 2.42 ms).
+        self.fused_combine = bool(fused_combine) if fused_combine is not None else False
         self.use_atomic = use_atomic_queue
         self.device = torch.device("cuda", torch.cuda.current_device())
         dev, bf16 = self.device, torch.bfloat16
