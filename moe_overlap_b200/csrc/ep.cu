@@ -42,7 +42,9 @@ namespace moe {
 namespace ep {
 
 constexpr int kMaxRanks = MOE_EP_MAX_RANKS;
-constexpr int kMaxExperts = 1024;
+// Experts per layer the exchange supports: its per-expert tables live in the
+// scatter's shared memory, which must stay small enough to run beside the GEMM.
+constexpr int kMaxExperts = 512;
 constexpr int kAssignPerLayoutBlock = 2048;  // 8 warps x 8 chunks x 32 lanes
 constexpr int kLayoutThreads = 256;
 // The scatter and pull blocks are sized to run beside a resident CTA of the
@@ -81,10 +83,13 @@ struct SlotLayout {
   uint64_t topk_idx;   // [cap][max_topk] int64
   uint64_t topk_w;     // [cap][max_topk] float
   uint64_t src;        // [cap] int2 {src_rank, src_token}
-  uint64_t dst;        // [cap] int32: src_token * max_topk + slot (-1 for padding rows)
+  uint64_t dst;        // [cap] int32: the row's index in its source rank's cb (-1: padding)
   uint64_t counts;     // [world][num_experts] int32
   uint64_t cb;         // [max_tokens * max_topk][hidden] bf16: this rank's tokens' expert
-                       // outputs, pushed here by their owners' GEMM epilogue
+                       // outputs, pushed here by their owners' GEMM epilogue, in blocks
+                       // ordered by global expert, each in (token, slot) order - the
+                       // order of the same rows on the owner, so runs of received rows
+                       // land on consecutive cb rows
 };
 
 struct SymLayout {
@@ -107,6 +112,8 @@ struct Endpoint {
   int32_t* block_hist = nullptr;    // [max_blocks][E] -> exclusive block base after count
   int32_t* rank_in_block = nullptr; // [max_tokens*max_topk]
   int32_t* send_pos[2] = {};        // [max_tokens*max_topk]
+  int32_t* cb_pos[2] = {};          // [max_tokens*max_topk] row of each (token, slot) in cb
+  CUtensorMap* d_cb_maps = nullptr; // [2][world] TMA store maps of every rank's cb (per slot)
   int32_t* offsets[2] = {};         // [per_rank+1] receiver expert offsets
   int32_t* my_counts = nullptr;     // [E]
   unsigned int* done_ctr = nullptr; // blocks finished in the current scatter
@@ -134,6 +141,7 @@ struct Params {
   int32_t* block_hist;
   int32_t* rank_in_block;
   int32_t* send_pos;
+  int32_t* cb_pos;
   int32_t* offsets_out;
   int32_t* my_counts;
   unsigned int* done_ctr;
@@ -153,6 +161,12 @@ struct Params {
 template <typename T>
 __device__ __forceinline__ T* at(uint8_t* base, uint64_t off) {
   return reinterpret_cast<T*>(base + off);
+}
+
+// The kernel's slot layout, selected with constant indices (a dynamic index into
+// the parameter struct would copy it to local memory).
+__device__ __forceinline__ SlotLayout slot_of(const Params& p) {
+  return p.slot ? p.lay.slot[1] : p.lay.slot[0];
 }
 
 // The epoch of the dispatch a kernel belongs to: the host's, or with host epoch 0
@@ -251,7 +265,7 @@ __global__ void count_kernel(Params p) {
   }
   __syncthreads();
   for (int d = 0; d < p.world; ++d) {
-    int32_t* dst = at<int32_t>(p.peers[d], p.lay.slot[p.slot].counts) + p.rank * E;
+    int32_t* dst = at<int32_t>(p.peers[d], slot_of(p).counts) + p.rank * E;
     for (int e = threadIdx.x; e < E; e += blockDim.x) dst[e] = p.my_counts[e];
   }
   __threadfence_system();
@@ -279,6 +293,7 @@ struct CountView {
   int exp_base[kMaxExperts];  // first row of expert e on its owner
   int my_prefix[kMaxExperts]; // rows of expert e from ranks before this one
   int exp_count[kMaxExperts]; // rows of expert e from all ranks (before alignment)
+  int my_base[kMaxExperts];   // first cb row of expert e's block (this rank's rows)
   int recv_total;             // rows this rank receives
   int overflow;               // some owner would exceed its capacity
   int fail;
@@ -286,7 +301,7 @@ struct CountView {
 
 __device__ void build_count_view(const Params& p, CountView& cv) {
   const int E = p.num_experts;
-  const int32_t* M = at<int32_t>(p.peers[p.rank], p.lay.slot[p.slot].counts);
+  const int32_t* M = at<int32_t>(p.peers[p.rank], slot_of(p).counts);
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int col = 0, before = 0;
     for (int q = 0; q < p.world; ++q) {
@@ -310,6 +325,14 @@ __device__ void build_count_view(const Params& p, CountView& cv) {
     }
     if (run > p.cap_rows) atomicOr(&cv.overflow, 1);
     if (d == p.rank) cv.recv_total = run;
+  }
+  if (threadIdx.x == 32) {
+    // This rank's cb blocks: its own rows per global expert, in expert order.
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      cv.my_base[e] = run;
+      run += M[p.rank * E + e];
+    }
   }
   __syncthreads();
 }
@@ -356,7 +379,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (kCommThreads / 32);
   const int nvec = p.hidden / 8;  // 16-byte vectors per row
-  const SlotLayout sl = p.lay.slot[p.slot];
+  const SlotLayout sl = slot_of(p);
   if (!overflow) {
     for (int t = blockIdx.x * (kCommThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
       const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
@@ -385,9 +408,13 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
               (lane == j) ? p.topk_w[a] : 0.0f;
         }
         if (lane == 0) {
+          // Row in this rank's cb: its block (global expert e, blocks in expert order,
+          // sized by this rank's counts) plus its rank among this rank's rows for e.
+          const int cb_row = cv.my_base[e] + p.block_hist[blk * E + e] + p.rank_in_block[a];
           at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
-          at<int32_t>(peer, sl.dst)[row] = t * p.max_topk + j;
+          at<int32_t>(peer, sl.dst)[row] = cb_row;
           p.send_pos[a] = row;
+          p.cb_pos[a] = cb_row;
         }
       }
       // Each lane loads 4 x 16 B per pass (2 KB of a row per warp)
@@ -537,7 +564,7 @@ __global__ void __launch_bounds__(kPullThreads, kCommMinBlocks) pull_kernel(Para
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (kPullThreads / 32);
   const int nvec = p.hidden / 8;
-  const SlotLayout sl = p.lay.slot[p.slot];
+  const SlotLayout sl = slot_of(p);
   for (int t = blockIdx.x * (kPullThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
     const uint4* srcs[MAXR];
     float scale[MAXR];
@@ -548,8 +575,7 @@ __global__ void __launch_bounds__(kPullThreads, kCommMinBlocks) pull_kernel(Para
       if (row < 0) continue;
       if (p.pushed) {
         // The owner's GEMM pushed this (token, slot) row into our combine rows.
-        srcs[ns] = at<const uint4>(p.peers[p.rank], sl.cb) +
-                   (static_cast<int64_t>(t) * p.max_topk + j) * nvec;
+        srcs[ns] = at<const uint4>(p.peers[p.rank], sl.cb) + static_cast<int64_t>(p.cb_pos[a]) * nvec;
       } else {
         const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
         srcs[ns] = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
@@ -570,7 +596,7 @@ __global__ void __launch_bounds__(256) topk_weight_grad_kernel(Params p, const _
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (blockDim.x / 32);
   const int nvec = p.hidden / 8;
-  const SlotLayout sl = p.lay.slot[p.slot];
+  const SlotLayout sl = slot_of(p);
   for (int a = blockIdx.x * (blockDim.x / 32) + warp; a < p.num_tokens * p.topk; a += warps_total) {
     const int t = a / p.topk;
     const int row = p.send_pos[a];
@@ -725,9 +751,11 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   off = align_up(off + uint64_t(ep->max_blocks) * num_experts * 4, 256);
   const uint64_t o_rib = off;
   off = align_up(off + uint64_t(assigns) * 4, 256);
-  uint64_t o_send[2], o_offs[2];
+  uint64_t o_send[2], o_offs[2], o_cbpos[2];
   for (int s = 0; s < 2; ++s) {
     o_send[s] = off;
+    off = align_up(off + uint64_t(assigns) * 4, 256);
+    o_cbpos[s] = off;
     off = align_up(off + uint64_t(assigns) * 4, 256);
     o_offs[s] = off;
     off = align_up(off + uint64_t(ep->per_rank + 1) * 4, 256);
@@ -736,6 +764,8 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   off = align_up(off + uint64_t(num_experts) * 4, 256);
   const uint64_t o_done = off;
   off = align_up(off + 256, 256);
+  const uint64_t o_maps = off;
+  off = align_up(off + 2ull * world * sizeof(CUtensorMap), 256);
   if (cudaMalloc(&ep->sym, ep->lay.bytes) != cudaSuccess) {
     delete ep;
     return MOE_ERR_CUDA;
@@ -758,7 +788,9 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   ep->d_peers = reinterpret_cast<uint8_t**>(ep->scratch + o_peers);
   ep->block_hist = reinterpret_cast<int32_t*>(ep->scratch + o_hist);
   ep->rank_in_block = reinterpret_cast<int32_t*>(ep->scratch + o_rib);
+  ep->d_cb_maps = reinterpret_cast<CUtensorMap*>(ep->scratch + o_maps);
   for (int s = 0; s < 2; ++s) {
+    ep->cb_pos[s] = reinterpret_cast<int32_t*>(ep->scratch + o_cbpos[s]);
     ep->send_pos[s] = reinterpret_cast<int32_t*>(ep->scratch + o_send[s]);
     ep->offsets[s] = reinterpret_cast<int32_t*>(ep->scratch + o_offs[s]);
   }
@@ -806,8 +838,29 @@ extern "C" int32_t moe_ep_connect(moe_ep_t ep, void* const* peer_bases) {
     ep->peers[d] = static_cast<uint8_t*>(peer_bases[d]);
   }
   if (ep->peers[ep->rank] != ep->sym) return MOE_ERR_INVALID_ARG;
-  return cudaMemcpy(ep->d_peers, ep->peers, sizeof(void*) * ep->world, cudaMemcpyHostToDevice) ==
-                 cudaSuccess
+  if (cudaMemcpy(ep->d_peers, ep->peers, sizeof(void*) * ep->world, cudaMemcpyHostToDevice) !=
+      cudaSuccess)
+    return MOE_ERR_CUDA;
+  // TMA store maps of every rank's combine rows (per slot): 32x32 bf16 boxes with
+  // 64-byte swizzle, used by the fused down-projection's epilogue.
+  CUtensorMap maps[2 * moe::ep::kMaxRanks];
+  std::memset(maps, 0, sizeof(maps));
+  const uint64_t cb_rows = uint64_t(ep->max_tokens) * ep->max_topk;
+  if (cb_rows > 0) {
+    for (int s = 0; s < 2; ++s)
+      for (int d = 0; d < ep->world; ++d) {
+        const uint64_t dims[2] = {uint64_t(ep->hidden), cb_rows};
+        const uint64_t strides[1] = {uint64_t(ep->hidden) * 2};
+        const uint32_t box[2] = {32, 32};
+        if (int rc = moe::encode_tiled(&maps[s * ep->world + d], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                       ep->peers[d] + ep->lay.slot[s].cb, dims, strides, box,
+                                       CU_TENSOR_MAP_SWIZZLE_64B);
+            rc != MOE_OK)
+          return rc;
+      }
+  }
+  return cudaMemcpy(ep->d_cb_maps, maps, sizeof(CUtensorMap) * 2 * ep->world,
+                    cudaMemcpyHostToDevice) == cudaSuccess
              ? MOE_OK
              : MOE_ERR_CUDA;
 }
@@ -879,6 +932,7 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
   p.block_hist = ep->block_hist;
   p.rank_in_block = ep->rank_in_block;
   p.send_pos = ep->send_pos[slot];
+  p.cb_pos = ep->cb_pos[slot];
   p.offsets_out = ep->offsets[slot];
   p.my_counts = ep->my_counts;
   p.done_ctr = ep->done_ctr;
@@ -925,6 +979,7 @@ static int32_t combine_reduce(moe_ep_t ep, const int64_t* topk_idx, const float*
   p.num_tokens = num_tokens;
   p.topk = topk;
   p.send_pos = ep->send_pos[slot];
+  p.cb_pos = ep->cb_pos[slot];
   p.out = static_cast<__nv_bfloat16*>(out);
   p.weighted = weighted ? 1 : 0;
   p.pushed = pushed;
@@ -974,6 +1029,7 @@ extern "C" int32_t moe_ep_push_gemm(moe_ep_t ep, const void* a, int64_t lda, con
   push.dst = reinterpret_cast<const int32_t*>(ep->sym + sl.dst);
   push.peers = ep->d_peers;
   push.cb = sl.cb;
+  push.maps = ep->d_cb_maps + slot * ep->world;
   if (m_total > 0) {
     const int rc = moe::gg::grouped_gemm_launch(
         a, lda, b, b_stride_e, b_stride_k, b_stride_n, nullptr, ep->hidden, ep->offsets[slot], 0,

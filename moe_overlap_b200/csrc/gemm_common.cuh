@@ -23,6 +23,7 @@ struct PushTarget {
   const int32_t* dst;      // [m_total] row index in the source rank's combine rows
   uint8_t* const* peers;   // [world] every rank's symmetric buffer, as mapped here
   uint64_t cb;             // byte offset of the combine rows in each buffer
+  const CUtensorMap* maps; // [world] TMA store maps of each rank's combine rows, or null
 };
 
 struct Params {
@@ -113,17 +114,30 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
   bool row_ok = row_in_tile < rows;
   const int64_t grow = int64_t(row0) + row_in_tile;
   T* crow;
+  // TMA store target of this warp's rows: C's map at row0 + 32*quad, or, for a
+  // combine push whose 32 rows all go to one source rank's consecutive cb rows,
+  // that rank's cb map at the first row (warp-uniform).
+  const void* tmap = tmap_c;
+  int trow = row0 + quad * 32;
   if constexpr (PUSH) {
     // Combine push: this row's destination on its source rank (peer memory).
     crow = nullptr;
+    int2 src = make_int2(-1, -1);
+    int32_t dst = -1;
     if (row_ok) {
-      const int2 src = p.push.src[grow];
-      const int32_t dst = p.push.dst[grow];
+      src = p.push.src[grow];
+      dst = p.push.dst[grow];
       if (src.x >= 0 && dst >= 0)
         crow = reinterpret_cast<T*>(p.push.peers[src.x] + p.push.cb) + int64_t(dst) * p.ldc;
       else
         row_ok = false;
     }
+    const int s0 = __shfl_sync(0xffffffffu, src.x, 0);
+    const int d0 = __shfl_sync(0xffffffffu, dst, 0);
+    const bool run = __all_sync(0xffffffffu, row_ok && src.x == s0 && dst == d0 + lane);
+    tmap = (run && p.push.maps != nullptr && stage != 0) ? static_cast<const void*>(p.push.maps + s0)
+                                                         : nullptr;
+    trow = d0;
   } else {
     crow = reinterpret_cast<T*>(p.c) + grow * p.ldc;
   }
@@ -162,8 +176,8 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
     tmem_wait_ld();
     const int col = n0 + ch * 32;
     const int nvec = vecs(ch);  // 16-byte vectors inside the matrix
-    const bool tma = tmap_c != nullptr && col < p.n &&
-                     (rows_clipped_by_map ? quad * 32 < rows : quad * 32 + 32 <= rows);  // warp-uniform
+    const bool tma = tmap != nullptr && col < p.n &&
+                     (PUSH || (rows_clipped_by_map ? quad * 32 < rows : quad * 32 + 32 <= rows));  // warp-uniform
     if (tma || nvec > 0) {
       float v[32];
 #pragma unroll
@@ -227,9 +241,9 @@ __device__ __forceinline__ void store_accumulator(uint32_t t_base, int quad, int
         __syncwarp();
         if (lane == 0) {
           if (e3 >= 0)
-            tma_store_3d(tmap_c, stage, col, row0 + quad * 32, e3);
+            tma_store_3d(tmap, stage, col, trow, e3);
           else
-            tma_store_2d(tmap_c, stage, col, row0 + quad * 32);
+            tma_store_2d(tmap, stage, col, trow);
           bulk_commit_group();
         }
       } else {

@@ -483,7 +483,7 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
   p.aux_in = aux_in;
   p.aux_out = aux_out;
   p.ld_aux = ld_aux;
-  p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0};
+  p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0, nullptr};
 
   // The pair kernel stores C through a {N, m_total} map in 32x32 boxes (64-byte swizzle).
   CUtensorMap tc;
