@@ -22,6 +22,12 @@ Differences a caller can see, all within the reference's contract:
     unused rows have ``recv_topk_idx == -1``.
   * ``combine(..., weighted=True)`` applies the dispatch's top-k weights inside
     the reduction (fused weighted combine).
+  * ``expert_gemm_push`` + ``combine_pushed`` fuse the combine's transfer into the
+    down-projection GEMM (its epilogue writes rows to their source ranks);
+    ``use_device_epochs`` makes every exchange kernel CUDA-graph-capturable;
+    ``inline=True`` runs a phase on the caller's stream.
+  * ``num_sms`` counts the exchange kernels' 128-thread blocks, which are sized to
+    run beside the persistent GEMM on every SM.
 Returned receive tensors are views of the dispatcher's buffers and stay valid
 until the dispatch after next (two slots alternate).
 """
@@ -115,8 +121,9 @@ def _env_int(name: str, default: int) -> int:
 class DeepEPDispatcher:
     """Intranode dispatch/combine over NVLink peer memory (drop-in for the DeepEP wrapper).
 
-    ``num_sms`` is the grid of the exchange kernels (the reference reserves the
-    same number of SMs for DeepEP, src/train_moe_baseline.py:151-152).
+    ``num_sms`` is the grid of the exchange kernels in 128-thread blocks (the
+    reference reserves that many SMs for DeepEP, src/train_moe_baseline.py:151-152;
+    here the blocks share the SMs with the GEMM instead of taking them from it).
     Capacity: ``max_tokens_per_rank`` tokens per dispatch (env
     ``MOE_B200_MAX_TOKENS``, default 8192), ``max_top_k`` (``MOE_B200_MAX_TOPK``,
     default 8), and ``max_recv_rows`` rows received per rank per dispatch
