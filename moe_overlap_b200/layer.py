@@ -12,10 +12,15 @@ work:
   * GELU is fused into the up-projection's epilogue (:243), the down-projection
     writes into the exchange buffer, and the combine applies the top-k weights
     while it reduces (:394-399 + deep_ep_comm.combine);
+  * the router's softmax / bias / top-k / renormalisation is one kernel
+    (router.router_topk) after the gate matmul (:316-318);
   * chunks of ``micro_batch_size`` tokens pipeline like the reference's loop
     (:349-441): the next chunk's dispatch runs on the exchange stream while the
-    current chunk's GEMMs run on the compute stream.
+    current chunk's GEMMs run on the compute stream, on the same SMs (the
+    exchange blocks are sized to run beside the persistent GEMM CTAs).
 World size 1 (no process group) runs the same kernels with a local exchange.
+Training: forward_autograd / RoutedExperts (backward on the same kernels), and
+TrainStepGraph to replay a whole training step as one CUDA graph.
 """
 from __future__ import annotations
 
@@ -54,9 +59,12 @@ class MoELayer:
     """Expert-parallel routed MoE layer.
 
     The grouped GEMMs use the atomic tile queue by default: they share the SMs
-    with the exchange kernels, and a CTA pair that starts late (its SM still
-    busy with a dispatch or combine block) then simply takes fewer tiles
-    instead of delaying a fixed striped share.
+    with the exchange kernels, and a CTA pair slowed by an exchange block beside
+    it then simply takes fewer tiles instead of delaying a fixed striped share.
+    ``num_comm_sms`` is the exchange kernels' grid (128-thread blocks) for the
+    phases that overlap a GEMM; the first dispatch, the last combine and the
+    training path use four blocks per SM.  ``fused_combine`` selects the
+    GEMM-fused combine push (off by default; it measured even with the pull).
     """
 
     def __init__(self, hidden_size: int, ffn_size: int, num_experts: int, top_k: int, *,
