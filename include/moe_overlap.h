@@ -258,8 +258,10 @@ typedef struct {
 } moe_ep_views_t;
 
 /* Allocates this rank's endpoint: a symmetric buffer holding two slots of
- * max_recv_rows received rows (plus expert outputs, metadata, counts, flags),
- * and local scratch for max_tokens tokens of up to max_topk experts each. */
+ * max_recv_rows received rows (plus expert outputs, metadata, counts, flags, and
+ * max_tokens * max_topk combine rows for the fused push), and local scratch for
+ * max_tokens tokens of up to max_topk experts each.  Limits: world <= 64,
+ * num_experts <= 512 and divisible by world, max_topk <= 8, hidden % 8 == 0. */
 MOE_API int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden,
                               int32_t max_tokens, int32_t max_topk, int64_t max_recv_rows,
                               moe_ep_t* out);
