@@ -96,7 +96,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--micro-batch", type=int, default=4096,
                     help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-graph", action="store_true",
-                    help="layer_train: time eager steps instead of a captured CUDA graph")
+                    help="layer workloads: time eager steps instead of a captured CUDA graph")
     ap.add_argument("--combine", choices=["auto", "push", "pull"], default="auto",
                     help="layer workloads: GEMM-fused combine push, or GEMM into expert_out + pull "
                          "combine (auto: the layer's default, pull)")
@@ -409,6 +409,23 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
         layer(x, routing=routing)
     torch.cuda.synchronize(device)
     mo.check_status(device, sync=True)
+    # On one GPU the timed forwards replay one CUDA graph (device-drawn exchange
+    # epochs) unless --no-graph; across GPUs they run eagerly, so that a capture
+    # problem on one rank cannot leave the others waiting.
+    graph, graph_note = None, None
+    if world == 1 and not args.no_graph:
+        try:
+            from moe_overlap_b200.layer import ForwardGraph
+
+            graph = ForwardGraph(layer, x, routing)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize(device)
+            mo.check_status(device, sync=True)
+        except Exception as exc:  # report and time eager forwards instead
+            graph = None
+            graph_note = f"capture failed ({type(exc).__name__}: {exc})"[:240]
+            torch.cuda.synchronize(device)
 
     sampler = ClockSampler(device)
     sampler.start()
@@ -418,7 +435,10 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
-        layer(x, routing=routing)
+        if graph is not None:
+            graph.replay()
+        else:
+            layer(x, routing=routing)
     end.record()
     torch.cuda.synchronize(device)
     if world > 1:
@@ -460,6 +480,7 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": args.workload, "description": cfg["desc"],
                        "tokens_per_rank": T, "micro_batch": args.micro_batch,
                        "chunks": [e - s for s, e in layer.chunk_plan(T)],
+                       "cuda_graph": graph is not None, "cuda_graph_note": graph_note,
                        "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                        else "pull",
                        "comm_sms": args.comm_sms, "gate_bias": bias_info,

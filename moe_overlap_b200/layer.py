@@ -436,3 +436,37 @@ class TrainStepGraph:
 
     def replay(self) -> None:
         self.graph.replay()
+
+
+class ForwardGraph:
+    """``layer(x, routing=routing)`` captured as one CUDA graph (static inputs).
+
+    Copy each batch into ``x`` (and its routing into the ``routing`` tensors, or
+    route inside by passing ``routing=None``) and call ``replay()``; ``out`` then
+    holds the result.  Uses device-drawn exchange epochs like TrainStepGraph, and
+    needs an even number of chunks per forward (chunk_plan) so that replays keep
+    the slot alternation.  With a process group every rank must capture and replay
+    in step.
+    """
+
+    def __init__(self, layer: MoELayer, x: torch.Tensor, routing=None, warmup: int = 2):
+        self.layer, self.x, self.routing = layer, x, routing
+        n_chunks = len(layer.chunk_plan(x.shape[0]))
+        if n_chunks % 2 != 0:
+            raise ValueError(f"a captured forward needs an even number of chunks (has {n_chunks}); "
+                             "adjust micro_batch_size")
+        layer.dispatcher.use_device_epochs()
+        cur = torch.cuda.current_stream(layer.device)
+        side = torch.cuda.Stream(layer.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                layer(x, routing=routing)
+        cur.wait_stream(side)
+        torch.cuda.synchronize(layer.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out, _ = layer(x, routing=routing)
+
+    def replay(self) -> None:
+        self.graph.replay()
