@@ -8,18 +8,26 @@ The compute runs in ``libmoe_overlap_b200.so`` (built in-tree by
 from .gemm import (
     expert_offsets_from_recv_counts,
     grouped_gemm,
+    grouped_gemm_wgrad,
     persistent_grouped_gemm,
     reference_grouped_gemm,
     tile_list,
 )
 from ._lib import MoeError, check_status
+from .router import router_topk
 
 __all__ = [
     "persistent_grouped_gemm",
     "grouped_gemm",
+    "grouped_gemm_wgrad",
     "expert_offsets_from_recv_counts",
     "reference_grouped_gemm",
     "tile_list",
+    "router_topk",
     "MoeError",
     "check_status",
 ]
+
+# The exchange (deep_ep_comm.DeepEPDispatcher, ep.Endpoint/LocalGroup) and the
+# layer (layer.MoELayer, TrainStepGraph, ForwardGraph) are imported from their
+# modules; they need torch.distributed only when a process group is given.
