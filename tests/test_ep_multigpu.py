@@ -51,3 +51,8 @@ def test_dispatcher_across_processes(world):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_moe_layer_across_processes(world):
     _run(world, "_layer_worker.py", "moe layer matches the oracle")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_moe_layer_training_across_processes(world):
+    _run(world, "_train_worker.py", "training step matches the reference")
