@@ -1,0 +1,43 @@
+"""Host-side pieces of bench.py: the BASELINE workloads' shapes and the config-5 gate bias."""
+import sys
+from pathlib import Path
+
+import numpy as np
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+import bench  # noqa: E402
+
+
+def test_workload_counts_follow_the_baseline_configs():
+    assert bench.workload_counts("gemm_cfg1") == [128] * 8
+    assert bench.workload_counts("gemm_cfg2") == [512] * 16
+    c3 = bench.workload_counts("gemm_cfg3")
+    assert len(c3) == 16 and sum(c3) == 16384
+    assert min(c3) == 0                      # at least one expert gets no rows
+    assert max(c3) > 0.25 * 16384            # the largest gets over a quarter
+    assert bench.workload_counts("gemm_cfg3") == c3  # seeded
+
+
+def test_zipf_gate_bias_reproduces_zipf_shares():
+    """The fitted per-expert bias makes top-2 routing of N(0,1) tokens follow Zipf(1.0)."""
+    rng = np.random.default_rng(0)
+    # the config-5 gate: H = 2048, N(0, 0.02) weights (logit spread ~0.9)
+    router = (rng.standard_normal((16, 2048)) * 0.02).astype(np.float32)
+    bias, iters, err = bench.zipf_gate_bias(router, 16, 2)
+    assert bias.shape == (16,) and err < 0.05, (iters, err)
+    x = rng.standard_normal((16384, 2048)).astype(np.float32)
+    z = x @ router.T + bias
+    top = np.argpartition(-z, 1, axis=-1)[:, :2]
+    share = np.bincount(top.reshape(-1), minlength=16) / top.size
+    p = 1.0 / np.arange(1, 17)
+    p /= p.sum()
+    assert float(np.max(np.abs(share - p) / p)) < 0.1
+
+
+def test_layer_workloads_match_the_baseline_shapes():
+    w = bench.LAYER_WORKLOADS
+    assert (w["layer_train"]["tokens"], w["layer_train"]["hidden"], w["layer_train"]["ffn"],
+            w["layer_train"]["experts"], w["layer_train"]["top_k"]) == (8 * 2048, 2048, 8192, 16, 2)
+    assert w["layer_train"]["renorm"] and not w["layer_train"]["zipf_bias"]
+    assert (w["ep_layer"]["tokens"], w["ep_layer"]["ffn"], w["ep_layer"]["top_k"]) == (8 * 1024, 8192, 2)
+    assert w["ep_layer"]["zipf_bias"] and not w["ep_layer"]["renorm"]
