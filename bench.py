@@ -100,6 +100,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--combine", choices=["auto", "push", "pull"], default="auto",
                     help="layer workloads: GEMM-fused combine push, or GEMM into expert_out + pull "
                          "combine (auto: the layer's default, pull)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="layer workloads: add per-rank phase-boundary times of one forward")
     ap.add_argument("--taper", action="store_true",
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
@@ -453,6 +455,24 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(total_flops)
     step_ms = float(t.item())
 
+    timeline = None
+    if args.timeline:
+        # One more forward with events at every phase boundary on the stream that
+        # runs it (ms from the forward's start, per rank).
+        marks = []
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        layer(x, routing=routing, timeline=marks)
+        torch.cuda.synchronize(device)
+        mine = {name: round(marks[0][1].elapsed_time(ev), 4) for name, ev in marks[1:]}
+        if world > 1:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, mine)
+        else:
+            gathered = [mine]
+        timeline = {f"rank{r}": t for r, t in enumerate(gathered)}
+
     _, phases = layer.forward_serialized(x, routing)
     comm_ms = phases["dispatch_ms"] + phases["combine_ms"]
     comp_ms = phases["experts_ms"]
@@ -502,6 +522,8 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
             "clocks": clocks,
             "gpu_launches_per_step": None,
         }
+        if timeline is not None:
+            line["timeline_ms"] = timeline
         print(json.dumps(line), flush=True)
     layer.close()
     if world > 1:
