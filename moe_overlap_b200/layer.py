@@ -188,7 +188,7 @@ class MoELayer:
         return list(zip(bounds[:-1], bounds[1:]))
 
     @staticmethod
-    def _mark(timeline, name: str, stream) -> None:
+    def _timeline_mark(timeline, name: str, stream) -> None:
         if timeline is not None:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record(stream)
@@ -209,36 +209,36 @@ class MoELayer:
         chunks = self.chunk_plan(t_total)
         disp = self.dispatcher
         cur_stream = torch.cuda.current_stream(self.device)
-        self._mark(timeline, "start", cur_stream)
+        self._timeline_mark(timeline, "start", cur_stream)
         # The first dispatch and the last combine have no GEMM beside them: they get
         # the solo grid; the others run one block per SM beside the GEMMs.
         cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
                             w[chunks[0][0]:chunks[0][1]], pad_rows=False,
                             num_sms=self.solo_comm_blocks)
-        self._mark(timeline, "dispatch0_end", disp.comm_stream)
+        self._timeline_mark(timeline, "dispatch0_end", disp.comm_stream)
         for i, (s, e) in enumerate(chunks):
             # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
             # starts them as soon as this chunk's rows have landed, and the host
             # time spent enqueuing the next dispatch overlaps them.
             with torch.cuda.stream(self.compute_stream):
                 cur.event.current_stream_wait()
-                self._mark(timeline, f"gemm{i}_start", self.compute_stream)
+                self._timeline_mark(timeline, f"gemm{i}_start", self.compute_stream)
                 y = self._experts(cur)
-                self._mark(timeline, f"gemm{i}_end", self.compute_stream)
+                self._timeline_mark(timeline, f"gemm{i}_end", self.compute_stream)
                 done = torch.cuda.Event()
                 done.record(self.compute_stream)
             nxt = None
             if i + 1 < len(chunks):
                 ns, ne = chunks[i + 1]
                 nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
-                self._mark(timeline, f"dispatch{i + 1}_end", disp.comm_stream)
+                self._timeline_mark(timeline, f"dispatch{i + 1}_end", disp.comm_stream)
             last = i + 1 == len(chunks)
             self._combine(y, cur.handle, previous_event=done, out=out[s:e],
                           num_sms=self.solo_comm_blocks if last else None)
-            self._mark(timeline, f"combine{i}_end", disp.comm_stream)
+            self._timeline_mark(timeline, f"combine{i}_end", disp.comm_stream)
             cur = nxt
         torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
-        self._mark(timeline, "end", cur_stream)
+        self._timeline_mark(timeline, "end", cur_stream)
         stats = self.stats(probs, idx) if return_stats else None
         return out, stats
 

@@ -73,3 +73,22 @@ def test_layer_chunk_plan_covers_the_batch():
                 assert plan[0][0] == 0 and plan[-1][1] == t
                 assert all(a[1] == b[0] for a, b in zip(plan[:-1], plan[1:]))
                 assert all(0 < e - s <= micro for s, e in plan) or t == 0
+
+
+def test_package_classes_define_each_method_once():
+    """A second definition of a method name in a class body silently replaces the
+    first (it once broke the layer forward); no class in the package may do that."""
+    import ast
+    from pathlib import Path
+
+    pkg = Path(__file__).resolve().parents[1] / "moe_overlap_b200"
+    for path in sorted(pkg.glob("*.py")):
+        tree = ast.parse(path.read_text())
+        for node in ast.walk(tree):
+            if isinstance(node, ast.ClassDef):
+                names = [f.name for f in node.body
+                         if isinstance(f, (ast.FunctionDef, ast.AsyncFunctionDef))
+                         and not any(isinstance(d, ast.Attribute) and d.attr in ("setter", "deleter")
+                                     for d in f.decorator_list)]
+                dup = {n for n in names if names.count(n) > 1}
+                assert not dup, (path.name, node.name, dup)
