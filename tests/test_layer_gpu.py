@@ -135,3 +135,27 @@ def test_forward_graph_replays_the_eager_forward(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(fg.out, want[i]), rep
     layer.close()
+
+
+def test_forward_timeline_marks_every_phase_in_order(cuda_device):
+    """forward(timeline=...) records start/end, one dispatch end per chunk, each
+    chunk's GEMM span and combine end, and leaves the output bit-identical."""
+    g = torch.Generator().manual_seed(23)
+    x = torch.randn(2048, 256, generator=g).to(torch.bfloat16).to(cuda_device)
+    layer = MoELayer(256, 512, 16, 2, micro_batch_size=512, num_comm_sms=16).init_random(seed=6)
+    want = layer(x)[0].clone()
+    marks = []
+    got = layer(x, timeline=marks)[0]
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    names = [n for n, _ in marks]
+    chunks = len(layer.chunk_plan(x.shape[0]))
+    assert names[0] == "start" and names[-1] == "end"
+    for i in range(chunks):
+        assert f"dispatch{i}_end" in names and f"combine{i}_end" in names
+        assert names.index(f"gemm{i}_start") < names.index(f"gemm{i}_end")
+    ev = dict(marks)
+    assert ev["start"].elapsed_time(ev["end"]) >= 0.0
+    for i in range(chunks):
+        assert ev[f"gemm{i}_start"].elapsed_time(ev[f"gemm{i}_end"]) >= 0.0
+    layer.close()
