@@ -41,6 +41,7 @@ sys.path.insert(0, str(REPO))
 METRIC = "grouped-GEMM TFLOP/s vs bf16 peak"
 UNIT = "TFLOP/s"
 FALLBACK_PEAK_TFLOPS = 1590.0
+PEER_COPY_GBPS = 770.0  # measured peer copy per direction per B200 on this pool
 
 WORKLOADS = {
     # name: (counts builder, k, n, dtype, atomic, description)
@@ -330,6 +331,14 @@ class ClockSampler(threading.Thread):
 
 
 # ---------------------------------------------------------------- GPU side --
+def exchange_row_totals(row_matrix) -> tuple[list[float], list[float]]:
+    """Remote rows each rank sends and receives, from rows[src, dst] (rows a rank
+    keeps for its own experts cross no link)."""
+    m = row_matrix.double().clone()
+    m.fill_diagonal_(0)
+    return m.sum(dim=1).tolist(), m.sum(dim=0).tolist()
+
+
 def zipf_gate_bias(router_w, num_experts: int, top_k: int, seed: int = 12345):
     """Per-expert gate bias whose top-k routing follows Zipf(1.0) over expert ids.
 
@@ -401,7 +410,17 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(recv_rows, group=group)  # rows each rank receives, summed over senders
     else:
         recv_rows = rows_to
-    remote_rows = float(rows_to.sum() - rows_to[rank])
+    # rows[src, dst] over all ranks: the busiest rank's inbound or outbound remote
+    # rows bound the exchange (under the Zipf gate, rank 0 mostly receives).
+    if world > 1:
+        gathered_rows = [torch.zeros_like(rows_to) for _ in range(world)]
+        dist.all_gather(gathered_rows, rows_to, group=group)
+        row_matrix = torch.stack(gathered_rows)
+    else:
+        row_matrix = rows_to.view(1, 1)
+    remote_out, remote_in = exchange_row_totals(row_matrix.cpu())
+    remote_rows = float(remote_out[rank])
+    busiest_rows = float(max(max(remote_out), max(remote_in)))
     expert_counts = torch.bincount(idx[idx >= 0].reshape(-1), minlength=E).double()
     if world > 1:
         dist.all_reduce(expert_counts, group=group)
@@ -478,8 +497,8 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     comp_ms = phases["experts_ms"]
     hidden = max(0.0, min(1.0, (comm_ms + comp_ms - step_ms) / comm_ms)) if comm_ms > 0 else None
     row_bytes = H * 2
-    dispatch_bytes = remote_rows * (row_bytes + K * 12 + 8)
-    combine_bytes = remote_rows * row_bytes
+    dispatch_bytes = busiest_rows * (row_bytes + K * 12 + 8)
+    combine_bytes = busiest_rows * row_bytes
     peak, peak_src = load_peaks()
     if rank == 0:
         tokens_per_s = world * T / (step_ms / 1e3)
@@ -512,12 +531,15 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
             "communication_hidden_ratio": None if hidden is None else round(hidden, 4),
             "serial_phase_ms": {k: round(v, 4) for k, v in phases.items()},
             "nvlink": {
-                "dispatch_GBps_per_rank": round(dispatch_bytes / (phases["dispatch_ms"] / 1e3) / 1e9, 1)
+                "dispatch_GBps_busiest_rank": round(dispatch_bytes / (phases["dispatch_ms"] / 1e3) / 1e9, 1)
                 if world > 1 and phases["dispatch_ms"] > 0 else None,
-                "combine_GBps_per_rank": round(combine_bytes / (phases["combine_ms"] / 1e3) / 1e9, 1)
+                "combine_GBps_busiest_rank": round(combine_bytes / (phases["combine_ms"] / 1e3) / 1e9, 1)
                 if world > 1 and phases["combine_ms"] > 0 else None,
-                "rank0_remote_rows": int(remote_rows),
-                "peer_copy_reference_GBps": 770,
+                "remote_rows_out_per_rank": [int(v) for v in remote_out],
+                "remote_rows_in_per_rank": [int(v) for v in remote_in],
+                "nvlink_floor_ms_per_exchange": round(dispatch_bytes / PEER_COPY_GBPS / 1e6, 4)
+                if world > 1 else None,
+                "peer_copy_reference_GBps": PEER_COPY_GBPS,
             },
             "clocks": clocks,
             "gpu_launches_per_step": None,

@@ -41,3 +41,15 @@ def test_layer_workloads_match_the_baseline_shapes():
     assert w["layer_train"]["renorm"] and not w["layer_train"]["zipf_bias"]
     assert (w["ep_layer"]["tokens"], w["ep_layer"]["ffn"], w["ep_layer"]["top_k"]) == (8 * 1024, 8192, 2)
     assert w["ep_layer"]["zipf_bias"] and not w["ep_layer"]["renorm"]
+
+
+def test_exchange_row_totals_ignore_rows_kept_locally():
+    import torch
+
+    rows = torch.tensor([[13132.0, 3252.0], [13194.0, 3190.0]])  # rows[src, dst]
+    out, inbound = bench.exchange_row_totals(rows)
+    assert out == [3252.0, 13194.0]
+    assert inbound == [13194.0, 3252.0]
+    assert rows[0, 0] == 13132.0  # the caller's matrix is left as it was
+    out1, in1 = bench.exchange_row_totals(torch.tensor([[5.0]]))
+    assert out1 == [0.0] and in1 == [0.0]
