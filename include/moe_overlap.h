@@ -311,6 +311,35 @@ MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_
                                 int32_t* status, void* stream);
 
 /*
+ * Cached re-dispatch (DeepEP's dispatch given a handle: deep_ep/buffer.py:383-390,
+ * deep_ep.cpp:588-600): new rows x for the tokens and top-k choices of the most
+ * recent dispatch, which went into src_slot, pushed into the other slot `slot` at
+ * the places that dispatch gave them.  No layout or count phase runs:
+ *   begin    raises this rank's count flag for `slot` in every rank ("my side of
+ *            the slot is free"); no counts are sent        ~ cached_notify_dispatch
+ *   scatter  waits (bounded) for every rank's flag, pushes the rows, copies this
+ *            rank's receive metadata and expert offsets from src_slot, zeroes the
+ *            alignment padding rows, and raises the data flag everywhere;
+ *   end      moe_ep_dispatch_end.
+ * topk_idx / topk_weights / num_tokens / topk must be those of the source
+ * dispatch (the rows' destinations and, with scale_rows, their weights); every
+ * rank runs the cached form for the same dispatch.  The layout, expert_alignment
+ * and receive counts are the source dispatch's.
+ */
+MOE_API int32_t moe_ep_dispatch_cached_begin(moe_ep_t ep, int32_t slot, uint64_t epoch, void* stream);
+MOE_API int32_t moe_ep_dispatch_cached_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                               const float* topk_weights, int32_t num_tokens,
+                                               int32_t topk, int32_t src_slot, int32_t slot,
+                                               uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
+                                               int32_t scale_rows, uint64_t wait_ns,
+                                               int32_t* status, void* stream);
+MOE_API int32_t moe_ep_dispatch_cached(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                       const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                       int32_t src_slot, int32_t slot, uint64_t epoch,
+                                       int32_t num_blocks, int32_t pad_rows, int32_t scale_rows,
+                                       uint64_t wait_ns, int32_t* status, void* stream);
+
+/*
  * Fused down-projection + combine push: the grouped GEMM C = A @ B[e] over this
  * rank's received rows (expert_offsets of `slot`, experts = num_experts/world,
  * n = hidden, bf16), whose epilogue writes each result row straight into the

@@ -122,6 +122,13 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_dispatch": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
                _i32, _i32, _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch_cached_begin": (_i32, [_c_void_p, _i32, _u64, _c_void_p]),
+    "moe_ep_dispatch_cached_scatter": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _u64, _i32,
+               _i32, _i32, _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch_cached": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _u64, _i32,
+               _i32, _i32, _u64, _c_void_p, _c_void_p]),
     "moe_ep_topk_weight_grad": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p]),
     "moe_ep_combine_begin": (_i32, [_c_void_p, _i32, _u64, _c_void_p]),

@@ -152,6 +152,11 @@ struct Params {
   int align;     // receive segments of each local expert rounded up to this many rows
   int scale_rows;  // multiply each pushed row by its slot's weight (bf16 result)
   int64_t* host_info;
+  // cached re-dispatch: the slot whose layout the rows follow
+  int src_slot;
+  const int32_t* src_send_pos;
+  const int32_t* src_cb_pos;
+  const int32_t* src_offsets;
   // combine
   __nv_bfloat16* out;
   int weighted;
@@ -495,6 +500,145 @@ __global__ void wait_data_kernel(Params p) {
   __syncthreads();
   if (!wait_all_flags(p, p.lay.data_flag, &fail) && threadIdx.x == 0)
     record_status(p.status, MOE_ERR_TIMEOUT);
+}
+
+// ------------------------------------------------------ cached re-dispatch --
+// New rows for the tokens and top-k choices of the dispatch into src_slot, pushed
+// to the places that dispatch gave them (its send_pos), so neither the layout nor
+// the count phase runs.  What stays is the handshake that makes a slot reusable:
+// a rank writes into another rank's slot only after that rank has raised its
+// count flag for the new epoch, i.e. has finished everything it enqueued before.
+__device__ __forceinline__ SlotLayout src_slot_of(const Params& p) {
+  return p.src_slot ? p.lay.slot[1] : p.lay.slot[0];
+}
+
+__global__ void cached_begin_kernel(Params p) {
+  __shared__ uint64_t epoch_sh;
+  if (threadIdx.x == 0) {
+    uint64_t e = p.epoch;
+    if (e == 0) {  // draw this dispatch's epoch on the device
+      e = *p.epoch_ctr + 1;
+      *p.epoch_ctr = e;
+      p.slot_epoch[p.slot] = e;
+    }
+    epoch_sh = e;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world) {
+    uint64_t* f = at<uint64_t>(p.peers[threadIdx.x], p.lay.count_flag) + p.slot * p.world + p.rank;
+    st_release_sys(f, epoch_sh);
+  }
+}
+
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) cached_scatter_kernel(Params p) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!wait_all_flags(p, p.lay.count_flag, &fail)) {
+    if (threadIdx.x == 0) record_status(p.status, MOE_ERR_TIMEOUT);
+    return;
+  }
+  const SlotLayout sl = slot_of(p);
+  const SlotLayout ss = src_slot_of(p);
+  // This rank's receive layout is the source slot's (written by an earlier scatter
+  // whose data flags this stream has already waited for).
+  const int64_t recv_total =
+      max(static_cast<int64_t>(0), min(static_cast<int64_t>(p.src_offsets[p.per_rank]), p.cap_rows));
+  if (blockIdx.x == 0) {
+    for (int le = threadIdx.x; le <= p.per_rank; le += blockDim.x) p.offsets_out[le] = p.src_offsets[le];
+    if (threadIdx.x == 0 && p.host_info != nullptr) {
+      const int64_t src_rows = reinterpret_cast<const volatile int64_t*>(p.host_info)[2 * p.src_slot + 1];
+      volatile int64_t* hi = p.host_info + 2 * p.slot;
+      hi[1] = src_rows < 0 ? -1 : recv_total;
+      __threadfence_system();
+      hi[0] = static_cast<int64_t>(kernel_epoch(p));
+    }
+  }
+
+  const int E = p.num_experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (kCommThreads / 32);
+  const int gwarp = blockIdx.x * (kCommThreads / 32) + warp;
+  const int nvec = p.hidden / 8;
+  for (int t = gwarp; t < p.num_tokens; t += warps_total) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
+    uint4* dst[8];
+    float dscale[8];
+    int nd = 0;
+    for (int j = 0; j < p.topk; ++j) {
+      const int a = t * p.topk + j;
+      const int row = p.src_send_pos[a];
+      const int64_t ev = p.topk_idx[a];
+      if (row < 0 || row >= p.cap_rows || ev < 0 || ev >= E) {
+        if (lane == 0) p.send_pos[a] = -1;
+        continue;
+      }
+      const int d = static_cast<int>(ev) / p.per_rank;
+      dscale[nd] = p.topk_w[a];
+      dst[nd++] = at<uint4>(p.peers[d], sl.recv_x) + static_cast<int64_t>(row) * nvec;
+      if (lane == 0) {
+        p.send_pos[a] = row;
+        p.cb_pos[a] = p.src_cb_pos[a];
+      }
+    }
+    constexpr int U = 4;
+    for (int base = 0; base < nvec; base += 32 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * 32 + lane;
+        if (i < nvec) v[u] = __ldg(src + i);
+      }
+      for (int q = 0; q < nd; ++q) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * 32 + lane;
+          if (i < nvec) dst[q][i] = p.scale_rows ? scale_bf16x8(v[u], dscale[q]) : v[u];
+        }
+      }
+    }
+  }
+
+  // This rank's receive rows: metadata from the source slot (one warp per row);
+  // alignment padding rows (no source token) are zeroed in the new slot.
+  uint8_t* me = p.peers[p.rank];
+  for (int64_t r = gwarp; r < recv_total; r += warps_total) {
+    const int2 s = at<const int2>(me, ss.src)[r];
+    if (lane < p.max_topk) {
+      at<int64_t>(me, sl.topk_idx)[r * p.max_topk + lane] = at<const int64_t>(me, ss.topk_idx)[r * p.max_topk + lane];
+      at<float>(me, sl.topk_w)[r * p.max_topk + lane] = at<const float>(me, ss.topk_w)[r * p.max_topk + lane];
+    }
+    if (lane == 0) {
+      at<int2>(me, sl.src)[r] = s;
+      at<int32_t>(me, sl.dst)[r] = at<const int32_t>(me, ss.dst)[r];
+    }
+    if (s.x < 0) {
+      uint4* row = at<uint4>(me, sl.recv_x) + r * nvec;
+      for (int i = lane; i < nvec; i += 32) row[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (p.pad_rows) {
+    const int64_t n = (p.cap_rows - recv_total) * p.max_topk;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      at<int64_t>(me, sl.topk_idx)[recv_total * p.max_topk + i] = -1;
+      at<float>(me, sl.topk_w)[recv_total * p.max_topk + i] = 0.0f;
+    }
+  }
+
+  // Last block to finish tells every rank that this rank's rows have landed.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(p.done_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < p.world; ++d)
+        st_release_sys(at<uint64_t>(p.peers[d], p.lay.data_flag) + p.slot * p.world + p.rank,
+                       kernel_epoch(p));
+    }
+  }
 }
 
 // ----------------------------------------------------------------- combine --
@@ -953,6 +1097,67 @@ extern "C" int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch
   Params p = base_params(ep, slot, epoch, wait_ns, status);
   wait_data_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream_)>>>(p);
   return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_cached_begin(moe_ep_t ep, int32_t slot, uint64_t epoch,
+                                                void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1) return MOE_ERR_INVALID_ARG;
+  Params p = base_params(ep, slot, epoch, 0, nullptr);
+  cached_begin_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_cached_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                                  const float* topk_weights, int32_t num_tokens,
+                                                  int32_t topk, int32_t src_slot, int32_t slot,
+                                                  uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
+                                                  int32_t scale_rows, uint64_t wait_ns,
+                                                  int32_t* status, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || src_slot < 0 || src_slot > 1 || src_slot == slot ||
+      num_tokens < 0 || num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk ||
+      num_blocks < 1 ||
+      (num_tokens > 0 && (x == nullptr || topk_idx == nullptr || topk_weights == nullptr)) ||
+      !moe::aligned16(x))
+    return MOE_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  Params p = base_params(ep, slot, epoch, wait_ns, status);
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.topk_idx = topk_idx;
+  p.topk_w = topk_weights;
+  p.num_tokens = num_tokens;
+  p.topk = topk;
+  p.send_pos = ep->send_pos[slot];
+  p.cb_pos = ep->cb_pos[slot];
+  p.offsets_out = ep->offsets[slot];
+  p.done_ctr = ep->done_ctr;
+  p.pad_rows = pad_rows ? 1 : 0;
+  p.scale_rows = scale_rows ? 1 : 0;
+  p.host_info = ep->host_info;
+  p.src_slot = src_slot;
+  p.src_send_pos = ep->send_pos[src_slot];
+  p.src_cb_pos = ep->cb_pos[src_slot];
+  p.src_offsets = ep->offsets[src_slot];
+  if (cudaMemsetAsync(ep->done_ctr, 0, sizeof(unsigned int), stream) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  cached_scatter_kernel<<<num_blocks, kCommThreads, 0, stream>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_cached(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                          const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                          int32_t src_slot, int32_t slot, uint64_t epoch,
+                                          int32_t num_blocks, int32_t pad_rows, int32_t scale_rows,
+                                          uint64_t wait_ns, int32_t* status, void* stream) {
+  if (ep == nullptr || src_slot < 0 || src_slot > 1 || src_slot == slot) return MOE_ERR_INVALID_ARG;
+  int rc = moe_ep_dispatch_cached_begin(ep, slot, epoch, stream);
+  if (rc == MOE_OK)
+    rc = moe_ep_dispatch_cached_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, src_slot,
+                                        slot, epoch, num_blocks, pad_rows, scale_rows, wait_ns,
+                                        status, stream);
+  if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
+  return rc;
 }
 
 extern "C" int32_t moe_ep_combine_begin(moe_ep_t ep, int32_t slot, uint64_t epoch, void* stream_) {

@@ -67,6 +67,8 @@ class DispatchHandle:
     x: torch.Tensor
     recv_rows: Optional[int]
     combined: bool = False
+    stream: Optional[torch.cuda.Stream] = None  # where the dispatch ran, and its end
+    event: Optional[torch.cuda.Event] = None
 
 
 @dataclass
@@ -196,15 +198,34 @@ class DeepEPDispatcher:
             "moe_ep_dispatch_layout")
         return per_rank, None, per_expert, in_rank
 
-    def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
+    def dispatch(self, x: torch.Tensor, topk_idx: Optional[torch.Tensor] = None,
+                 topk_weights: Optional[torch.Tensor] = None,
                  previous_event: Optional[object] = None, *,
+                 handle: Optional["DispatchHandle"] = None,
                  exact_size: Optional[bool] = None, expert_alignment: int = 1,
                  scale_rows: bool = False, num_sms: Optional[int] = None,
                  pad_rows: Optional[bool] = None, inline: bool = False) -> DispatchResult:
+        """Sends each token's row to the ranks owning its top-k experts.
+
+        With ``handle`` (the handle of the most recent dispatch; ``topk_idx`` and
+        ``topk_weights`` then stay None, as in DeepEP's cached mode,
+        deep_ep/buffer.py:383-390) the rows of ``x`` go to the places that dispatch
+        gave its tokens: no layout or count phase, the same receive layout,
+        expert offsets and metadata, and with ``scale_rows`` that dispatch's
+        weights.  The result carries a new handle for the combine.
+        """
         if x.dtype != torch.bfloat16:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
             raise ValueError(f"x must be [num_tokens, {self.hidden_size}]")
+        if handle is not None:
+            if topk_idx is not None or topk_weights is not None:
+                raise ValueError("a cached dispatch takes the routing from its handle: "
+                                 "pass topk_idx=None and topk_weights=None")
+            return self._dispatch_cached(x, handle, previous_event, exact_size, scale_rows,
+                                         num_sms, pad_rows, inline)
+        if topk_idx is None or topk_weights is None:
+            raise ValueError("dispatch needs topk_idx and topk_weights (or the handle of a dispatch)")
         if topk_idx.dim() != 2 or topk_idx.shape[0] != x.shape[0] or topk_weights.shape != topk_idx.shape:
             raise ValueError("topk_idx and topk_weights must be [num_tokens, top_k]")
         num_tokens, topk = topk_idx.shape
@@ -242,7 +263,8 @@ class DeepEPDispatcher:
                 t.record_stream(self.comm_stream)
         views = self._ep.slots[slot]
         rows = self._ep.received_rows(slot, epoch) if exact else views.recv_x.shape[0]
-        handle = DispatchHandle(slot, epoch, num_tokens, topk, ic, wc, xc, rows if exact else None)
+        handle = DispatchHandle(slot, epoch, num_tokens, topk, ic, wc, xc, rows if exact else None,
+                                stream=stream, event=event)
         self._outstanding.append(handle)
         kcols = views.recv_topk_idx.stride(0)
         return DispatchResult(
@@ -250,6 +272,57 @@ class DeepEPDispatcher:
             recv_topk_idx=views.recv_topk_idx.as_strided((rows, topk), (kcols, 1)),
             recv_topk_weights=views.recv_topk_weights.as_strided((rows, topk), (kcols, 1)),
             handle=handle,
+            event=EventOverlap(event),
+            expert_offsets=offs,
+            recv_src=views.recv_src[:rows],
+        )
+
+    def _dispatch_cached(self, x, handle, previous_event, exact_size, scale_rows, num_sms, pad_rows,
+                         inline) -> DispatchResult:
+        if not isinstance(handle, DispatchHandle) or handle.epoch != self._epoch:
+            raise RuntimeError("a cached dispatch needs the handle of this dispatcher's most recent dispatch")
+        if x.shape[0] != handle.num_tokens:
+            raise ValueError(f"x must have the {handle.num_tokens} tokens of the handle's dispatch")
+        if len(self._outstanding) >= 2:
+            raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
+        exact = self.exact_size if exact_size is None else exact_size
+        if exact and self._device_epochs:
+            raise ValueError("exact_size needs host epochs; with device epochs use expert_offsets")
+        _lib.check_status(self.device)
+        self._epoch += 1
+        epoch, slot = self._epoch, self._epoch % 2
+        stream = self._enter_comm(previous_event, inline)
+        if handle.stream is not None and handle.stream != stream and handle.event is not None:
+            # The scatter reads the positions the handle's dispatch wrote on its stream.
+            stream.wait_event(handle.event)
+        with torch.cuda.stream(stream):
+            xc = x.contiguous()
+            if xc.data_ptr() % 16 != 0:
+                xc = xc.clone()
+            pad = (not exact) if pad_rows is None else bool(pad_rows)
+            self._ep.dispatch_cached(xc, handle.topk_idx, handle.topk_weights, handle.slot, slot,
+                                     0 if self._device_epochs else epoch, num_sms or self.num_sms, pad,
+                                     self.wait_ns, self._status, scale_rows)
+            offs = self._ep.slots[slot].expert_offsets
+            event = torch.cuda.Event()
+            event.record(stream)
+        if not inline and not torch.cuda.is_current_stream_capturing():
+            x.record_stream(self.comm_stream)
+        views = self._ep.slots[slot]
+        if exact:
+            rows = handle.recv_rows if handle.recv_rows is not None else self._ep.received_rows(slot, epoch)
+        else:
+            rows = views.recv_x.shape[0]
+        new = DispatchHandle(slot, epoch, handle.num_tokens, handle.topk, handle.topk_idx,
+                             handle.topk_weights, xc, rows if exact else None,
+                             stream=stream, event=event)
+        self._outstanding.append(new)
+        kcols = views.recv_topk_idx.stride(0)
+        return DispatchResult(
+            recv_x=views.recv_x[:rows],
+            recv_topk_idx=views.recv_topk_idx.as_strided((rows, handle.topk), (kcols, 1)),
+            recv_topk_weights=views.recv_topk_weights.as_strided((rows, handle.topk), (kcols, 1)),
+            handle=new,
             event=EventOverlap(event),
             expert_offsets=offs,
             recv_src=views.recv_src[:rows],

@@ -173,6 +173,34 @@ class Endpoint:
                                          self._stream()),
             "moe_ep_dispatch_end")
 
+    def dispatch_cached_begin(self, slot, epoch):
+        _lib.check_call(self.lib.moe_ep_dispatch_cached_begin(self.handle, slot, epoch, self._stream()),
+                        "moe_ep_dispatch_cached_begin")
+
+    def dispatch_cached_scatter(self, x, topk_idx, topk_w, src_slot, slot, epoch, num_blocks,
+                                pad_rows, wait_ns, status, scale_rows: bool = False):
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_cached_scatter(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                                    topk_w.data_ptr(), t, k, src_slot, slot, epoch,
+                                                    num_blocks, 1 if pad_rows else 0,
+                                                    1 if scale_rows else 0, wait_ns,
+                                                    status.data_ptr(), self._stream()),
+            "moe_ep_dispatch_cached_scatter")
+
+    def dispatch_cached(self, x, topk_idx, topk_w, src_slot, slot, epoch, num_blocks, pad_rows,
+                        wait_ns, status, scale_rows: bool = False):
+        """Rows x for the tokens and top-k choices of the dispatch into ``src_slot``,
+        in that dispatch's layout, into ``slot`` (see moe_ep_dispatch_cached)."""
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_cached(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                            topk_w.data_ptr(), t, k, src_slot, slot, epoch,
+                                            num_blocks, 1 if pad_rows else 0,
+                                            1 if scale_rows else 0, wait_ns, status.data_ptr(),
+                                            self._stream()),
+            "moe_ep_dispatch_cached")
+
     def combine_begin(self, slot, epoch):
         _lib.check_call(self.lib.moe_ep_combine_begin(self.handle, slot, epoch, self._stream()),
                         "moe_ep_combine_begin")
@@ -308,6 +336,23 @@ class LocalGroup:
         for r, ep in enumerate(self.eps):
             ep.dispatch_scatter(xs[r], idxs[r], ws[r], slot, epoch, self.num_blocks, pad_rows,
                                 self.wait_ns, self.status, expert_alignment, scale_rows)
+        for ep in self.eps:
+            ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
+        return slot, epoch
+
+    def dispatch_cached(self, xs, idxs, ws, src_slot: int, pad_rows: bool = False,
+                        scale_rows: bool = False):
+        """Cached re-dispatch of rows xs[r] in the layout of the dispatch into
+        ``src_slot`` (which must be the most recent one); idxs/ws are its inputs."""
+        if (self.epoch + 1) % 2 == src_slot:
+            raise ValueError("a cached dispatch follows the most recent dispatch (the other slot)")
+        self.epoch += 1
+        slot, epoch = self.epoch % 2, self._kernel_epoch(self.epoch)
+        for ep in self.eps:
+            ep.dispatch_cached_begin(slot, epoch)
+        for r, ep in enumerate(self.eps):
+            ep.dispatch_cached_scatter(xs[r], idxs[r], ws[r], src_slot, slot, epoch, self.num_blocks,
+                                       pad_rows, self.wait_ns, self.status, scale_rows)
         for ep in self.eps:
             ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
         return slot, epoch

@@ -351,7 +351,7 @@ class MoELayer:
                                inline=True)
         ev.current_stream_wait()
         self._mark("fwd_combine")
-        return out, dict(res=res, pre=pre, h=h, idx=idx, w=w.float())
+        return out, dict(res=res, pre=pre, h=h)
 
     def _train_backward(self, state: dict, dout: torch.Tensor):
         disp, res = self.dispatcher, state["res"]
@@ -368,10 +368,10 @@ class MoELayer:
         dw = disp.topk_weight_grad(dout, res.handle, num_sms=self.solo_comm_blocks)
         self._mark("bwd_topk_weight_grad")
         # The output gradient goes back to the experts weighted: dY = w * dout rows,
-        # laid out exactly like the forward rows (same routing and alignment).
-        rb = disp.dispatch(dout, state["idx"], state["w"], exact_size=False, pad_rows=False, inline=True,
-                           expert_alignment=TRAIN_ALIGNMENT, scale_rows=True,
-                           num_sms=self.solo_comm_blocks)
+        # laid out exactly like the forward rows: a cached dispatch on the forward's
+        # handle (same routing, alignment and receive layout; no layout/count phase).
+        rb = disp.dispatch(dout, handle=res.handle, exact_size=False, pad_rows=False, inline=True,
+                           scale_rows=True, num_sms=self.solo_comm_blocks)
         rb.event.current_stream_wait()
         self._mark("bwd_dispatch")
         d_pre = torch.empty_like(state["pre"])

@@ -106,6 +106,39 @@ def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: in
     return recv, send_pos
 
 
+def dispatch_cached(xs, topk_idxs, topk_weights, num_experts: int, src_recv, src_send_pos,
+                    scale_rows: bool = False):
+    """Cached re-dispatch (DeepEP's dispatch given a handle,
+    thirdParty/DeepEP/deep_ep/buffer.py:383-390): new rows ``xs`` for the tokens
+    and top-k choices of an earlier dispatch, whose result was (src_recv,
+    src_send_pos).  Each (token, slot) row goes to the row that dispatch gave it;
+    every receiver keeps that dispatch's metadata and offsets, and its alignment
+    padding rows are zero.  Same return shape as ``dispatch``.
+    """
+    world = len(xs)
+    per_rank = num_experts // world
+    recv = []
+    for d in range(world):
+        src = src_recv[d]
+        n = int(src["offsets"][-1])
+        rx = np.zeros((n, xs[0].shape[1]), dtype=np.uint16)
+        recv.append(dict(x=rx, topk_idx=src["topk_idx"].copy(), topk_weights=src["topk_weights"].copy(),
+                         src_rank=src["src_rank"].copy(), src_token=src["src_token"].copy(),
+                         offsets=src["offsets"].copy()))
+    for r in range(world):
+        idx = np.asarray(topk_idxs[r], dtype=np.int64)
+        for (t, j), row in np.ndenumerate(src_send_pos[r]):
+            e = int(idx[t, j])
+            if row < 0 or not 0 <= e < num_experts:
+                continue
+            if scale_rows:
+                prod = bf16_bits_to_f32(xs[r][t]) * np.float32(topk_weights[r][t, j])
+                recv[e // per_rank]["x"][row] = f32_to_bf16_bits(prod.astype(np.float32))
+            else:
+                recv[e // per_rank]["x"][row] = xs[r][t]
+    return recv, [np.array(s, copy=True) for s in src_send_pos]
+
+
 def topk_weight_grad(grad_outs, ys, topk_idxs, send_pos, num_experts: int):
     """d loss / d w[t, j] of the weighted combine: <grad_out[t], y_{owner}(row(t, j))>
     in float64 (the product sums in fp32 in its own order), 0 for empty slots."""

@@ -326,3 +326,99 @@ def test_push_gemm_combine_equals_pull_combine(cuda_device, world, topk):
             assert float(diff.max()) <= 2 ** -7 * float(np.abs(bf16_bits_to_f32(yo)).max()) + 1e-2
     finally:
         grp.close()
+
+
+@pytest.mark.parametrize("world,align,device_epochs", [(1, 64, False), (2, 64, False), (4, 16, True)])
+def test_cached_dispatch_matches_oracle(cuda_device, world, align, device_epochs):
+    """A cached re-dispatch of new rows on the previous dispatch's layout equals the
+    oracle's dispatch of those rows (scaled by the weights) bit for bit: rows,
+    metadata, offsets, padding and send positions; its combine is bit-exact too."""
+    tokens, topk, hidden, E = 301, 2, 256, 16
+    xs, idxs, ws = routing(world, tokens, E, topk, seed=500 + world, hidden=hidden)
+    g = torch.Generator().manual_seed(600 + world)
+    x2 = [torch.randn(tokens, hidden, generator=g).to(torch.bfloat16) for _ in range(world)]
+    grp = LocalGroup(world, E, hidden, tokens, topk, world * tokens * topk + E * align, num_blocks=6)
+    try:
+        if device_epochs:
+            grp.use_device_epochs()
+        di = [i.to(cuda_device) for i in idxs]
+        dw = [w.to(cuda_device) for w in ws]
+        src_slot, _ = grp.dispatch([x.to(cuda_device) for x in xs], di, dw, pad_rows=True,
+                                   expert_alignment=align)
+        # Garbage in the target slot's receive rows: padding rows must come out zero.
+        for ep in grp.eps:
+            ep.slots[1 - src_slot].recv_x.fill_(float("nan"))
+        slot, epoch = grp.dispatch_cached([x.to(cuda_device) for x in x2], di, dw, src_slot,
+                                          pad_rows=True, scale_rows=True)
+        torch.cuda.synchronize()
+        assert slot != src_slot
+        assert int(grp.status.item()) == 0, _lib.status_string(int(grp.status.item()))
+        recv, send_pos = oep.dispatch([to_storage(x) for x in x2], [i.numpy() for i in idxs],
+                                      [w.numpy() for w in ws], E, expert_alignment=align,
+                                      scale_rows=True)
+        ys = []
+        for d, ep in enumerate(grp.eps):
+            v, want = ep.slots[slot], recv[d]
+            n = int(want["offsets"][-1])
+            assert np.array_equal(v.expert_offsets.cpu().numpy(), want["offsets"])
+            assert np.array_equal(to_storage(v.recv_x[:n]), want["x"])
+            assert np.array_equal(v.recv_topk_idx[:n, :topk].cpu().numpy(), want["topk_idx"])
+            assert np.array_equal(v.recv_topk_weights[:n, :topk].cpu().numpy(), want["topk_weights"])
+            assert np.array_equal(v.recv_src[:n, 0].cpu().numpy(), want["src_rank"])
+            assert np.array_equal(v.recv_src[:n, 1].cpu().numpy(), want["src_token"])
+            assert bool((v.recv_topk_idx[n:] == -1).all())
+            y = (v.recv_x[:n].float() * 0.75 + 0.125).to(torch.bfloat16)
+            v.expert_out[:n].copy_(y)
+            ys.append(to_storage(y))
+        for r, ep in enumerate(grp.eps):
+            got = ep.slots[slot].send_pos[: tokens * topk].view(tokens, topk).cpu().numpy()
+            assert np.array_equal(got, send_pos[r])
+        outs = [torch.empty(tokens, hidden, dtype=torch.bfloat16, device=cuda_device)
+                for _ in range(world)]
+        grp.combine(di, dw, slot, epoch, False, outs)
+        torch.cuda.synchronize()
+        assert int(grp.status.item()) == 0
+        want = oep.combine(ys, [i.numpy() for i in idxs], send_pos, E)
+        for r in range(world):
+            assert np.array_equal(to_storage(outs[r]), want[r]), r
+    finally:
+        grp.close()
+
+
+def test_dispatcher_cached_dispatch_api(cuda_device):
+    """DeepEPDispatcher.dispatch(x, handle=...) (world 1): same rows as a full
+    dispatch with the handle's routing; misuse is rejected on the host."""
+    from moe_overlap_b200.deep_ep_comm import DeepEPDispatcher
+
+    tokens, topk, hidden, E = 257, 2, 128, 8
+    xs, idxs, ws = routing(1, tokens, E, topk, seed=77, hidden=hidden)
+    x2 = torch.randn(tokens, hidden, generator=torch.Generator().manual_seed(78)).to(torch.bfloat16)
+    disp = DeepEPDispatcher(None, hidden, E, num_sms=8, max_tokens_per_rank=tokens, max_top_k=topk)
+    try:
+        idx, w = idxs[0].to(cuda_device), ws[0].to(cuda_device)
+        first = disp.dispatch(xs[0].to(cuda_device), idx, w)
+        with pytest.raises(ValueError):
+            disp.dispatch(x2.to(cuda_device), idx, w, handle=first.handle)
+        with pytest.raises(ValueError):
+            disp.dispatch(x2[:-1].to(cuda_device), handle=first.handle)
+        again = disp.dispatch(x2.to(cuda_device), handle=first.handle)
+        again.event.current_stream_wait()
+        torch.cuda.synchronize()
+        recv, pos = oep.dispatch([to_storage(x2)], [idxs[0].numpy()], [ws[0].numpy()], E)
+        n = int(recv[0]["offsets"][-1])
+        assert again.recv_x.shape[0] == n
+        assert np.array_equal(to_storage(again.recv_x), recv[0]["x"])
+        assert np.array_equal(again.recv_topk_idx.cpu().numpy(), recv[0]["topk_idx"])
+        _, ev = disp.combine(first.recv_x.new_zeros(first.recv_x.shape), first.handle)
+        ev.current_stream_wait()
+        # the cached handle's slot is now the most recent; an older handle is refused
+        with pytest.raises(RuntimeError):
+            disp.dispatch(x2.to(cuda_device), handle=first.handle)
+        out2, ev2 = disp.combine(again.recv_x.clone(), again.handle)
+        ev2.current_stream_wait()
+        torch.cuda.synchronize()
+        # expert outputs = the received rows: each token comes back summed over its slots
+        want = oep.combine([recv[0]["x"]], [idxs[0].numpy()], pos, E)
+        assert np.array_equal(to_storage(out2), want[0])
+    finally:
+        disp.close()
