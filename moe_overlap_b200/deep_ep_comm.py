@@ -22,6 +22,8 @@ Differences a caller can see, all within the reference's contract:
     unused rows have ``recv_topk_idx == -1``.
   * ``combine(..., weighted=True)`` applies the dispatch's top-k weights inside
     the reduction (fused weighted combine).
+  * ``dispatch(x, handle=h)`` is DeepEP's cached mode: new rows on the layout of
+    the most recent dispatch ``h``, with no layout or count phase.
   * ``expert_gemm_push`` + ``combine_pushed`` fuse the combine's transfer into the
     down-projection GEMM (its epilogue writes rows to their source ranks);
     ``use_device_epochs`` makes every exchange kernel CUDA-graph-capturable;

@@ -175,8 +175,9 @@ def persistent_grouped_gemm(
     size; ``use_atomic_queue`` selects the global atomic tile queue, whose
     counter (``work_counter``, int32 ``[1]``) is reset by this call.  The
     Triton tuning knobs ``block_m/block_n/block_k/num_warps/num_stages`` are
-    accepted for compatibility; the kernel's tile shape is fixed at 128x256x64
-    (tcgen05 UMMA 128x256x16, four TMA stages).
+    accepted for compatibility; the tile shape is fixed: 256x256 per CTA pair
+    (tcgen05 cta_group::2 UMMA 256x256x16, six TMA stages of 64-deep k-blocks),
+    or 128x256 on the one-SM kernel used for a grid of one SM.
     """
     if a_cat.device.type != "cuda" or b_expert.device.type != "cuda":
         raise ValueError("persistent_grouped_gemm requires CUDA tensors.")
