@@ -85,9 +85,9 @@ class MoELayer:
         self.micro = max(1, int(micro_batch_size))
         self.taper = taper_chunks
         # The GEMM-fused combine push (expert_gemm_push + combine_pushed) is off by
-        # default: its epilogue stores rows one by one to their source ranks, which
-        # costs more GEMM time than the separate combine it removes (config 5 on
-        # 2 B200s: 1.70 vs 1.60 ms per step; config 4 on one: 2.55 vs 2.42 ms).
+        # default: with TMA bulk stores into the source ranks it ties the separate
+        # pull combine (config 5 on 2 B200s, per-step medians: 1.596 / 1.600 ms
+        # against 1.592 / 1.590 ms), and its longer GEMM hides the same exposure.
         self.fused_combine = bool(fused_combine) if fused_combine is not None else False
         self.use_atomic = use_atomic_queue
         self.device = torch.device("cuda", torch.cuda.current_device())
