@@ -189,3 +189,16 @@ def test_grouped_gemm_activation_codes_checked_on_host():
     ex_tail = (None, None, None, None, 64, None, None)
     for act in (_lib.MOE_ACT_DGELU, _lib.MOE_ACT_MUL_AUX, _lib.MOE_ACT_GELU_SAVE_GRAD):
         assert lib.moe_grouped_gemm_ex(*common, act, 1, 0, *ex_tail) == _lib.MOE_ERR_INVALID_ARG, act
+
+
+def test_cached_dispatch_entry_points_reject_bad_arguments_on_host():
+    """Without an endpoint, or with the source slot equal to the target slot, the
+    cached re-dispatch returns MOE_ERR_INVALID_ARG before any CUDA call."""
+    lib = _lib.load()
+    bad = _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_ep_dispatch_cached_begin(None, 0, 1, None) == bad
+    for src_slot, slot in ((0, 1), (1, 1), (2, 0), (0, -1)):
+        assert lib.moe_ep_dispatch_cached_scatter(None, None, None, None, 4, 2, src_slot, slot, 1, 8,
+                                                  0, 0, 10**9, None, None) == bad, (src_slot, slot)
+        assert lib.moe_ep_dispatch_cached(None, None, None, None, 4, 2, src_slot, slot, 1, 8, 0, 0,
+                                          10**9, None, None) == bad, (src_slot, slot)
