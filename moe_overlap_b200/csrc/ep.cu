@@ -1150,7 +1150,12 @@ extern "C" int32_t moe_ep_dispatch_cached(moe_ep_t ep, const void* x, const int6
                                           int32_t src_slot, int32_t slot, uint64_t epoch,
                                           int32_t num_blocks, int32_t pad_rows, int32_t scale_rows,
                                           uint64_t wait_ns, int32_t* status, void* stream) {
-  if (ep == nullptr || src_slot < 0 || src_slot > 1 || src_slot == slot) return MOE_ERR_INVALID_ARG;
+  if (ep == nullptr || src_slot < 0 || src_slot > 1 || slot < 0 || slot > 1 || src_slot == slot ||
+      num_tokens < 0 || num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk ||
+      num_blocks < 1 ||
+      (num_tokens > 0 && (x == nullptr || topk_idx == nullptr || topk_weights == nullptr)) ||
+      !moe::aligned16(x))
+    return MOE_ERR_INVALID_ARG;  // checked before the begin phase raises any flag
   int rc = moe_ep_dispatch_cached_begin(ep, slot, epoch, stream);
   if (rc == MOE_OK)
     rc = moe_ep_dispatch_cached_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, src_slot,
@@ -1281,6 +1286,11 @@ extern "C" int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* to
                                    int32_t slot, uint64_t epoch, int32_t num_blocks,
                                    int32_t pad_rows, int32_t expert_alignment, int32_t scale_rows,
                                    uint64_t wait_ns, int32_t* status, void* stream) {
+  // Every argument the later phases check is checked here first: a phase that
+  // fails after the begin phase has raised this rank's count flag would leave the
+  // peers waiting for rows that never come.
+  if (num_blocks < 1 || expert_alignment < 1 || expert_alignment > 4096)
+    return MOE_ERR_INVALID_ARG;
   int rc = moe_ep_dispatch_begin(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
                                  status, stream);
   if (rc == MOE_OK)

@@ -237,6 +237,10 @@ class DeepEPDispatcher:
                 f"({self.max_tokens} x {self.max_topk}); raise MOE_B200_MAX_TOKENS / MOE_B200_MAX_TOPK")
         if len(self._outstanding) >= 2:
             raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
+        if not 1 <= int(expert_alignment) <= 4096:
+            raise ValueError("expert_alignment must be in [1, 4096]")
+        if num_sms is not None and int(num_sms) < 1:
+            raise ValueError("num_sms must be at least 1")
         exact = self.exact_size if exact_size is None else exact_size
         if exact and self._device_epochs:
             raise ValueError("exact_size needs host epochs; with device epochs use expert_offsets")
@@ -287,6 +291,8 @@ class DeepEPDispatcher:
             raise ValueError(f"x must have the {handle.num_tokens} tokens of the handle's dispatch")
         if len(self._outstanding) >= 2:
             raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
+        if num_sms is not None and int(num_sms) < 1:
+            raise ValueError("num_sms must be at least 1")
         exact = self.exact_size if exact_size is None else exact_size
         if exact and self._device_epochs:
             raise ValueError("exact_size needs host epochs; with device epochs use expert_offsets")
