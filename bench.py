@@ -316,20 +316,28 @@ class ClockSampler(threading.Thread):
 
     def stop(self) -> dict:
         self._stop_evt.set()
-        self.join(timeout=2)
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
-        mask = 0
-        for s in busy:
-            mask |= s[1]
-        return {
-            "sm_mhz": int(statistics.median(s[0] for s in busy)),
-            "sm_max_mhz": self.max_mhz,
-            "reasons": [name for bit, name in _REASONS.items() if mask & bit and bit != 0x1],
-            "samples": len(busy),
-            "power_w_max": round(max(s[2] for s in busy), 1),
-        }
+        if self.is_alive():
+            self.join(timeout=2)
+        return summarize_clocks(self.samples, self.max_mhz)
+
+
+def summarize_clocks(samples, max_mhz) -> dict:
+    """The line's ``clocks`` object from (sm MHz, event-reason mask, watts) samples:
+    median SM clock and the union of reasons over the samples taken while the GPU
+    was not idle (all samples if it always was); the idle bit itself is not listed."""
+    if not samples:
+        return {"sm_mhz": None, "sm_max_mhz": max_mhz, "reasons": [], "samples": 0}
+    busy = [s for s in samples if not (s[1] & 0x1)] or list(samples)
+    mask = 0
+    for s in busy:
+        mask |= s[1]
+    return {
+        "sm_mhz": int(statistics.median(s[0] for s in busy)),
+        "sm_max_mhz": max_mhz,
+        "reasons": [name for bit, name in _REASONS.items() if mask & bit and bit != 0x1],
+        "samples": len(busy),
+        "power_w_max": round(max(s[2] for s in busy), 1),
+    }
 
 
 # ---------------------------------------------------------------- GPU side --

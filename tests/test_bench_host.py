@@ -53,3 +53,17 @@ def test_exchange_row_totals_ignore_rows_kept_locally():
     assert rows[0, 0] == 13132.0  # the caller's matrix is left as it was
     out1, in1 = bench.exchange_row_totals(torch.tensor([[5.0]]))
     assert out1 == [0.0] and in1 == [0.0]
+
+
+def test_clock_summary_skips_idle_samples_and_names_reasons():
+    samples = [(1965, 0x1, 120.0),            # idle: left out
+               (1965, 0x0, 900.0),
+               (1890, 0x4, 1000.0),           # sw_power_cap
+               (1965, 0x4 | 0x20, 950.0)]     # + sw_thermal_slowdown
+    c = bench.summarize_clocks(samples, 1965)
+    assert c["samples"] == 3 and c["sm_max_mhz"] == 1965
+    assert c["sm_mhz"] == 1965 and c["power_w_max"] == 1000.0
+    assert c["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
+    assert bench.summarize_clocks([], 1965)["samples"] == 0
+    only_idle = bench.summarize_clocks([(300, 0x1, 80.0)], 1965)
+    assert only_idle["samples"] == 1 and only_idle["reasons"] == []
