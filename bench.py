@@ -341,6 +341,23 @@ def summarize_clocks(samples, max_mhz) -> dict:
 
 
 # ---------------------------------------------------------------- GPU side --
+def reduce_e2e_legs(serial_ms: float, pipe_ms: float, world: int, device) -> tuple[float, float]:
+    """Max over ranks of both end-to-end legs; the pipelined one counts only if every
+    rank has it (a rank that fell back passes -1).  Every rank makes the same two
+    all-reduces, whatever its own result."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([serial_ms, pipe_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        t_min = t.clone()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t_min, op=dist.ReduceOp.MIN)
+        if float(t_min[1].item()) < 0:
+            t[1] = -1.0
+    return float(t[0].item()), float(t[1].item())
+
+
 def exchange_row_totals(row_matrix) -> tuple[list[float], list[float]]:
     """Remote rows each rank sends and receives, from rows[src, dst] (rows a rank
     keeps for its own experts cross no link)."""
@@ -910,14 +927,7 @@ def main() -> None:
         except RuntimeError as exc:  # keep the serial figure, say why
             print(f"bench: pipelined end-to-end leg not used: {exc}", file=sys.stderr, flush=True)
             pipe_ms = -1.0
-        t = torch.tensor([serial_ms, pipe_ms], dtype=torch.float64, device=device)
-        if world > 1:
-            t_min = t.clone()
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            dist.all_reduce(t_min, op=dist.ReduceOp.MIN)
-            if float(t_min[1].item()) < 0:
-                t[1] = -1.0  # a rank without the pipelined figure: report the serial one
-        serial_ms, pipe_ms = float(t[0].item()), float(t[1].item())
+        serial_ms, pipe_ms = reduce_e2e_legs(serial_ms, pipe_ms, world, device)
         mo.check_status(device, sync=True)
         e2e_ms = pipe_ms if pipe_ms > 0 else serial_ms
         e2e = {

@@ -1,8 +1,10 @@
-"""Host-side pieces of bench.py: the BASELINE workloads' shapes and the config-5 gate bias."""
+"""Host-side pieces of bench.py: workload shapes, the config-5 gate bias, exchange row
+totals, the clock summary and the cross-rank reduction of the end-to-end legs."""
 import sys
 from pathlib import Path
 
 import numpy as np
+import pytest
 
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 import bench  # noqa: E402
@@ -67,3 +69,37 @@ def test_clock_summary_skips_idle_samples_and_names_reasons():
     assert bench.summarize_clocks([], 1965)["samples"] == 0
     only_idle = bench.summarize_clocks([(300, 0x1, 80.0)], 1965)
     assert only_idle["samples"] == 1 and only_idle["reasons"] == []
+
+
+def _e2e_rank(rank, world, port, pipe_ms, q):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q.put((rank, bench.reduce_e2e_legs(10.0 + rank, pipe_ms[rank], world, "cpu")))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("pipe_ms,want", [((6.0, 7.0), (11.0, 7.0)), ((6.0, -1.0), (11.0, -1.0))])
+def test_e2e_legs_reduce_over_gloo_ranks(pipe_ms, want):
+    """Max over ranks; one rank without the pipelined figure makes every rank report -1."""
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_e2e_rank, args=(r, 2, port, pipe_ms, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0] == want and got[1] == want
