@@ -202,3 +202,45 @@ def test_cached_dispatch_entry_points_reject_bad_arguments_on_host():
                                                   0, 0, 10**9, None, None) == bad, (src_slot, slot)
         assert lib.moe_ep_dispatch_cached(None, None, None, None, 4, 2, src_slot, slot, 1, 8, 0, 0,
                                           10**9, None, None) == bad, (src_slot, slot)
+
+
+C_CLIENT = r"""
+#include <stdio.h>
+#include <string.h>
+#include "moe_overlap.h"
+int main(void) {
+  int32_t counts[4] = {3, 0, 5, 2};
+  int64_t off[5];
+  if (moe_expert_offsets_host(counts, 0, 4, off, 1) != MOE_OK) return 1;
+  if (off[0] != 0 || off[1] != 3 || off[2] != 3 || off[3] != 8 || off[4] != 10) return 2;
+  if (moe_abi_version() != MOE_ABI_VERSION) return 3;
+  if (strlen(moe_status_string(MOE_ERR_TIMEOUT)) == 0) return 4;
+  if (moe_ep_dispatch_cached_begin(NULL, 0, 1, NULL) != MOE_ERR_INVALID_ARG) return 5;
+  puts("ok");
+  return 0;
+}
+"""
+
+
+def test_header_is_plain_c_and_a_c_program_links_the_library(tmp_path):
+    """A C host (no C++, no torch) compiles against include/moe_overlap.h with
+    -std=c99 -pedantic -Werror, links the library and calls its host-side entry points."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    repo = Path(__file__).resolve().parents[1]
+    _lib.load()  # fails loudly if the library is not built
+    lib = _lib.LIB_PATH
+    src = tmp_path / "client.c"
+    src.write_text(C_CLIENT)
+    exe = tmp_path / "client"
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                        "-I", str(repo / "include"), str(src), "-L", str(lib.parent),
+                        "-l" + lib.stem[3:], f"-Wl,-rpath,{lib.parent}", "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.strip() == "ok", (run.returncode, run.stdout, run.stderr)
