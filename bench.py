@@ -105,6 +105,9 @@ def parse_args() -> argparse.Namespace:
                          "combine (auto: the layer's default, pull)")
     ap.add_argument("--timeline", action="store_true",
                     help="layer workloads: add per-rank phase-boundary times of one forward")
+    ap.add_argument("--nvtx", action="store_true",
+                    help="layer workloads: NVTX ranges per chunk, named as the reference's "
+                         "(deepep_dispatch_chunk_i, expert_compute_chunk_i, deepep_combine_chunk_i)")
     ap.add_argument("--taper", action="store_true",
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
@@ -417,6 +420,7 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
                      micro_batch_size=args.micro_batch,
                      taper_chunks=args.taper,
                      fused_combine=None if args.combine == "auto" else args.combine == "push",
+                     enable_nvtx=args.nvtx,
                      ).init_random(std=0.02, seed=0)
     bias_info = None
     if cfg["zipf_bias"]:

@@ -24,6 +24,7 @@ TrainStepGraph to replay a whole training step as one CUDA graph.
 """
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from typing import Optional
 
@@ -37,6 +38,21 @@ from .router import router_topk
 # Expert segments of a training dispatch are padded to this many rows so the
 # weight-gradient GEMM's 64-row k-blocks never straddle two experts.
 TRAIN_ALIGNMENT = 64
+
+
+@contextlib.contextmanager
+def nvtx_range(name: str, enabled: bool):
+    """An NVTX range around host-side enqueueing when ``enabled`` (and CUDA is
+    present), as the reference's SimpleMoE marks its chunks with --enable-nvtx
+    (src/train_moe_baseline.py:74-83)."""
+    if enabled and torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
 
 
 @dataclass
@@ -72,8 +88,12 @@ class MoELayer:
                  router_bias: bool = False, num_comm_sms: int = 148,
                  micro_batch_size: int = 4096, use_atomic_queue: bool = True,
                  max_recv_rows: Optional[int] = None, training: bool = False,
-                 taper_chunks: bool = False, fused_combine: Optional[bool] = None):
+                 taper_chunks: bool = False, fused_combine: Optional[bool] = None,
+                 enable_nvtx: bool = False):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
+        # NVTX ranges named as the reference's (deepep_dispatch_chunk_i,
+        # expert_compute_chunk_i, deepep_combine_chunk_i; train_moe_baseline.py:364-413)
+        self.enable_nvtx = enable_nvtx
         self.group = group
         self.world = group.size() if group is not None else 1
         self.rank = group.rank() if group is not None else 0
@@ -212,15 +232,17 @@ class MoELayer:
         self._timeline_mark(timeline, "start", cur_stream)
         # The first dispatch and the last combine have no GEMM beside them: they get
         # the solo grid; the others run one block per SM beside the GEMMs.
-        cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
-                            w[chunks[0][0]:chunks[0][1]], pad_rows=False,
-                            num_sms=self.solo_comm_blocks)
+        nv = self.enable_nvtx
+        with nvtx_range("deepep_dispatch_chunk_0", nv):
+            cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
+                                w[chunks[0][0]:chunks[0][1]], pad_rows=False,
+                                num_sms=self.solo_comm_blocks)
         self._timeline_mark(timeline, "dispatch0_end", disp.comm_stream)
         for i, (s, e) in enumerate(chunks):
             # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
             # starts them as soon as this chunk's rows have landed, and the host
             # time spent enqueuing the next dispatch overlaps them.
-            with torch.cuda.stream(self.compute_stream):
+            with torch.cuda.stream(self.compute_stream), nvtx_range(f"expert_compute_chunk_{i}", nv):
                 cur.event.current_stream_wait()
                 self._timeline_mark(timeline, f"gemm{i}_start", self.compute_stream)
                 y = self._experts(cur)
@@ -230,11 +252,13 @@ class MoELayer:
             nxt = None
             if i + 1 < len(chunks):
                 ns, ne = chunks[i + 1]
-                nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
+                with nvtx_range(f"deepep_dispatch_chunk_{i + 1}", nv):
+                    nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
                 self._timeline_mark(timeline, f"dispatch{i + 1}_end", disp.comm_stream)
             last = i + 1 == len(chunks)
-            self._combine(y, cur.handle, previous_event=done, out=out[s:e],
-                          num_sms=self.solo_comm_blocks if last else None)
+            with nvtx_range(f"deepep_combine_chunk_{i}", nv):
+                self._combine(y, cur.handle, previous_event=done, out=out[s:e],
+                              num_sms=self.solo_comm_blocks if last else None)
             self._timeline_mark(timeline, f"combine{i}_end", disp.comm_stream)
             cur = nxt
         torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)

@@ -9,6 +9,7 @@ statistics to 1e-5.
 from pathlib import Path
 
 import numpy as np
+import pytest
 
 from oracle import moe_layer as ol
 
@@ -92,3 +93,25 @@ def test_package_classes_define_each_method_once():
                                      for d in f.decorator_list)]
                 dup = {n for n in names if names.count(n) > 1}
                 assert not dup, (path.name, node.name, dup)
+
+
+def test_nvtx_range_is_balanced_and_a_no_op_when_off(monkeypatch):
+    """The layer's NVTX ranges (reference names, enabled by enable_nvtx) push and pop
+    once each, also when the body raises, and touch nothing when disabled."""
+    import torch
+
+    from moe_overlap_b200.layer import nvtx_range
+
+    calls = []
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda n: calls.append(("push", n)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop",)))
+    with nvtx_range("deepep_dispatch_chunk_0", True):
+        pass
+    with pytest.raises(ValueError):
+        with nvtx_range("expert_compute_chunk_0", True):
+            raise ValueError("x")
+    with nvtx_range("deepep_combine_chunk_0", False):
+        pass
+    assert calls == [("push", "deepep_dispatch_chunk_0"), ("pop",),
+                     ("push", "expert_compute_chunk_0"), ("pop",)]
