@@ -512,6 +512,9 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
+        # ~1.5 ms of device-side delay first: the host enqueues the whole forward
+        # meanwhile, so the marks show the device's schedule, not the host's launches.
+        torch.cuda._sleep(3_000_000)
         layer(x, routing=routing, timeline=marks)
         torch.cuda.synchronize(device)
         mine = {name: round(marks[0][1].elapsed_time(ev), 4) for name, ev in marks[1:]}

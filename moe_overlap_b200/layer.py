@@ -268,14 +268,19 @@ class MoELayer:
 
     __call__ = forward
 
-    def forward_serialized(self, x: torch.Tensor, routing) -> tuple[torch.Tensor, dict]:
+    def forward_serialized(self, x: torch.Tensor, routing,
+                           host_cover_cycles: int = 2_000_000) -> tuple[torch.Tensor, dict]:
         """The same forward with every phase run alone, for overlap accounting.
 
         Each chunk's dispatch, expert GEMMs and combine run one after another
         with a device synchronisation (and, across ranks, a barrier) between
         phases; returns the output and the summed device time of each phase in
         ms (max over ranks), i.e. the serial times that the overlapped forward
-        hides behind each other.
+        hides behind each other.  Each phase is enqueued behind a device-side
+        delay of ``host_cover_cycles`` SM cycles (~1 ms), started before its
+        events, so the host's enqueueing of the phase (argument checks and
+        several launches) happens while the GPU is busy and the events time the
+        phase's device work only, as it runs inside the pipelined forward.
         """
         x = x.to(torch.bfloat16).contiguous()
         _, idx, w = routing
@@ -288,6 +293,8 @@ class MoELayer:
         def timed(key, fn):
             self._sync_all()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if host_cover_cycles > 0:
+                torch.cuda._sleep(int(host_cover_cycles))
             start.record()
             r = fn()
             torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
