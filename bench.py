@@ -640,6 +640,9 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
         layer.trace.append((name, ev))
 
     layer.trace = []
+    # ~2 ms of device-side delay first: the host enqueues the step meanwhile (the step
+    # has no host synchronisation), so the marks time device work, not host launches.
+    torch.cuda._sleep(4_000_000)
     mark("step_start")
     step(x, dout)
     mark("router_bwd")
