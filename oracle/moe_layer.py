@@ -67,7 +67,7 @@ def layer_forward_bf16(x_bits, idx, w, w1_bits, w2_bits, expert_offset: int = 0,
     """The build's rounding points, for a given routing; returns bf16 bits [T, H].
 
     With ``return_magnitude`` also returns sum_j |w_j * y_j| per element, the
-    scale against which rounding differences of the summed terms are judged.
+    scale against which rounding differences of the summed terms are measured.
 
     x_bits [T, H], w1_bits [E_local, F, H], w2_bits [E_local, H, F] are bf16 bit
     patterns; idx holds global expert ids (experts outside
@@ -167,7 +167,7 @@ def experts_backward_bf16(x_bits, idx, w, w1_bits, w2_bits, dout_bits):
       ``dw``   float64 [T, k]:  <dout, y>;
       ``dw1``  bf16 bits [E, F, H] = sum dpre^T x;  ``dw2`` bf16 bits [E, H, F] = sum dy^T h;
       ``mag_dx``, ``mag_dw1``, ``mag_dw2``: the sums of absolute terms behind each
-      element, against which summation-order differences are judged.
+      element, against which summation-order differences are measured.
     """
     t_count, hidden = x_bits.shape
     n_exp, ffn, _ = w1_bits.shape
