@@ -721,7 +721,9 @@ __global__ void __launch_bounds__(kPullThreads, kCommMinBlocks) pull_kernel(Para
         // The owner's GEMM pushed this (token, slot) row into our combine rows.
         srcs[ns] = at<const uint4>(p.peers[p.rank], sl.cb) + static_cast<int64_t>(p.cb_pos[a]) * nvec;
       } else {
-        const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
+        const int64_t ev = p.topk_idx[a];
+        if (ev < 0 || ev >= p.num_experts) continue;  // not the dispatch's ids: nothing to pull
+        const int d = static_cast<int>(ev) / p.per_rank;
         srcs[ns] = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
       }
       scale[ns] = p.weighted ? p.topk_w[a] : 1.0f;
@@ -745,8 +747,9 @@ __global__ void __launch_bounds__(256) topk_weight_grad_kernel(Params p, const _
     const int t = a / p.topk;
     const int row = p.send_pos[a];
     float acc = 0.0f;
-    if (row >= 0) {
-      const int d = static_cast<int>(p.topk_idx[a]) / p.per_rank;
+    const int64_t ev = p.topk_idx[a];
+    if (row >= 0 && ev >= 0 && ev < p.num_experts) {
+      const int d = static_cast<int>(ev) / p.per_rank;
       const uint4* y = at<const uint4>(p.peers[d], sl.y) + static_cast<int64_t>(row) * nvec;
       const uint4* g = reinterpret_cast<const uint4*>(grad_out + static_cast<int64_t>(t) * p.hidden);
       for (int i = lane; i < nvec; i += 32) {

@@ -143,14 +143,17 @@ __global__ void __launch_bounds__(32 * kWarps) topk_bwd_kernel(const float* prob
   float dsel = 0.0f;  // lane j < k holds dp for slot j
   int esel = -1;
   if (lane < k) {
-    esel = static_cast<int>(idx[static_cast<int64_t>(t) * k + lane]);
-    dsel = dw[static_cast<int64_t>(t) * k + lane];
+    const int64_t ev = idx[static_cast<int64_t>(t) * k + lane];
+    if (ev >= 0 && ev < E) {  // an id outside [0, E) selects nothing and reads nothing
+      esel = static_cast<int>(ev);
+      dsel = dw[static_cast<int64_t>(t) * k + lane];
+    }
   }
   if (renormalize) {
-    const float ps = (lane < k) ? prow[esel] : 0.0f;
+    const float ps = (esel >= 0) ? prow[esel] : 0.0f;
     const float s = warp_sum(ps);
     const float wj = ps / s;
-    const float dot = warp_sum(lane < k ? dsel * wj : 0.0f);
+    const float dot = warp_sum(esel >= 0 ? dsel * wj : 0.0f);
     dsel = (dsel - dot) / s;
   }
   float dp[kPerLane], pv[kPerLane], inner = 0.0f;
