@@ -86,7 +86,8 @@ __global__ void __launch_bounds__(32 * kWarps) topk_fwd_kernel(const T* logits, 
     const int e = lane + 32 * i;
     if (e < E) probs[static_cast<int64_t>(t) * E + e] = p[i];
   }
-  // k rounds of a warp arg-max; a taken expert is marked with -1.
+  // k rounds of a warp arg-max; a taken expert is marked with -1 (probabilities
+  // are >= 0, so the mark never ties a candidate).
   float taken_w[kMaxK];
   int taken_e[kMaxK];
   float wsum = 0.0f;
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(32 * kWarps) topk_fwd_kernel(const T* logits, 
 #pragma unroll
     for (int i = 0; i < kPerLane; ++i) {
       const int e = lane + 32 * i;
-      if (e < E && (p[i] > best || (p[i] == best && e < be))) {
+      if (e < E && p[i] != -1.0f && (p[i] > best || (p[i] == best && e < be))) {
         best = p[i];
         be = e;
       }
@@ -109,6 +110,21 @@ __global__ void __launch_bounds__(32 * kWarps) topk_fwd_kernel(const T* logits, 
         best = ob;
         be = oe;
       }
+    }
+    if (be == 0x7fffffff) {
+      // No comparable candidate: a NaN logit makes every probability NaN.  Take
+      // the lowest expert id not taken yet, as a stable sort of all-equal values
+      // would (the same in every lane, so the branch is warp-uniform).
+      int ce = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && p[i] != -1.0f && e < ce) ce = e;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ce = min(ce, __shfl_xor_sync(0xffffffffu, ce, o));
+      be = ce;
+      best = __int_as_float(0x7fc00000);  // its probability: NaN
     }
 #pragma unroll
     for (int i = 0; i < kPerLane; ++i)

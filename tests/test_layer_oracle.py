@@ -115,3 +115,14 @@ def test_nvtx_range_is_balanced_and_a_no_op_when_off(monkeypatch):
         pass
     assert calls == [("push", "deepep_dispatch_chunk_0"), ("pop",),
                      ("push", "expert_compute_chunk_0"), ("pop",)]
+
+
+def test_oracle_topk_takes_the_lowest_ids_for_a_nan_row():
+    """A NaN logit makes the row's probabilities NaN; the oracle's stable sort then
+    keeps id order, so the row takes experts 0..k-1 (the router kernel matches it)."""
+    z = np.random.default_rng(0).normal(size=(3, 16)).astype(np.float32)
+    z[1, 5] = np.nan
+    with np.errstate(invalid="ignore"):
+        probs, idx, _ = ol.topk_from_logits(z, 3, renormalize=True)
+    assert idx[1].tolist() == [0, 1, 2]
+    assert np.isnan(probs[1]).all() and np.isfinite(probs[[0, 2]]).all()

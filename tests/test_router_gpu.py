@@ -76,3 +76,24 @@ def test_router_topk_rejects_bad_shapes(cuda_device):
         router_topk(torch.zeros(4, 300, device=cuda_device), 2)  # more than 256 experts
     with pytest.raises(MoeError):
         router_topk(torch.zeros(4, 8, device=cuda_device), 9)  # top_k > experts
+
+
+def test_router_topk_nan_row_takes_the_lowest_ids(cuda_device):
+    """A row with a NaN logit (all its probabilities NaN) gets experts 0..k-1 as the
+    oracle's stable sort does; other rows are unaffected; every id is in range and
+    the backward reads only in-range ids."""
+    t, e, k = 40, 16, 3
+    logits = _logits(t, e, torch.float32, seed=99)
+    logits[7, 3] = float("nan")
+    dl = logits.to(cuda_device).requires_grad_(True)
+    probs, idx, w = router_topk(dl, k, renormalize=True)
+    w.backward(torch.ones(t, k, device=cuda_device))
+    torch.cuda.synchronize()
+    got_i = idx.cpu().numpy()
+    assert got_i.min() >= 0 and got_i.max() < e
+    with np.errstate(invalid="ignore"):
+        want_p, want_i, _ = ol.topk_from_logits(logits.numpy(), k, None, True)
+    assert got_i[7].tolist() == [0, 1, 2] == want_i[7].tolist()
+    rows = [r for r in range(t) if r != 7]
+    np.testing.assert_allclose(probs.detach().cpu().numpy()[rows], want_p[rows], rtol=2e-6, atol=1e-9)
+    assert np.isfinite(dl.grad.cpu().numpy()[rows]).all()
