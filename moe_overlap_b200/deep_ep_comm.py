@@ -186,8 +186,16 @@ class DeepEPDispatcher:
             self.comm_stream.wait_stream(cur)
         return stream
 
+    def _require_on_device(self, **tensors) -> None:
+        """The exchange kernels take raw pointers: every operand must be on this
+        dispatcher's GPU (a host pointer handed to a kernel would fault it)."""
+        for name, t in tensors.items():
+            if t is not None and t.device != self.device:
+                raise ValueError(f"{name} must be on {self.device}, not {t.device}")
+
     def get_dispatch_layout(self, topk_idx: torch.Tensor, num_experts: int):
         """(num_tokens_per_rank, None, num_tokens_per_expert, is_token_in_rank) as DeepEP returns."""
+        self._require_on_device(topk_idx=topk_idx)
         idx = topk_idx.to(torch.int64).contiguous()
         t, k = idx.shape
         per_rank = torch.empty(self.world, dtype=torch.int32, device=idx.device)
@@ -220,6 +228,7 @@ class DeepEPDispatcher:
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
             raise ValueError(f"x must be [num_tokens, {self.hidden_size}]")
+        self._require_on_device(x=x, topk_idx=topk_idx, topk_weights=topk_weights)
         if handle is not None:
             if topk_idx is not None or topk_weights is not None:
                 raise ValueError("a cached dispatch takes the routing from its handle: "
@@ -374,6 +383,7 @@ class DeepEPDispatcher:
         the dispatch after next reuses that slot.
         """
         self._check_slot_live(handle)
+        self._require_on_device(grad_out=grad_out)
         if grad_out.shape != (handle.num_tokens, self.hidden_size):
             raise ValueError(f"grad_out must be [{handle.num_tokens}, {self.hidden_size}]")
         out = torch.empty(handle.num_tokens, handle.topk, dtype=torch.float32, device=self.device)
@@ -396,6 +406,7 @@ class DeepEPDispatcher:
         if expert_out.dtype != torch.bfloat16 or expert_out.dim() != 2 or \
                 expert_out.size(1) != self.hidden_size:
             raise ValueError(f"expert_out must be bf16 [rows, {self.hidden_size}]")
+        self._require_on_device(expert_out=expert_out, out=out)
         if self._outstanding and self._outstanding[0] is not handle:
             raise RuntimeError("combine the oldest outstanding dispatch first")
         _lib.check_status(self.device)
@@ -438,6 +449,7 @@ class DeepEPDispatcher:
         ``combine_pushed(handle, ...)``.
         """
         self._check_slot_live(handle)
+        self._require_on_device(h=h, weight=weight, work_counter=work_counter)
         if h.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
             raise ValueError("expert_gemm_push expects bf16 rows and weights")
         if weight.dim() != 3 or weight.shape[0] != self.experts_per_rank or \

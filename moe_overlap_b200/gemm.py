@@ -30,6 +30,16 @@ _ACT_CODE = {None: _lib.MOE_ACT_NONE, "none": _lib.MOE_ACT_NONE, "gelu": _lib.MO
              "mul_aux": _lib.MOE_ACT_MUL_AUX}
 
 
+def _require_on_device(device: torch.device, **tensors) -> None:
+    """Every given tensor must be a CUDA tensor on ``device``: the kernels take raw
+    pointers, and a host pointer handed to one would fault the GPU."""
+    if device.type != "cuda":
+        raise ValueError("grouped GEMM operands must be CUDA tensors")
+    for name, t in tensors.items():
+        if t is not None and t.device != device:
+            raise ValueError(f"{name} must be on {device}, not {t.device}")
+
+
 def _aligned(t: torch.Tensor) -> bool:
     return t.data_ptr() % 16 == 0
 
@@ -85,6 +95,8 @@ def grouped_gemm(
     ``w.transpose(1, 2)`` of ``[E, N, K]`` weights; no copy is made for either.
     """
     device = a_cat.device
+    _require_on_device(device, b_expert=b_expert, expert_offsets=expert_offsets, out=out,
+                       work_counter=work_counter, row_scale=row_scale, aux_in=aux_in, aux_out=aux_out)
     m_total, k_size = a_cat.shape
     num_experts, _, n_size = b_expert.shape
     dtype_code = _DTYPE_CODE[a_cat.dtype]
@@ -311,6 +323,7 @@ def grouped_gemm_wgrad(a: torch.Tensor, b: torch.Tensor, expert_offsets: torch.T
     exchange's ``expert_alignment=64``).  Returns ``[E, M, N]`` in the input dtype.
     """
     device = a.device
+    _require_on_device(device, b=b, expert_offsets=expert_offsets, out=out)
     rows, m = a.shape
     num_experts = expert_offsets.numel() - 1
     n = b.shape[1]

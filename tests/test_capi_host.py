@@ -244,3 +244,32 @@ def test_header_is_plain_c_and_a_c_program_links_the_library(tmp_path):
     assert r.returncode == 0, r.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.strip() == "ok", (run.returncode, run.stdout, run.stderr)
+
+
+def test_extended_gemm_entry_points_refuse_host_tensors():
+    """grouped_gemm / grouped_gemm_wgrad hand raw pointers to the kernels: a CPU
+    operand (a host pointer on the GPU) is refused on the host instead."""
+    from moe_overlap_b200 import gemm as gg
+
+    a, b, off = _cpu_args()
+    with pytest.raises(ValueError, match="must be CUDA tensors"):
+        gg.grouped_gemm(a, b, off)
+    with pytest.raises(ValueError, match="must be CUDA tensors"):
+        gg.grouped_gemm_wgrad(torch.zeros(64, 8, dtype=torch.bfloat16),
+                              torch.zeros(64, 8, dtype=torch.bfloat16), torch.tensor([0, 64]))
+    cuda0 = torch.device("cuda", 0)
+    with pytest.raises(ValueError, match=r"aux_in must be on cuda:0, not cpu"):
+        gg._require_on_device(cuda0, out=None, aux_in=torch.zeros(2))
+    gg._require_on_device(cuda0, out=None)  # absent operands are fine
+
+
+def test_dispatcher_refuses_operands_off_its_device():
+    """The exchange kernels take raw pointers; the dispatcher refuses a tensor that is
+    not on its GPU before anything is enqueued (checked here without a GPU)."""
+    from moe_overlap_b200.deep_ep_comm import DeepEPDispatcher
+
+    d = DeepEPDispatcher.__new__(DeepEPDispatcher)  # no buffers needed for the check
+    d.device = torch.device("cuda", 0)
+    with pytest.raises(ValueError, match=r"x must be on cuda:0, not cpu"):
+        d._require_on_device(x=torch.zeros(4, 8), topk_idx=None)
+    d._require_on_device(topk_weights=None)
