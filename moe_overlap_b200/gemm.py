@@ -291,6 +291,7 @@ def tile_list(
     kernel walks.  Returns three int32 CUDA tensors.
     """
     device = expert_offsets.device
+    _require_on_device(device)
     offs64 = 1 if expert_offsets.dtype == torch.int64 else 0
     offs = expert_offsets if expert_offsets.dtype in (torch.int32, torch.int64) else expert_offsets.to(torch.int32)
     offs = offs.contiguous()

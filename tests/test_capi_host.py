@@ -261,6 +261,8 @@ def test_extended_gemm_entry_points_refuse_host_tensors():
     with pytest.raises(ValueError, match=r"aux_in must be on cuda:0, not cpu"):
         gg._require_on_device(cuda0, out=None, aux_in=torch.zeros(2))
     gg._require_on_device(cuda0, out=None)  # absent operands are fine
+    with pytest.raises(ValueError, match="must be CUDA tensors"):
+        gg.tile_list(off, 8, 8)
 
 
 def test_dispatcher_refuses_operands_off_its_device():
