@@ -114,6 +114,12 @@ class Endpoint:
             host_info=(ctypes.c_int64 * 2).from_address(int(v.host_info)),
         )
 
+    def _on_device(self, *tensors) -> None:
+        """Kernels take raw pointers: every tensor operand must be on this endpoint's GPU."""
+        for t in tensors:
+            if t is not None and t.device != self.device:
+                raise ValueError(f"exchange operands must be on {self.device}, not {t.device}")
+
     # ------------------------------------------------------------ connection --
     def export_handle(self) -> bytes:
         buf = ctypes.create_string_buffer(64)
@@ -149,6 +155,7 @@ class Endpoint:
         return torch.cuda.current_stream(self.device).cuda_stream
 
     def dispatch_begin(self, x, topk_idx, topk_w, slot, epoch, status):
+        self._on_device(x, topk_idx, topk_w)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch_begin(self.handle, x.data_ptr(), topk_idx.data_ptr(),
@@ -158,6 +165,7 @@ class Endpoint:
 
     def dispatch_scatter(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows, wait_ns,
                          status, expert_alignment: int = 1, scale_rows: bool = False):
+        self._on_device(x, topk_idx, topk_w)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch_scatter(self.handle, x.data_ptr(), topk_idx.data_ptr(),
@@ -179,6 +187,7 @@ class Endpoint:
 
     def dispatch_cached_scatter(self, x, topk_idx, topk_w, src_slot, slot, epoch, num_blocks,
                                 pad_rows, wait_ns, status, scale_rows: bool = False):
+        self._on_device(x, topk_idx, topk_w)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch_cached_scatter(self.handle, x.data_ptr(), topk_idx.data_ptr(),
@@ -190,6 +199,7 @@ class Endpoint:
 
     def dispatch_cached(self, x, topk_idx, topk_w, src_slot, slot, epoch, num_blocks, pad_rows,
                         wait_ns, status, scale_rows: bool = False):
+        self._on_device(x, topk_idx, topk_w)
         """Rows x for the tokens and top-k choices of the dispatch into ``src_slot``,
         in that dispatch's layout, into ``slot`` (see moe_ep_dispatch_cached)."""
         t, k = topk_idx.shape
@@ -207,6 +217,7 @@ class Endpoint:
 
     def combine_end(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns,
                     status):
+        self._on_device(topk_idx, topk_w, out)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_combine_end(self.handle, topk_idx.data_ptr(),
@@ -217,6 +228,7 @@ class Endpoint:
 
     def dispatch(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows, wait_ns, status,
                  expert_alignment: int = 1, scale_rows: bool = False):
+        self._on_device(x, topk_idx, topk_w)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch(self.handle, x.data_ptr(), topk_idx.data_ptr(),
@@ -227,6 +239,7 @@ class Endpoint:
             "moe_ep_dispatch")
 
     def topk_weight_grad(self, grad_out, topk_idx, slot, out, num_blocks):
+        self._on_device(grad_out, topk_idx, out)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_topk_weight_grad(self.handle, grad_out.data_ptr(), topk_idx.data_ptr(),
@@ -235,6 +248,7 @@ class Endpoint:
             "moe_ep_topk_weight_grad")
 
     def combine(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns, status):
+        self._on_device(topk_idx, topk_w, out)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_combine(self.handle, topk_idx.data_ptr(),
@@ -244,6 +258,7 @@ class Endpoint:
             "moe_ep_combine")
 
     def push_gemm(self, a, b, slot, epoch, num_sms, use_atomic, work_counter, status) -> None:
+        self._on_device(a, b, work_counter)
         """Fused down-projection + combine push of ``a`` rows (this rank's receive
         layout of ``slot``) by ``b`` [E_local, K, hidden] (any strides that
         moe_grouped_gemm accepts); see moe_ep_push_gemm."""
@@ -257,6 +272,7 @@ class Endpoint:
 
     def combine_pushed(self, topk_idx, topk_w, slot, epoch, weighted, out, num_blocks, wait_ns,
                        status) -> None:
+        self._on_device(topk_idx, topk_w, out)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_combine_pushed(self.handle, topk_idx.data_ptr(),

@@ -275,3 +275,10 @@ def test_dispatcher_refuses_operands_off_its_device():
     with pytest.raises(ValueError, match=r"x must be on cuda:0, not cpu"):
         d._require_on_device(x=torch.zeros(4, 8), topk_idx=None)
     d._require_on_device(topk_weights=None)
+    from moe_overlap_b200.ep import Endpoint
+
+    e = Endpoint.__new__(Endpoint)
+    e.device = torch.device("cuda", 0)
+    with pytest.raises(ValueError, match=r"exchange operands must be on cuda:0, not cpu"):
+        e.dispatch_begin(torch.zeros(4, 8), torch.zeros(4, 2, dtype=torch.int64),
+                         torch.zeros(4, 2), 0, 1, None)
