@@ -2,7 +2,7 @@
 """Benchmark of the moe_overlap_b200 hot path (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemm_cfg2|gemm_cfg3|gemm_cfg1]
+                    [--workload gemm_cfg2|gemm_cfg3|gemm_cfg1|ep_layer|layer_fwd|layer_train]
 
 Default workload: BASELINE config 2 -- grouped GEMM forward, 16 experts x 512
 rows, H=2048, F=4096, bf16, striped persistent schedule over every SM.  One
@@ -17,14 +17,22 @@ region (expert weights stay resident, as model parameters do), with copy-in,
 GEMM and copy-out of consecutive steps overlapped on three streams; the same
 steps run back to back on one stream are reported beside it.
 
-With N > 1 (torchrun) every rank runs its own copy of the workload: the
-grouped GEMM has no cross-rank exchange, so scaling is weak and there is no
-collective on the data path.
+The default line carries two more measurements of the same run:
+  ``gemm_cfg3``  BASELINE config 3 (16 experts, Zipf(1.2)-skewed 16384 rows, one
+                 expert empty, atomic tile queue), timed like the headline;
+  ``ep_layer``   BASELINE config 5, the expert-parallel MoE layer (router,
+                 dispatch, grouped GEMMs, weighted combine) with the 16 experts
+                 sharded over the N ranks of the run: tokens/s of all ranks,
+                 rows received per rank, the communication-hidden ratio, and the
+                 device time and NVLink rate of every exchange launch.
+With N > 1 (torchrun) every rank runs its own copy of the config 2 and 3 GEMMs
+(the grouped GEMM has no cross-rank exchange, so scaling is weak and there is
+no collective on their data path), and all ranks run config 5 together.
 
 ``--impl reference`` times the reference's CPU implementation of the path on
-this host's cores: the numpy restatement of the per-expert loop in
-``oracle/`` (the reference's Python cannot travel to the GPU box), on a
-bounded sample of the same workload per step.
+this host's cores: the per-expert torch loop of ``reference_grouped_gemm``
+(restated in ``oracle/torch_loop.py``; the reference's Python cannot travel to
+the GPU box), over the same workload and configuration as the headline.
 """
 from __future__ import annotations
 
@@ -112,6 +120,8 @@ def parse_args() -> argparse.Namespace:
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default workload: skip the gemm_cfg3 and ep_layer measurements")
     return ap.parse_args()
 
 
@@ -143,41 +153,48 @@ def profiled_traffic(workload: str) -> float | None:
     return None
 
 
+def gemm_config(name: str, num_sms: int, world: int) -> dict:
+    """The ``config`` object of a grouped-GEMM line; both arms print the same one."""
+    wl = WORKLOADS[name]
+    counts = workload_counts(name)
+    rows = int(sum(counts))
+    in_mib = (rows * wl["k"] + len(counts) * wl["k"] * wl["n"]) * 2 >> 20
+    return {
+        "workload": name,
+        "description": wl["desc"],
+        "rows": rows,
+        "counts": counts,
+        "num_sms": num_sms,
+        "schedule": "atomic" if wl["atomic"] else "striped",
+        "l2": "flushed between timed launches (256 MiB write, outside the events); "
+              f"inputs also exceed L2 (A+B = {in_mib} MiB)",
+        "parallelism": f"replica x{world} (no data-path collective)",
+    }
+
+
+def device_sm_count(local_rank: int = 0) -> int:
+    """SMs of this rank's GPU (148 on a B200 when no GPU is visible)."""
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            return torch.cuda.get_device_properties(local_rank).multi_processor_count
+    except Exception:
+        pass
+    return 148
+
+
+def rows_computed(counts) -> int:
+    """Rows the CTA-pair GEMM multiplies for these expert counts (tensor work incl. padding):
+    every expert's rows are cut into 256-row pair tiles."""
+    return sum(256 * (-(-int(c) // 256)) for c in counts)
+
+
 # ---------------------------------------------------------------- CPU side --
-class CpuGemm:
-    """The oracle's per-expert loop with the expert weights kept resident in fp32.
+def set_cpu_threads(n: int) -> int:
+    import torch
 
-    Weights are model parameters, so they are converted once, outside the
-    timed region; each sample converts its activation rows, multiplies in fp32
-    (numpy BLAS) and rounds the result to the storage dtype, as
-    oracle/grouped_gemm.py does.
-    """
-
-    def __init__(self, a_np, b_np, offsets, dtype):
-        from oracle.numerics import to_f32
-
-        self.a_np, self.dtype = a_np, dtype
-        self.off = [int(v) for v in offsets]
-        self.b32 = [to_f32(b_np[e], dtype) for e in range(b_np.shape[0])]
-        self.experts = [e for e in range(len(self.off) - 1) if self.off[e + 1] > self.off[e]]
-
-    def run(self, experts, rows_cap=None) -> int:
-        from oracle.numerics import from_f32, to_f32
-
-        flops = 0
-        for e in experts:
-            s, t = self.off[e], self.off[e + 1]
-            if rows_cap is not None:
-                t = min(t, s + rows_cap)
-            if t <= s:
-                continue
-            acc = to_f32(self.a_np[s:t], self.dtype) @ self.b32[e]
-            from_f32(acc, self.dtype)
-            flops += 2 * (t - s) * self.a_np.shape[1] * self.b32[e].shape[1]
-        return flops
-
-
-def set_blas_threads(n: int) -> int:
+    torch.set_num_threads(n)
     try:
         from threadpoolctl import threadpool_limits
 
@@ -187,19 +204,67 @@ def set_blas_threads(n: int) -> int:
     return n
 
 
-def cpu_baseline(a, b, offsets, dtype, budget_s: float = 20.0) -> dict:
-    """Oracle (numpy restatement of the per-expert torch loop) on this host."""
-    from tests._inputs import to_storage
+class CpuReference:
+    """The reference's CPU grouped GEMM on this host: the per-expert torch loop of
+    ``reference_grouped_gemm`` (src/triton_grouped_gemm.py:446-457), restated in
+    oracle/torch_loop.py, in the workload's dtype on all host cores."""
 
-    cores = set_blas_threads(cpu_cores())
-    g = CpuGemm(to_storage(a), to_storage(b), offsets.tolist(), dtype)
-    g.run(g.experts[:1], rows_cap=64)  # warm BLAS threads
-    done_flops, done_experts = 0, 0
+    def __init__(self, name: str):
+        from oracle.torch_loop import grouped_gemm_loop, loop_flops
+        from tests._inputs import gemm_inputs
+
+        wl = WORKLOADS[name]
+        self.name, self.dtype = name, wl["dtype"]
+        self.counts = workload_counts(name)
+        self.a, self.b, off = gemm_inputs(self.counts, wl["k"], wl["n"], wl["dtype"], seed=0)
+        self.off = off.tolist()
+        self.out = None
+        self.experts = [e for e, c in enumerate(self.counts) if c > 0]
+        self._loop, self._flops = grouped_gemm_loop, loop_flops
+
+    def step(self, experts=None) -> int:
+        """One pass of the loop (all experts, or the given sample); returns its flops."""
+        self.out = self._loop(self.a, self.b, self.off, experts, self.out)
+        return self._flops(self.a.shape, self.b.shape, self.off, experts)
+
+    def plan(self, n_steps: int, budget_s: float) -> tuple[list | None, str]:
+        """The experts one step runs so that ``n_steps`` steps fit in ``budget_s``:
+        the whole workload when it fits, else the largest prefix of the experts."""
+        self.step(self.experts[:1])  # warm the threads
+        t0 = time.perf_counter()
+        full_flops = self.step()
+        per_flop = (time.perf_counter() - t0) / max(1, full_flops)
+        if per_flop * full_flops * n_steps <= budget_s:
+            return None, f"the whole workload per step ({len(self.experts)} experts, " \
+                         f"{full_flops / 1e9:.1f} GFLOP)"
+        sample, flops = [], 0
+        for e in self.experts:
+            f = self._flops(self.a.shape, self.b.shape, self.off, [e])
+            if sample and per_flop * (flops + f) * n_steps > budget_s:
+                break
+            sample.append(e)
+            flops += f
+        return sample, f"experts {sample} of {len(self.experts)} per step ({flops / 1e9:.1f} " \
+                       f"GFLOP), to keep {n_steps} steps within {budget_s:.0f} s"
+
+
+def cpu_sample_text(name: str, what: str) -> str:
+    return (f"{what} of {name}: per-expert torch matmul loop in {WORKLOADS[name]['dtype']} "
+            "(reference_grouped_gemm, src/triton_grouped_gemm.py:446-457, restated in "
+            "oracle/torch_loop.py), inputs resident in host memory")
+
+
+def cpu_baseline(name: str, budget_s: float = 20.0) -> dict:
+    """The reference's CPU grouped GEMM timed on this host (bounded sample)."""
+    cores = set_cpu_threads(cpu_cores())
+    ref = CpuReference(name)
+    ref.step(ref.experts[:1])
+    done_flops, passes = 0, 0
     t0 = time.perf_counter()
-    for e in g.experts:
-        done_flops += g.run([e])
-        done_experts += 1
-        if time.perf_counter() - t0 > budget_s:
+    while True:
+        done_flops += ref.step()
+        passes += 1
+        if time.perf_counter() - t0 > min(budget_s, 2.0) or passes >= 5:
             break
     dt = time.perf_counter() - t0
     return {
@@ -207,42 +272,27 @@ def cpu_baseline(a, b, offsets, dtype, budget_s: float = 20.0) -> dict:
         "unit": UNIT,
         "cores": cores,
         "kind": "port",
-        "sample": f"{done_experts} of {len(g.experts)} non-empty experts of the same workload "
-                  f"({done_flops / 1e9:.1f} GFLOP in {dt:.2f} s): numpy fp32 matmul with resident "
-                  f"fp32 weights + activation conversion + output rounding (oracle/)",
+        "sample": cpu_sample_text(name, f"{passes} whole passes ({done_flops / 1e9:.1f} GFLOP in "
+                                        f"{dt:.2f} s)"),
     }
 
 
 def run_reference(args, rank: int) -> None:
-    """The reference arm: CPU implementation of the path, rank 0 only."""
+    """The reference arm: the reference's CPU implementation of the path, rank 0 only,
+    on the headline's workload, metric and configuration."""
     if rank != 0:
         return
-    import torch
-
-    from tests._inputs import gemm_inputs, to_storage
-
-    wl = WORKLOADS[args.workload]
-    counts = workload_counts(args.workload)
-    a, b, offsets = gemm_inputs(counts, wl["k"], wl["n"], wl["dtype"], seed=0)
-    g = CpuGemm(to_storage(a), to_storage(b), offsets.tolist(), wl["dtype"])
-    cores = set_blas_threads(cpu_cores())
-    # Size each step's sample (rows of one expert) so the whole run stays near a minute.
-    g.run(g.experts[:1], rows_cap=64)
-    probe_t = time.perf_counter()
-    g.run(g.experts[:1], rows_cap=128)
-    per_row_s = max((time.perf_counter() - probe_t) / 128, 1e-7)
-    budget_per_step = 60.0 / max(1, args.steps + args.warmup)
-    rows_cap = int(max(16, min(max(counts), budget_per_step / per_row_s)))
-    for i in range(args.warmup):
-        g.run([g.experts[i % len(g.experts)]], rows_cap)
+    cores = set_cpu_threads(cpu_cores())
+    ref = CpuReference(args.workload)
+    sample, sample_text = ref.plan(args.steps + args.warmup, budget_s=150.0)
+    for _ in range(args.warmup):
+        ref.step(sample)
     flops, t0 = 0, time.perf_counter()
-    for i in range(args.steps):
-        flops += g.run([g.experts[i % len(g.experts)]], rows_cap)
+    for _ in range(args.steps):
+        flops += ref.step(sample)
     dt = time.perf_counter() - t0
     value = flops / dt / 1e12
-    sample = (f"per step: up to {rows_cap} rows of one expert (cycling over {len(g.experts)} experts) "
-              f"of {args.workload}; numpy fp32 matmul with resident fp32 weights, activation "
-              f"conversion and output rounding (oracle/)")
+    sample = cpu_sample_text(args.workload, sample_text)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -255,16 +305,15 @@ def run_reference(args, rank: int) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": wl["dtype"],
-        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
-        "config": {"workload": args.workload, "description": wl["desc"]},
+        "dtype": WORKLOADS[args.workload]["dtype"],
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; generated on CPU)",
+        "config": gemm_config(args.workload, device_sm_count(), args.gpus),
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-    del torch
 
 
 # ---------------------------------------------------------------- clocks --
@@ -397,23 +446,35 @@ def zipf_gate_bias(router_w, num_experts: int, top_k: int, seed: int = 12345):
     return bias.astype(np.float32), it, err
 
 
-def run_layer(args, rank: int, world: int, local_rank: int) -> None:
-    """MoE-layer workloads: tokens/s of the forward, overlap accounting, NVLink GB/s."""
+def init_group(world: int, device):
+    """NCCL process group over every rank of the run (None for one rank)."""
+    if world <= 1:
+        return None
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
+    return dist.group.WORLD
+
+
+def measure_layer(args, name: str, rank: int, world: int, device, group, steps: int,
+                  warmup: int, timeline: bool = False, graph_ok: bool = True) -> dict:
+    """MoE-layer forward (or config 4's forward) over every rank.
+
+    Returns the measurement as a dict (the same on every rank; every rank takes
+    the same collective steps): tokens/s of all ranks over ``steps`` timed
+    forwards (CUDA events, max over ranks), the communication-hidden ratio from
+    serialized phase times, and the device time of every exchange launch of the
+    first chunk with the NVLink rate it implies.
+    """
     import torch
     import torch.distributed as dist
 
     import moe_overlap_b200 as mo
     from moe_overlap_b200.layer import MoELayer, random_weights
 
-    cfg = LAYER_WORKLOADS[args.workload]
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    group = None
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
-        group = dist.group.WORLD
+    cfg = LAYER_WORKLOADS[name]
     T, H, Fd, E, K = cfg["tokens"], cfg["hidden"], cfg["ffn"], cfg["experts"], cfg["top_k"]
     layer = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
                      router_bias=cfg["zipf_bias"], num_comm_sms=args.comm_sms,
@@ -433,38 +494,39 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(device)
     routing = layer.route(x)
     idx = routing[1]
-    flops_local = torch.zeros(1, dtype=torch.float64, device=device)
-    owner = idx // layer.experts_per_rank
-    rows_to = torch.bincount(owner[idx >= 0].reshape(-1), minlength=world).double()
-    if world > 1:
-        recv_rows = rows_to.clone()
-        dist.all_reduce(recv_rows, group=group)  # rows each rank receives, summed over senders
-    else:
-        recv_rows = rows_to
-    # rows[src, dst] over all ranks: the busiest rank's inbound or outbound remote
-    # rows bound the exchange (under the Zipf gate, rank 0 mostly receives).
-    if world > 1:
-        gathered_rows = [torch.zeros_like(rows_to) for _ in range(world)]
-        dist.all_gather(gathered_rows, rows_to, group=group)
-        row_matrix = torch.stack(gathered_rows)
-    else:
-        row_matrix = rows_to.view(1, 1)
-    remote_out, remote_in = exchange_row_totals(row_matrix.cpu())
+
+    def row_matrix(sel):
+        """rows[src, dst] of the assignments in ``sel`` over all ranks."""
+        owner = sel // layer.experts_per_rank
+        rows_to = torch.bincount(owner[sel >= 0].reshape(-1), minlength=world).double()
+        if world > 1:
+            gathered = [torch.zeros_like(rows_to) for _ in range(world)]
+            dist.all_gather(gathered, rows_to, group=group)
+            return torch.stack(gathered).cpu()
+        return rows_to.view(1, 1).cpu()
+
+    mat = row_matrix(idx)
+    recv_rows = mat.sum(dim=0)  # rows each rank receives, summed over senders
+    remote_out, remote_in = exchange_row_totals(mat)
     busiest_rows = float(max(max(remote_out), max(remote_in)))
+    first = layer.chunk_plan(T)[0]
+    mat0 = row_matrix(idx[first[0]:first[1]])
+    out0, in0 = exchange_row_totals(mat0)
     expert_counts = torch.bincount(idx[idx >= 0].reshape(-1), minlength=E).double()
     if world > 1:
         dist.all_reduce(expert_counts, group=group)
     realised_share = (expert_counts / expert_counts.sum()).tolist()
-    flops_local[0] = 4.0 * float(recv_rows[rank]) * H * Fd  # two GEMMs on this rank's rows
-    for _ in range(max(3, args.warmup)):
+    flops_total = 4.0 * float(recv_rows.sum()) * H * Fd  # two GEMMs on every rank's rows
+
+    for _ in range(max(3, warmup)):
         layer(x, routing=routing)
     torch.cuda.synchronize(device)
     mo.check_status(device, sync=True)
     # On one GPU the timed forwards replay one CUDA graph (device-drawn exchange
-    # epochs) unless --no-graph; across GPUs they run eagerly, so that a capture
-    # problem on one rank cannot leave the others waiting.
+    # epochs); across GPUs they run eagerly, so that a capture problem on one rank
+    # cannot leave the others waiting.
     graph, graph_note = None, None
-    if world == 1 and not args.no_graph:
+    if world == 1 and graph_ok:
         try:
             from moe_overlap_b200.layer import ForwardGraph
 
@@ -481,11 +543,11 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     sampler = ClockSampler(device)
     sampler.start()
     if world > 1:
-        dist.barrier()
+        dist.barrier(group=group)
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         if graph is not None:
             graph.replay()
         else:
@@ -493,94 +555,134 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     end.record()
     torch.cuda.synchronize(device)
     if world > 1:
-        dist.barrier()
+        dist.barrier(group=group)
     clocks = sampler.stop()
     mo.check_status(device, sync=True)
-    step_ms = start.elapsed_time(end) / args.steps
-    t = torch.tensor([step_ms], dtype=torch.float64, device=device)
-    total_flops = flops_local.clone()
+    t = torch.tensor([start.elapsed_time(end) / steps], dtype=torch.float64, device=device)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(total_flops)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     step_ms = float(t.item())
+    del graph
 
-    timeline = None
-    if args.timeline:
+    marks_by_rank = None
+    if timeline:
         # One more forward with events at every phase boundary on the stream that
-        # runs it (ms from the forward's start, per rank).
+        # runs it (ms from the forward's start, per rank), behind ~1.5 ms of
+        # device-side delay so the marks show the device's schedule.
         marks = []
         if world > 1:
-            dist.barrier()
+            dist.barrier(group=group)
         torch.cuda.synchronize(device)
-        # ~1.5 ms of device-side delay first: the host enqueues the whole forward
-        # meanwhile, so the marks show the device's schedule, not the host's launches.
         torch.cuda._sleep(3_000_000)
         layer(x, routing=routing, timeline=marks)
         torch.cuda.synchronize(device)
-        mine = {name: round(marks[0][1].elapsed_time(ev), 4) for name, ev in marks[1:]}
-        if world > 1:
-            gathered = [None] * world
-            dist.all_gather_object(gathered, mine)
-        else:
-            gathered = [mine]
-        timeline = {f"rank{r}": t for r, t in enumerate(gathered)}
+        mine = {n: round(marks[0][1].elapsed_time(ev), 4) for n, ev in marks[1:]}
+        marks_by_rank = gather_objects(mine, world, group)
 
     _, phases = layer.forward_serialized(x, routing)
     comm_ms = phases["dispatch_ms"] + phases["combine_ms"]
     comp_ms = phases["experts_ms"]
     hidden = max(0.0, min(1.0, (comm_ms + comp_ms - step_ms) / comm_ms)) if comm_ms > 0 else None
+
+    # Every exchange launch of the first chunk, run alone; per-rank device times.
+    kt = gather_objects({k: round(v, 4) for k, v in layer.exchange_phase_times(x, routing).items()},
+                        world, group)
+    mo.check_status(device, sync=True)
     row_bytes = H * 2
-    dispatch_bytes = busiest_rows * (row_bytes + K * 12 + 8)
-    combine_bytes = busiest_rows * row_bytes
-    peak, peak_src = load_peaks()
-    if rank == 0:
-        tokens_per_s = world * T / (step_ms / 1e3)
-        tflops = float(total_flops.item()) / (step_ms / 1e3) / 1e12
-        line = {
-            "metric": "MoE-layer tokens/s",
-            "value": round(tokens_per_s, 1),
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(step_ms, 4),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
-            "config": {"workload": args.workload, "description": cfg["desc"],
-                       "tokens_per_rank": T, "micro_batch": args.micro_batch,
-                       "chunks": [e - s for s, e in layer.chunk_plan(T)],
-                       "cuda_graph": graph is not None, "cuda_graph_note": graph_note,
-                       "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
-                       else "pull",
-                       "comm_sms": args.comm_sms, "gate_bias": bias_info,
-                       "realised_expert_share": [round(v, 4) for v in realised_share],
-                       "rows_received_per_rank": [int(v) for v in recv_rows.tolist()],
-                       "parallelism": f"ep{world}"},
-            "expert_gemm_tflops": round(tflops, 2),
-            "expert_gemm_frac_of_peak": round(tflops / (world * peak), 4),
-            "communication_hidden_ratio": None if hidden is None else round(hidden, 4),
-            "serial_phase_ms": {k: round(v, 4) for k, v in phases.items()},
-            "nvlink": {
-                "dispatch_GBps_busiest_rank": round(dispatch_bytes / (phases["dispatch_ms"] / 1e3) / 1e9, 1)
-                if world > 1 and phases["dispatch_ms"] > 0 else None,
-                "combine_GBps_busiest_rank": round(combine_bytes / (phases["combine_ms"] / 1e3) / 1e9, 1)
-                if world > 1 and phases["combine_ms"] > 0 else None,
-                "remote_rows_out_per_rank": [int(v) for v in remote_out],
-                "remote_rows_in_per_rank": [int(v) for v in remote_in],
-                "nvlink_floor_ms_per_exchange": round(dispatch_bytes / PEER_COPY_GBPS / 1e6, 4)
-                if world > 1 else None,
-                "peer_copy_reference_GBps": PEER_COPY_GBPS,
-            },
-            "clocks": clocks,
-            "gpu_launches_per_step": None,
+    meta_bytes = K * 12 + 12  # top-k ids and weights, {source rank, token}, combine row index
+    exchange = {"chunk": f"first chunk ({first[1] - first[0]} tokens per rank), "
+                         f"{layer.solo_comm_blocks} blocks of 128 threads",
+                "kernel_ms_per_rank": kt,
+                "remote_rows_out_per_rank": [int(v) for v in out0],
+                "remote_rows_in_per_rank": [int(v) for v in in0]}
+    if world > 1:
+        def gbps(nbytes, ms):
+            return round(nbytes / (ms / 1e3) / 1e9, 1) if ms > 0 else None
+        disp_ms = [sum(kt[r].get(f"dispatch_{p}", 0.0) for p in ("layout_count", "scatter", "wait"))
+                   for r in range(world)]
+        rates = {
+            # rows this rank pushed to peers / its scatter kernel (which also waits for the peers' counts)
+            "scatter_out_GBps": [gbps(out0[r] * (row_bytes + meta_bytes), kt[r].get("dispatch_scatter", 0.0))
+                                 for r in range(world)],
+            # rows peers pushed here / this rank's whole dispatch (start to every row landed)
+            "dispatch_in_GBps": [gbps(in0[r] * (row_bytes + meta_bytes), disp_ms[r]) for r in range(world)],
+            # rows this rank's tokens pulled back from peers / its pull kernel
+            "pull_in_GBps": [gbps(out0[r] * row_bytes, kt[r].get("combine_pull", 0.0))
+                             for r in range(world)],
         }
-        if timeline is not None:
-            line["timeline_ms"] = timeline
-        print(json.dumps(line), flush=True)
+        busiest = max(range(world), key=lambda r: max(out0[r], in0[r]))
+        exchange.update(rates)
+        exchange["busiest_rank"] = busiest
+        cands = [rates[k][busiest] for k in rates if rates[k][busiest] is not None]
+        exchange["busiest_rank_GBps"] = max(cands) if cands else None
+        exchange["nvlink_peak_GBps"] = {"nominal_per_direction": 900.0,
+                                        "measured_peer_copy": PEER_COPY_GBPS}
+    peak, peak_src = load_peaks()
+    tflops = flops_total / (step_ms / 1e3) / 1e12
+    result = {
+        "metric": "MoE-layer tokens/s",
+        "value": round(world * T / (step_ms / 1e3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": max(3, warmup),
+        "ms_per_step": round(step_ms, 4),
+        "config": {"workload": name, "description": cfg["desc"],
+                   "tokens_per_rank": T, "micro_batch": args.micro_batch,
+                   "chunks": [e - s for s, e in layer.chunk_plan(T)],
+                   "cuda_graph": world == 1 and graph_ok and graph_note is None,
+                   "cuda_graph_note": graph_note,
+                   "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
+                   else "pull",
+                   "comm_sms": args.comm_sms, "gate_bias": bias_info,
+                   "realised_expert_share": [round(v, 4) for v in realised_share],
+                   "rows_received_per_rank": [int(v) for v in recv_rows.tolist()],
+                   "parallelism": f"ep{world}"},
+        "expert_gemm_tflops": round(tflops, 2),
+        "expert_gemm_frac_of_peak": round(tflops / (world * peak), 4),
+        "communication_hidden_ratio": None if hidden is None else round(hidden, 4),
+        "serial_phase_ms": {k: round(v, 4) for k, v in phases.items()},
+        "exchange": exchange,
+        "nvlink": {
+            "remote_rows_out_per_rank": [int(v) for v in remote_out],
+            "remote_rows_in_per_rank": [int(v) for v in remote_in],
+            "nvlink_floor_ms_per_exchange": round(busiest_rows * (row_bytes + meta_bytes)
+                                                  / PEER_COPY_GBPS / 1e6, 4) if world > 1 else None,
+        },
+        "clocks": clocks,
+    }
+    if marks_by_rank is not None:
+        result["timeline_ms"] = {f"rank{r}": m for r, m in enumerate(marks_by_rank)}
     layer.close()
+    return result
+
+
+def gather_objects(obj, world: int, group) -> list:
+    """``obj`` of every rank, indexed by rank (a one-item list for one rank)."""
+    if world <= 1:
+        return [obj]
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, obj, group=group)
+    return out
+
+
+def run_layer(args, rank: int, world: int, local_rank: int) -> None:
+    """MoE-layer forward workloads as their own line: tokens/s, overlap, exchange rates."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    group = init_group(world, device)
+    res = measure_layer(args, args.workload, rank, world, device, group, args.steps, args.warmup,
+                        timeline=args.timeline, graph_ok=not args.no_graph)
+    if rank == 0:
+        line = {**res, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
+                "warmup": args.warmup, "gpu_launches_per_step": None}
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -604,10 +706,7 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
     cfg = LAYER_WORKLOADS[args.workload]
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
+    init_group(world, device)
     T, H, Fd, E, K = cfg["tokens"], cfg["hidden"], cfg["ffn"], cfg["experts"], cfg["top_k"]
     layer = MoELayer(H, Fd, E, K, renormalize=cfg["renorm"], num_comm_sms=args.comm_sms,
                      micro_batch_size=T, training=True).init_random(std=0.02, seed=0)
@@ -776,6 +875,197 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+class GemmRun:
+    """One grouped-GEMM workload resident on this rank's GPU, timed launch by launch.
+
+    Each timed launch is preceded by a 256 MiB write (outside its events) that
+    evicts L2; the launches are timed with CUDA events on the launching stream.
+    """
+
+    def __init__(self, name: str, device, sm_count: int):
+        import torch
+
+        import moe_overlap_b200 as mo
+        from tests._inputs import gemm_inputs
+
+        self.mo, self.name, self.device, self.sm_count = mo, name, device, sm_count
+        self.wl = WORKLOADS[name]
+        self.counts = workload_counts(name)
+        self.a_cpu, self.b_cpu, self.off_cpu = gemm_inputs(self.counts, self.wl["k"], self.wl["n"],
+                                                           self.wl["dtype"], seed=0)
+        self.rows = int(sum(self.counts))
+        self.flops = 2.0 * self.rows * self.wl["k"] * self.wl["n"]
+        self.a = self.a_cpu.to(device)
+        self.b = self.b_cpu.to(device)
+        self.off = self.off_cpu.to(device)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        self.stream = torch.cuda.current_stream(device)
+
+    def step(self, a=None, off=None):
+        return self.mo.persistent_grouped_gemm(self.a if a is None else a, self.b,
+                                               self.off if off is None else off,
+                                               num_sms=self.sm_count,
+                                               use_atomic_queue=self.wl["atomic"],
+                                               work_counter=self.counter)
+
+    def timed(self, steps: int, warmup: int, world: int) -> dict:
+        """Per-launch times (ms), their max-over-ranks total, and the clocks meanwhile."""
+        import torch
+        import torch.distributed as dist
+
+        for _ in range(max(3, warmup)):
+            self.step()
+            self.flush.fill_(1)
+        torch.cuda.synchronize(self.device)
+        self.mo.check_status(self.device, sync=True)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        sampler = ClockSampler(self.device)
+        sampler.start()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(self.device)
+        for i in range(steps):
+            self.flush.fill_(i & 0xFF)  # evict L2 between launches (outside the events)
+            starts[i].record(self.stream)
+            self.step()
+            ends[i].record(self.stream)
+        torch.cuda.synchronize(self.device)
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop()
+        self.mo.check_status(self.device, sync=True)
+        launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        total_ms = sum(launch_ms)
+        if world > 1:
+            t = torch.tensor([total_ms], dtype=torch.float64, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total_ms = float(t.item())
+        return {"launch_ms": launch_ms, "total_ms": total_ms, "clocks": clocks}
+
+    def roofline(self, launch_ms: list) -> dict:
+        peak, peak_src = load_peaks()
+        achieved = self.flops / (statistics.mean(launch_ms) / 1e3) / 1e12
+        return {
+            "bound": "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": UNIT,
+            "frac": round(achieved / peak, 4),
+            "peak_source": peak_src,
+            "traffic": profiled_traffic(self.name),
+            "kernel": ("moe::gg::grouped_gemm_kernel (1 SM)" if self.sm_count < 2 or
+                       os.environ.get("MOE_B200_GEMM_KERNEL") == "1"
+                       else "moe::gg::pair::grouped_gemm_pair_kernel (CTA pairs, TMA-store epilogue)"),
+            "algorithmic_work": f"2*M*K*N = {self.flops / 1e9:.2f} GFLOP per launch "
+                                f"(M={self.rows} real rows)",
+            "rows_computed": rows_computed(self.counts),
+        }
+
+    def release(self) -> None:
+        for name in ("a", "b", "off", "flush", "counter"):
+            setattr(self, name, None)
+
+
+def measure_e2e(run: GemmRun, steps: int, warmup: int, world: int) -> dict:
+    """The headline metric end to end through ``persistent_grouped_gemm``.
+
+    Every step copies A and the offsets in from pinned host memory, runs the GEMM
+    and copies C back out.  The serial leg does the three on one stream; the
+    pipelined leg puts copy-in, GEMM and copy-out on three streams with two input
+    buffers, so step i's copy-out (PCIe device-to-host) overlaps step i+1's
+    copy-in (host-to-device) and GEMM, as a caller streaming batches through the
+    GEMM would run it.  The headline is the pipelined leg.
+    """
+    import torch
+    import torch.distributed as dist
+
+    mo, device, stream = run.mo, run.device, run.stream
+    a_host = run.a_cpu.pin_memory()
+    off_host = run.off_cpu.pin_memory()
+    c_host = torch.empty((run.rows, run.wl["n"]), dtype=run.a_cpu.dtype).pin_memory()
+    a_dev = torch.empty_like(run.a)
+    off_dev = torch.empty_like(run.off)
+
+    def e2e_step():
+        a_dev.copy_(a_host, non_blocking=True)
+        off_dev.copy_(off_host, non_blocking=True)
+        c = run.step(a_dev, off_dev)
+        c_host.copy_(c, non_blocking=True)
+
+    s_in = torch.cuda.Stream(device)
+    s_out = torch.cuda.Stream(device)
+    a_bufs = [torch.empty_like(run.a) for _ in range(2)]
+    off_bufs = [torch.empty_like(run.off) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_gemm = [torch.cuda.Event() for _ in range(2)]
+    issued = [0]
+
+    def e2e_pipelined_step():
+        i = issued[0]
+        issued[0] += 1
+        k = i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_gemm[k])  # step i-2's GEMM has read a_bufs[k]
+            a_bufs[k].copy_(a_host, non_blocking=True)
+            off_bufs[k].copy_(off_host, non_blocking=True)
+            ev_in[k].record(s_in)
+        stream.wait_event(ev_in[k])
+        c = run.step(a_bufs[k], off_bufs[k])
+        ev_gemm[k].record(stream)
+        s_out.wait_event(ev_gemm[k])
+        with torch.cuda.stream(s_out):
+            c_host.copy_(c, non_blocking=True)
+        c.record_stream(s_out)  # C's memory is reused only after its copy-out
+
+    def timed_leg(fn) -> float:
+        for _ in range(max(3, warmup)):
+            fn()
+        torch.cuda.synchronize(device)
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        s_in.wait_stream(stream)
+        for _ in range(steps):
+            fn()
+        stream.wait_stream(s_in)
+        stream.wait_stream(s_out)
+        e_end.record(stream)
+        torch.cuda.synchronize(device)
+        return e_start.elapsed_time(e_end)
+
+    if world > 1:
+        dist.barrier()
+    serial_ms = timed_leg(e2e_step)
+    want_c = c_host.clone()
+    c_host.zero_()
+    pipe_ms = -1.0
+    if world > 1:
+        dist.barrier()
+    try:
+        pipe_ms = timed_leg(e2e_pipelined_step)
+        if not torch.equal(c_host, want_c):
+            raise RuntimeError("pipelined result differs from the serial one")
+    except RuntimeError as exc:  # keep the serial figure, say why
+        print(f"bench: pipelined end-to-end leg not used: {exc}", file=sys.stderr, flush=True)
+        pipe_ms = -1.0
+    serial_ms, pipe_ms = reduce_e2e_legs(serial_ms, pipe_ms, world, device)
+    mo.check_status(device, sync=True)
+    e2e_ms = pipe_ms if pipe_ms > 0 else serial_ms
+    return {
+        "value": round(world * run.flops * steps / (e2e_ms / 1e3) / 1e12, 3),
+        "unit": UNIT,
+        "h2d_bytes_per_step": a_host.numel() * a_host.element_size()
+        + off_host.numel() * off_host.element_size(),
+        "d2h_bytes_per_step": c_host.numel() * c_host.element_size(),
+        "ms_per_step": round(e2e_ms / steps, 4),
+        "pipelined": pipe_ms > 0,
+        "serial_ms_per_step": round(serial_ms / steps, 4),
+    }
+
+
 def main() -> None:
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -794,166 +1084,49 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    import moe_overlap_b200 as mo
-    from tests._inputs import gemm_inputs
-
     if not torch.cuda.is_available():
         raise RuntimeError("bench.py needs a CUDA device")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
-
-    wl = WORKLOADS[args.workload]
-    counts = workload_counts(args.workload)
-    a_cpu, b_cpu, off_cpu = gemm_inputs(counts, wl["k"], wl["n"], wl["dtype"], seed=0)
-    m_rows = int(sum(counts))
-    flops = 2.0 * m_rows * wl["k"] * wl["n"]
+    group = init_group(world, device)
     sm_count = torch.cuda.get_device_properties(device).multi_processor_count
-    a = a_cpu.to(device)
-    b = b_cpu.to(device)
-    off = off_cpu.to(device)
-    counter = torch.zeros(1, dtype=torch.int32, device=device)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    stream = torch.cuda.current_stream(device)
 
-    def step():
-        return mo.persistent_grouped_gemm(a, b, off, num_sms=sm_count,
-                                          use_atomic_queue=wl["atomic"], work_counter=counter)
+    run = GemmRun(args.workload, device, sm_count)
+    res = run.timed(args.steps, args.warmup, world)
+    value = world * run.flops * args.steps / (res["total_ms"] / 1e3) / 1e12
+    e2e = None if args.no_e2e else measure_e2e(run, args.steps, args.warmup, world)
+    roofline = run.roofline(res["launch_ms"])
+    run.release()
+    torch.cuda.empty_cache()
 
-    for _ in range(max(3, args.warmup)):
-        step()
-        flush.fill_(1)
-    torch.cuda.synchronize(device)
-    mo.check_status(device, sync=True)
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    sampler = ClockSampler(device)
-    sampler.start()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    for i in range(args.steps):
-        flush.fill_(i & 0xFF)  # evict L2 between launches (outside the events)
-        starts[i].record(stream)
-        step()
-        ends[i].record(stream)
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop()
-    mo.check_status(device, sync=True)
-    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(launch_ms)
-    if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    value = world * flops * args.steps / (total_ms / 1e3) / 1e12
-    avg_launch_s = statistics.mean(launch_ms) / 1e3
-    achieved = flops / avg_launch_s / 1e12
-    peak, peak_src = load_peaks()
-
-    # ---- end to end through the public API, host buffers in and out ----
-    # Every step copies A and the offsets in from pinned host memory, runs
-    # persistent_grouped_gemm and copies C back out.  The serial leg does the three
-    # on one stream; the pipelined leg puts copy-in, GEMM and copy-out on three
-    # streams with two input buffers, so step i's copy-out (PCIe device-to-host)
-    # overlaps step i+1's copy-in (host-to-device) and GEMM, as a caller streaming
-    # batches through the GEMM would run it.  The headline is the pipelined leg.
-    e2e = None
-    if not args.no_e2e:
-        a_host = a_cpu.pin_memory()
-        off_host = off_cpu.pin_memory()
-        c_host = torch.empty((m_rows, wl["n"]), dtype=a_cpu.dtype).pin_memory()
-        a_dev = torch.empty_like(a)
-        off_dev = torch.empty_like(off)
-
-        def e2e_step():
-            a_dev.copy_(a_host, non_blocking=True)
-            off_dev.copy_(off_host, non_blocking=True)
-            c = mo.persistent_grouped_gemm(a_dev, b, off_dev, num_sms=sm_count,
-                                           use_atomic_queue=wl["atomic"], work_counter=counter)
-            c_host.copy_(c, non_blocking=True)
-
-        s_in = torch.cuda.Stream(device)
-        s_out = torch.cuda.Stream(device)
-        a_bufs = [torch.empty_like(a) for _ in range(2)]
-        off_bufs = [torch.empty_like(off) for _ in range(2)]
-        ev_in = [torch.cuda.Event() for _ in range(2)]
-        ev_gemm = [torch.cuda.Event() for _ in range(2)]
-        issued = [0]
-
-        def e2e_pipelined_step():
-            i = issued[0]
-            issued[0] += 1
-            k = i % 2
-            with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(ev_gemm[k])  # step i-2's GEMM has read a_bufs[k]
-                a_bufs[k].copy_(a_host, non_blocking=True)
-                off_bufs[k].copy_(off_host, non_blocking=True)
-                ev_in[k].record(s_in)
-            stream.wait_event(ev_in[k])
-            c = mo.persistent_grouped_gemm(a_bufs[k], b, off_bufs[k], num_sms=sm_count,
-                                           use_atomic_queue=wl["atomic"], work_counter=counter)
-            ev_gemm[k].record(stream)
-            s_out.wait_event(ev_gemm[k])
-            with torch.cuda.stream(s_out):
-                c_host.copy_(c, non_blocking=True)
-            c.record_stream(s_out)  # C's memory is reused only after its copy-out
-
-        def timed_leg(fn) -> float:
-            for _ in range(max(3, args.warmup)):
-                fn()
-            torch.cuda.synchronize(device)
-            e_start = torch.cuda.Event(enable_timing=True)
-            e_end = torch.cuda.Event(enable_timing=True)
-            e_start.record(stream)
-            s_in.wait_stream(stream)
-            for _ in range(args.steps):
-                fn()
-            stream.wait_stream(s_in)
-            stream.wait_stream(s_out)
-            e_end.record(stream)
-            torch.cuda.synchronize(device)
-            return e_start.elapsed_time(e_end)
-
-        if world > 1:
-            dist.barrier()
-        serial_ms = timed_leg(e2e_step)
-        want_c = c_host.clone()
-        c_host.zero_()
-        pipe_ms = -1.0
-        if world > 1:
-            dist.barrier()
-        try:
-            pipe_ms = timed_leg(e2e_pipelined_step)
-            if not torch.equal(c_host, want_c):
-                raise RuntimeError("pipelined result differs from the serial one")
-        except RuntimeError as exc:  # keep the serial figure, say why
-            print(f"bench: pipelined end-to-end leg not used: {exc}", file=sys.stderr, flush=True)
-            pipe_ms = -1.0
-        serial_ms, pipe_ms = reduce_e2e_legs(serial_ms, pipe_ms, world, device)
-        mo.check_status(device, sync=True)
-        e2e_ms = pipe_ms if pipe_ms > 0 else serial_ms
-        e2e = {
-            "value": round(world * flops * args.steps / (e2e_ms / 1e3) / 1e12, 3),
+    extras = {}
+    if args.workload == "gemm_cfg2" and not args.no_extras:
+        # BASELINE config 3 (the skewed config the north-star target names), timed alike.
+        r3 = GemmRun("gemm_cfg3", device, sm_count)
+        t3 = r3.timed(args.steps, args.warmup, world)
+        extras["gemm_cfg3"] = {
+            "value": round(world * r3.flops * args.steps / (t3["total_ms"] / 1e3) / 1e12, 3),
             "unit": UNIT,
-            "h2d_bytes_per_step": a_host.numel() * a_host.element_size()
-            + off_host.numel() * off_host.element_size(),
-            "d2h_bytes_per_step": c_host.numel() * c_host.element_size(),
-            "ms_per_step": round(e2e_ms / args.steps, 4),
-            "pipelined": pipe_ms > 0,
-            "serial_ms_per_step": round(serial_ms / args.steps, 4),
+            "ms_per_step": round(t3["total_ms"] / args.steps, 5),
+            "steps": args.steps,
+            "config": gemm_config("gemm_cfg3", sm_count, world),
+            "roofline": r3.roofline(t3["launch_ms"]),
+            "clocks": t3["clocks"],
         }
+        r3.release()
+        del r3
+        torch.cuda.empty_cache()
+        # the expert-parallel layer over every rank of this run.
+        ep = measure_layer(args, "ep_layer", rank, world, device, group,
+                           steps=min(args.steps, 20), warmup=args.warmup)
+        for key in ("metric",):
+            ep.pop(key, None)
+        extras["ep_layer"] = ep
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(a_cpu, b_cpu, off_cpu, wl["dtype"])
+        cpu = cpu_baseline(args.workload)
 
     if rank == 0:
         line = {
@@ -963,41 +1136,19 @@ def main() -> None:
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": round(total_ms / args.steps, 5),
+            "ms_per_step": round(res["total_ms"] / args.steps, 5),
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": wl["dtype"],
+            "dtype": run.wl["dtype"],
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; generated on CPU)",
-            "config": {
-                "workload": args.workload,
-                "description": wl["desc"],
-                "rows": m_rows,
-                "counts": counts,
-                "num_sms": sm_count,
-                "schedule": "atomic" if wl["atomic"] else "striped",
-                "l2": "flushed between timed launches (256 MiB write, outside the events); "
-                      "inputs also exceed L2 (A+B = "
-                      f"{(a.numel() * a.element_size() + b.numel() * b.element_size()) >> 20} MiB)",
-                "parallelism": f"replica x{world} (no data-path collective)",
-            },
-            "roofline": {
-                "bound": "tensor",
-                "achieved": round(achieved, 2),
-                "peak": peak,
-                "unit": UNIT,
-                "frac": round(achieved / peak, 4),
-                "peak_source": peak_src,
-                "traffic": profiled_traffic(args.workload),
-                "kernel": ("moe::gg::grouped_gemm_kernel (1 SM)" if sm_count < 2 or
-                           os.environ.get("MOE_B200_GEMM_KERNEL") == "1"
-                           else "moe::gg::pair::grouped_gemm_pair_kernel (CTA pairs, TMA-store epilogue)"),
-                "algorithmic_work": f"2*M*K*N = {flops / 1e9:.2f} GFLOP per launch (M={m_rows} real rows)",
-            },
+            "config": gemm_config(args.workload, sm_count, world),
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "clocks": clocks,
+            "clocks": res["clocks"],
             "gpu_launches": args.steps,
+            **extras,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -159,7 +159,8 @@ MOE_API int32_t moe_grouped_gemm_wgrad(const void* a, int64_t lda, const void* b
  * 2^31 - 4096; larger problems are refused with MOE_ERR_CAPACITY.
  * Set-up: the first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture.
+ * any stream capture.  A failed lookup returns MOE_ERR_CUDA and is retried by
+ * the next call on that device.
  * Sharing: every call on a device uses the same counter, which keeps what the
  * last call left and is re-zeroed on `stream` at the start of each call.  Calls
  * that overlap on the GPU (e.g. on two streams at once) race on it and must be

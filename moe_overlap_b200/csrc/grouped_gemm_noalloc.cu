@@ -26,30 +26,33 @@ constexpr int kNoAllocScratchWords = 64;
 static __device__ __align__(256) int32_t g_gemm_noalloc_scratch[kNoAllocScratchWords];
 
 struct NoAllocSlot {
-  std::once_flag once;
-  int32_t* dev_ptr = nullptr;
-  int rc = MOE_OK;
+  std::mutex mu;
+  int32_t* dev_ptr = nullptr;  // set only once a lookup has succeeded
 };
 NoAllocSlot g_noalloc[kMaxDevices];
 
 // Device address of the scratch array on the current device.  In host code the
 // array's name is only a host-side stand-in, so the real address has to be
-// looked up once per device, with that device current.
+// looked up once per device, with that device current.  A failed lookup (for
+// instance one attempted during stream capture) is not remembered: the next
+// call on that device tries again, and the CUDA error it left is cleared so
+// that it is not reported later against an unrelated operation.
 int noalloc_scratch(int32_t** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return MOE_ERR_UNSUPPORTED;
   NoAllocSlot& s = g_noalloc[dev];
-  std::call_once(s.once, [&] {
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (s.dev_ptr == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_gemm_noalloc_scratch) != cudaSuccess || p == nullptr) {
-      s.rc = MOE_ERR_CUDA;
-      return;
+      cudaGetLastError();
+      return MOE_ERR_CUDA;
     }
     s.dev_ptr = static_cast<int32_t*>(p);
-  });
+  }
   *out = s.dev_ptr;
-  return s.rc;
+  return MOE_OK;
 }
 
 }  // namespace

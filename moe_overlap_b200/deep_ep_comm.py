@@ -117,6 +117,12 @@ def exchange_buffers(group, rank: int, world: int, own_base: int, export_handle,
     return bases
 
 
+def _mark(timeline: list, name: str, stream) -> None:
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record(stream)
+    timeline.append((name, ev))
+
+
 def _env_int(name: str, default: int) -> int:
     v = os.environ.get(name)
     return int(v) if v not in (None, "") else default
@@ -214,8 +220,15 @@ class DeepEPDispatcher:
                  handle: Optional["DispatchHandle"] = None,
                  exact_size: Optional[bool] = None, expert_alignment: int = 1,
                  scale_rows: bool = False, num_sms: Optional[int] = None,
-                 pad_rows: Optional[bool] = None, inline: bool = False) -> DispatchResult:
+                 pad_rows: Optional[bool] = None, inline: bool = False,
+                 timeline: Optional[list] = None) -> DispatchResult:
         """Sends each token's row to the ranks owning its top-k experts.
+
+        ``timeline`` (a list) receives (phase, CUDA event) pairs recorded on the
+        exchange stream: ``start``, then one after each of the dispatch's three
+        launches: ``layout_count`` (per-expert ranks and the count push),
+        ``scatter`` (rows pushed to their owners) and ``wait`` (every peer's rows
+        landed here).
 
         With ``handle`` (the handle of the most recent dispatch; ``topk_idx`` and
         ``topk_weights`` then stay None, as in DeepEP's cached mode,
@@ -267,9 +280,19 @@ class DeepEPDispatcher:
             # marks the rows past the received count (-1 ids, zero weights) so the
             # views read like DeepEP's.  Callers that use expert_offsets can skip it.
             pad = (not exact) if pad_rows is None else bool(pad_rows)
-            self._ep.dispatch(xc, ic, wc, slot, 0 if self._device_epochs else epoch,
-                              num_sms or self.num_sms, pad, self.wait_ns,
-                              self._status, expert_alignment, scale_rows)
+            kepoch, blocks = 0 if self._device_epochs else epoch, num_sms or self.num_sms
+            if timeline is None:
+                self._ep.dispatch(xc, ic, wc, slot, kepoch, blocks, pad, self.wait_ns,
+                                  self._status, expert_alignment, scale_rows)
+            else:  # the same three launches, with an event before and after each
+                _mark(timeline, "start", stream)
+                self._ep.dispatch_begin(xc, ic, wc, slot, kepoch, self._status)
+                _mark(timeline, "layout_count", stream)
+                self._ep.dispatch_scatter(xc, ic, wc, slot, kepoch, blocks, pad, self.wait_ns,
+                                          self._status, expert_alignment, scale_rows)
+                _mark(timeline, "scatter", stream)
+                self._ep.dispatch_end(slot, kepoch, self.wait_ns, self._status)
+                _mark(timeline, "wait", stream)
             offs = self._ep.slots[slot].expert_offsets
             event = torch.cuda.Event()
             event.record(stream)
@@ -400,7 +423,13 @@ class DeepEPDispatcher:
                 previous_event: Optional[object] = None, *,
                 weighted: bool = False,
                 out: Optional[torch.Tensor] = None,
-                num_sms: Optional[int] = None, inline: bool = False) -> Tuple[torch.Tensor, object]:
+                num_sms: Optional[int] = None, inline: bool = False,
+                timeline: Optional[list] = None) -> Tuple[torch.Tensor, object]:
+        """Sums, per token, the expert outputs its owners produced for it (in original
+        token order); with ``weighted`` each row is scaled by its top-k weight.
+        ``timeline`` (a list) receives (phase, CUDA event) pairs recorded on the
+        exchange stream: ``start``, ``ready`` (this rank's outputs announced to
+        every peer) and ``pull`` (rows pulled and reduced)."""
         if not isinstance(handle, DispatchHandle) or handle.combined:
             raise RuntimeError("combine needs the handle of an outstanding dispatch")
         if expert_out.dtype != torch.bfloat16 or expert_out.dim() != 2 or \
@@ -424,9 +453,18 @@ class DeepEPDispatcher:
                 if rows > views.expert_out.shape[0]:
                     raise ValueError("expert_out has more rows than the receive buffer")
                 views.expert_out[:rows].copy_(expert_out)
-            self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot,
-                             0 if self._device_epochs else handle.epoch,
-                             weighted, out, num_sms or self.num_sms, self.wait_ns, self._status)
+            kepoch = 0 if self._device_epochs else handle.epoch
+            if timeline is None:
+                self._ep.combine(handle.topk_idx, handle.topk_weights, handle.slot, kepoch,
+                                 weighted, out, num_sms or self.num_sms, self.wait_ns, self._status)
+            else:  # the same two launches, with an event before and after each
+                _mark(timeline, "start", stream)
+                self._ep.combine_begin(handle.slot, kepoch)
+                _mark(timeline, "ready", stream)
+                self._ep.combine_end(handle.topk_idx, handle.topk_weights, handle.slot, kepoch,
+                                     weighted, out, num_sms or self.num_sms, self.wait_ns,
+                                     self._status)
+                _mark(timeline, "pull", stream)
             event = torch.cuda.Event()
             event.record(stream)
         # (under CUDA-graph capture the graph keeps its memory; nothing to record)

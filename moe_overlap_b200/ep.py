@@ -199,9 +199,9 @@ class Endpoint:
 
     def dispatch_cached(self, x, topk_idx, topk_w, src_slot, slot, epoch, num_blocks, pad_rows,
                         wait_ns, status, scale_rows: bool = False):
-        self._on_device(x, topk_idx, topk_w)
         """Rows x for the tokens and top-k choices of the dispatch into ``src_slot``,
         in that dispatch's layout, into ``slot`` (see moe_ep_dispatch_cached)."""
+        self._on_device(x, topk_idx, topk_w)
         t, k = topk_idx.shape
         _lib.check_call(
             self.lib.moe_ep_dispatch_cached(self.handle, x.data_ptr(), topk_idx.data_ptr(),
@@ -258,10 +258,10 @@ class Endpoint:
             "moe_ep_combine")
 
     def push_gemm(self, a, b, slot, epoch, num_sms, use_atomic, work_counter, status) -> None:
-        self._on_device(a, b, work_counter)
         """Fused down-projection + combine push of ``a`` rows (this rank's receive
         layout of ``slot``) by ``b`` [E_local, K, hidden] (any strides that
         moe_grouped_gemm accepts); see moe_ep_push_gemm."""
+        self._on_device(a, b, work_counter)
         _lib.check_call(
             self.lib.moe_ep_push_gemm(self.handle, a.data_ptr(), a.stride(0), b.data_ptr(),
                                       b.stride(0), b.stride(1), b.stride(2), a.shape[0], a.shape[1],

@@ -144,19 +144,22 @@ def grouped_gemm(
     lib = _lib.load()
     _lib.check_status(device)
     status = _lib.status_word(device)
-    rc = lib.moe_grouped_gemm_ex(
-        a_use.data_ptr(), a_use.stride(0),
-        b_use.data_ptr(), b_use.stride(0), b_use.stride(1), b_use.stride(2),
-        c_use.data_ptr(), c_use.stride(0),
-        offs.data_ptr(), offs64,
-        m_total, k_size + k_pad, n_use, num_experts,
-        dtype_code, act_code, int(num_sms), 1 if use_atomic_queue else 0,
-        counter_ptr,
-        row_scale.data_ptr() if row_scale is not None else None,
-        aux_in.data_ptr() if aux_in is not None else None,
-        aux_out.data_ptr() if aux_out is not None else None,
-        ld_aux, status.data_ptr(), _lib.stream_handle(device),
-    )
+    # The C layer reads the SM count and architecture of the current device and
+    # launches there: make the operands' device current for the call.
+    with torch.cuda.device(device):
+        rc = lib.moe_grouped_gemm_ex(
+            a_use.data_ptr(), a_use.stride(0),
+            b_use.data_ptr(), b_use.stride(0), b_use.stride(1), b_use.stride(2),
+            c_use.data_ptr(), c_use.stride(0),
+            offs.data_ptr(), offs64,
+            m_total, k_size + k_pad, n_use, num_experts,
+            dtype_code, act_code, int(num_sms), 1 if use_atomic_queue else 0,
+            counter_ptr,
+            row_scale.data_ptr() if row_scale is not None else None,
+            aux_in.data_ptr() if aux_in is not None else None,
+            aux_out.data_ptr() if aux_out is not None else None,
+            ld_aux, status.data_ptr(), _lib.stream_handle(device),
+        )
     _lib.check_call(rc, "moe_grouped_gemm_ex")
     if c_use is not out:
         out.copy_(c_use[:, :n_size])
@@ -299,17 +302,19 @@ def tile_list(
     lib = _lib.load()
     count = torch.zeros(1, dtype=torch.int32, device=device)
     stream = _lib.stream_handle(device)
-    rc = lib.moe_tile_list(offs.data_ptr(), offs64, num_experts, m_total, n_size, block_m, block_n,
-                           order, None, None, None, 0, count.data_ptr(), None, stream)
+    with torch.cuda.device(device):
+        rc = lib.moe_tile_list(offs.data_ptr(), offs64, num_experts, m_total, n_size, block_m,
+                               block_n, order, None, None, None, 0, count.data_ptr(), None, stream)
     _lib.check_call(rc, "moe_tile_list")
     total = int(count.item())
     we = torch.empty(total, dtype=torch.int32, device=device)
     wm = torch.empty_like(we)
     wn = torch.empty_like(we)
     if total:
-        rc = lib.moe_tile_list(offs.data_ptr(), offs64, num_experts, m_total, n_size, block_m,
-                               block_n, order, we.data_ptr(), wm.data_ptr(), wn.data_ptr(), total,
-                               count.data_ptr(), None, stream)
+        with torch.cuda.device(device):
+            rc = lib.moe_tile_list(offs.data_ptr(), offs64, num_experts, m_total, n_size, block_m,
+                                   block_n, order, we.data_ptr(), wm.data_ptr(), wn.data_ptr(),
+                                   total, count.data_ptr(), None, stream)
         _lib.check_call(rc, "moe_tile_list")
     return we, wm, wn
 
@@ -341,10 +346,12 @@ def grouped_gemm_wgrad(a: torch.Tensor, b: torch.Tensor, expert_offsets: torch.T
         num_sms = torch.cuda.get_device_properties(device).multi_processor_count
     lib = _lib.load()
     _lib.check_status(device)
-    rc = lib.moe_grouped_gemm_wgrad(a_c.data_ptr(), a_c.stride(0), b_c.data_ptr(), b_c.stride(0),
-                                    out.data_ptr(), out.stride(1), out.stride(0), offs.data_ptr(),
-                                    offs64, rows, m, n, num_experts, _DTYPE_CODE[a.dtype],
-                                    int(num_sms), _lib.status_word(device).data_ptr(),
-                                    _lib.stream_handle(device))
+    with torch.cuda.device(device):
+        rc = lib.moe_grouped_gemm_wgrad(a_c.data_ptr(), a_c.stride(0), b_c.data_ptr(),
+                                        b_c.stride(0), out.data_ptr(), out.stride(1), out.stride(0),
+                                        offs.data_ptr(), offs64, rows, m, n, num_experts,
+                                        _DTYPE_CODE[a.dtype], int(num_sms),
+                                        _lib.status_word(device).data_ptr(),
+                                        _lib.stream_handle(device))
     _lib.check_call(rc, "moe_grouped_gemm_wgrad")
     return out

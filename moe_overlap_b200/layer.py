@@ -314,6 +314,49 @@ class MoELayer:
             times = dict(zip(sorted(times), t.tolist()))
         return out, times
 
+    def exchange_phase_times(self, x: torch.Tensor, routing,
+                             host_cover_cycles: int = 2_000_000) -> dict:
+        """Device time (ms) of each exchange launch of the first chunk, run alone.
+
+        The first chunk's dispatch (layout + count push, scatter, wait for every
+        peer's rows) and, after its expert GEMMs, its combine (ready flag, pull +
+        reduce) run with a device synchronisation and, across ranks, a barrier
+        before each, behind a device-side delay of ``host_cover_cycles`` SM cycles
+        so the host's enqueueing is not timed.  Both use the grid of the forward's
+        unoverlapped phases (four blocks per SM).  Returns this rank's times:
+        ``dispatch_layout_count``, ``dispatch_scatter``, ``dispatch_wait``,
+        ``combine_ready``, ``combine_pull``.  The scatter includes the wait for
+        every peer's counts, and the dispatch's wait the arrival of the peers' rows.
+        """
+        x = x.to(torch.bfloat16).contiguous()
+        _, idx, w = routing
+        s, e = self.chunk_plan(x.shape[0])[0]
+        disp = self.dispatcher
+        marks_d, marks_c = [], []
+        self._sync_all()
+        if host_cover_cycles > 0:
+            torch.cuda._sleep(int(host_cover_cycles))
+        res = disp.dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False,
+                            num_sms=self.solo_comm_blocks, timeline=marks_d)
+        res.event.current_stream_wait()
+        y = self._experts(res)
+        self._sync_all()
+        if host_cover_cycles > 0:
+            torch.cuda._sleep(int(host_cover_cycles))
+        out = torch.empty(e - s, self.hidden, dtype=torch.bfloat16, device=self.device)
+        if y is None:  # fused combine push: the transfer ran inside the GEMM
+            _, ev = self._combine(None, res.handle, out=out, num_sms=self.solo_comm_blocks)
+        else:
+            _, ev = disp.combine(y, res.handle, weighted=True, out=out,
+                                 num_sms=self.solo_comm_blocks, timeline=marks_c)
+        ev.current_stream_wait()
+        self._sync_all()
+        times = {}
+        for marks, prefix in ((marks_d, "dispatch_"), (marks_c, "combine_")):
+            for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
+                times[prefix + name] = a.elapsed_time(b)
+        return times
+
     def _sync_all(self) -> None:
         torch.cuda.synchronize(self.device)
         if self.world > 1:
@@ -469,6 +512,10 @@ class TrainStepGraph:
                 self._clear_grads()
                 out, _, _ = layer.forward_autograd(x)
                 out.backward(dout)
+                # Drop the warm-up's autograd graph: a node kept alive from it would keep
+                # the parameters' AccumulateGrad nodes bound to this side stream, not to
+                # the capture stream that produces the captured step's gradients.
+                del out
         cur.wait_stream(side)
         torch.cuda.synchronize(layer.device)
         self._clear_grads()

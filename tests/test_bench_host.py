@@ -103,3 +103,38 @@ def test_e2e_legs_reduce_over_gloo_ranks(pipe_ms, want):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert got[0] == want and got[1] == want
+
+
+def test_both_arms_print_the_same_gemm_config():
+    """The reference arm and the headline describe the workload with one config object."""
+    cfg = bench.gemm_config("gemm_cfg2", 148, 1)
+    assert cfg == bench.gemm_config("gemm_cfg2", 148, 1)
+    assert cfg["rows"] == 8192 and cfg["counts"] == [512] * 16 and cfg["schedule"] == "striped"
+    assert bench.gemm_config("gemm_cfg3", 148, 2)["schedule"] == "atomic"
+
+
+def test_rows_computed_counts_pair_tiles():
+    assert bench.rows_computed([512] * 16) == 8192
+    assert bench.rows_computed([1, 0, 257]) == 256 + 512
+
+
+def test_torch_loop_restatement_matches_the_numpy_oracle():
+    """oracle/torch_loop.py (the timed CPU reference) agrees with the oracle's fp32 loop
+    to one bf16 rounding (both accumulate in fp32 and round once)."""
+    import torch
+
+    from oracle import grouped_gemm as og
+    from oracle.numerics import to_f32
+    from oracle.torch_loop import grouped_gemm_loop, loop_flops
+    from tests._inputs import gemm_inputs, to_storage
+
+    counts = [37, 0, 129, 64]
+    a, b, off = gemm_inputs(counts, 256, 192, "bf16", seed=3)
+    got = grouped_gemm_loop(a, b, off.tolist())
+    want, defined = og.grouped_gemm(to_storage(a), to_storage(b), off.numpy(), "bf16")
+    g = to_f32(to_storage(got), "bf16")[defined]
+    w = to_f32(want, "bf16")[defined]
+    assert np.max(np.abs(g - w)) <= 2.0 ** -7 * np.max(np.abs(w)) + 1e-2
+    assert loop_flops(a.shape, b.shape, off.tolist()) == 2 * sum(counts) * 256 * 192
+    assert loop_flops(a.shape, b.shape, off.tolist(), [2]) == 2 * 129 * 256 * 192
+    del torch

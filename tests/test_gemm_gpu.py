@@ -259,3 +259,23 @@ def test_epilogue_gelu_save_grad_and_mul_aux(cuda_device, num_sms):
     assert_matches_oracle(c2, want2, defined, "bf16")
     with pytest.raises(mo.MoeError):
         mo.grouped_gemm(da, db, doff, activation="gelu_save_grad")  # aux_out is required
+
+
+def test_operands_on_a_device_that_is_not_current():
+    """Operands on cuda:1 while cuda:0 is current run on cuda:1, as torch ops do."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    dev1 = torch.device("cuda", 1)
+    if torch.cuda.get_device_capability(dev1)[0] != 10:
+        pytest.skip("needs an sm_100 device")
+    counts = [40, 0, 300, 129]
+    a, b, off = gemm_inputs(counts, 128, 256, "bf16", seed=31)
+    with torch.cuda.device(0):
+        c = mo.persistent_grouped_gemm(a.to(dev1), b.to(dev1), off.to(dev1), num_sms=148)
+        h = mo.grouped_gemm(a.to(dev1), b.to(dev1), off.to(dev1), activation="gelu")
+        we, _, _ = mo.tile_list(off.to(dev1), int(off[-1]), 256)
+    mo.check_status(dev1, sync=True)
+    assert c.device == dev1 and we.device == dev1
+    for out, act in ((c, None), (h, "gelu")):
+        ref, defined = og.grouped_gemm(to_storage(a), to_storage(b), off.numpy(), "bf16", act)
+        assert_matches_oracle(out, ref, defined, "bf16")

@@ -152,6 +152,7 @@ def test_backward_after_another_dispatch_is_rejected(cuda_device):
     layer.close()
 
 
+@pytest.mark.filterwarnings("error:The AccumulateGrad node's stream does not match")
 def test_train_step_graph_replays_the_eager_step(cuda_device):
     """A training step captured as a CUDA graph (device-drawn exchange epochs) gives the
     eager step's results on the same data, replay after replay and for new data."""

@@ -6,8 +6,8 @@ an allocation could stall the device): its atomic tile-queue counter lives in a
 fixed device array inside the library instead of a caller-provided buffer.
 
 The test calls it through the C ABI twice in a row, and checks both results
-against the regular moe_grouped_gemm entry point with the tolerance the other
-GEMM tests use.  The second call only passes if the shared counter was cleared
+against the regular moe_grouped_gemm entry point and against the CPU oracle's
+fp32-accumulated per-expert loop, with the tolerance the other GEMM tests use.  The second call only passes if the shared counter was cleared
 again, since the first call leaves it at (tiles + grid).  This file sorts last
 so a run that stops at the first failure has already run every other test; it
 passes alone in a fresh process as well.
@@ -19,15 +19,19 @@ import pytest
 import torch
 
 from moe_overlap_b200 import _lib
+from oracle import grouped_gemm as og
 from oracle.numerics import to_f32
 from tests._inputs import gemm_inputs, to_storage, zipf_counts
 
 pytestmark = pytest.mark.gpu
 
 
-def _within_gemm_tolerance(got: torch.Tensor, want: torch.Tensor, rows: int) -> None:
+def _within_gemm_tolerance(got: torch.Tensor, want, rows: int) -> None:
+    """bf16 rule of the GEMM tests: max_abs <= 2^-7 max|ref| + 1e-2, rel-L2 <= 1e-2.
+    ``want`` is a device tensor or the oracle's bf16 storage array."""
     g = to_f32(to_storage(got[:rows]), "bf16").astype(np.float64)
-    w = to_f32(to_storage(want[:rows]), "bf16").astype(np.float64)
+    w_store = to_storage(want[:rows]) if isinstance(want, torch.Tensor) else want[:rows]
+    w = to_f32(w_store, "bf16").astype(np.float64)
     diff = np.abs(g - w)
     atol = 2.0 ** -7 * float(np.abs(w).max()) + 1e-2
     rel_l2 = float(np.linalg.norm(diff) / max(np.linalg.norm(w), 1e-30))
@@ -37,8 +41,9 @@ def _within_gemm_tolerance(got: torch.Tensor, want: torch.Tensor, rows: int) -> 
 def test_noalloc_entry_point_matches_regular_entry_point(cuda_device):
     lib = _lib.load()
     counts = zipf_counts(2500, 12, 1.2, seed=21)
-    a, b, off = gemm_inputs(counts, 384, 520, "bf16", seed=22)
-    a, b, off = a.to(cuda_device), b.to(cuda_device), off.to(cuda_device)
+    a_cpu, b_cpu, off_cpu = gemm_inputs(counts, 384, 520, "bf16", seed=22)
+    oracle_c, _ = og.grouped_gemm(to_storage(a_cpu), to_storage(b_cpu), off_cpu.numpy(), "bf16")
+    a, b, off = a_cpu.to(cuda_device), b_cpu.to(cuda_device), off_cpu.to(cuda_device)
     m_total, k = a.shape
     num_experts, _, n = b.shape
     stream = torch.cuda.current_stream(cuda_device).cuda_stream
@@ -67,6 +72,7 @@ def test_noalloc_entry_point_matches_regular_entry_point(cuda_device):
         assert int(status.item()) == 0, _lib.status_string(int(status.item()))
         assert not torch.isnan(got[:rows]).any()
         _within_gemm_tolerance(got, want, rows)
+        _within_gemm_tolerance(got, oracle_c, rows)
 
 
 def test_noalloc_entry_point_refuses_oversized_problems(cuda_device):
