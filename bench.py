@@ -185,9 +185,17 @@ def device_sm_count(local_rank: int = 0) -> int:
 
 
 def rows_computed(counts) -> int:
-    """Rows the CTA-pair GEMM multiplies for these expert counts (tensor work incl. padding):
-    every expert's rows are cut into 256-row pair tiles."""
-    return sum(256 * (-(-int(c) // 256)) for c in counts)
+    """Rows the CTA-pair GEMM multiplies for these expert counts (tensor work incl. padding).
+
+    Every expert's rows are cut into 256-row pair tiles; a last tile of at most
+    128 rows runs swapped (the weights take the MMA's 256-row side and the tile's
+    rows a 128-wide N), so it costs 128 rows; a longer last tile costs 256.
+    """
+    total = 0
+    for c in counts:
+        full, tail = divmod(int(c), 256)
+        total += 256 * full + (0 if tail == 0 else (128 if tail <= 128 else 256))
+    return total
 
 
 # ---------------------------------------------------------------- CPU side --
@@ -264,7 +272,7 @@ def cpu_baseline(name: str, budget_s: float = 20.0) -> dict:
     while True:
         done_flops += ref.step()
         passes += 1
-        if time.perf_counter() - t0 > min(budget_s, 2.0) or passes >= 5:
+        if time.perf_counter() - t0 > min(budget_s, 3.0) or passes >= 100:
             break
     dt = time.perf_counter() - t0
     return {

@@ -46,6 +46,7 @@ struct Params {
   void* aux_out;           // aux_out[row, col] = v (before the activation)
   int64_t ld_aux;
   int c_tma;               // the CTA-pair kernel may store C through its TMA store map
+  int swap_tails;          // the CTA-pair kernel computes tiles of <= 128 rows swapped
   PushTarget push;         // combine push instead of C (push.src != null)
 };
 

@@ -346,6 +346,16 @@ static bool gemm_tma_store() {
   return v;
 }
 
+// MOE_B200_GEMM_SWAP=0 computes every tile of the CTA-pair kernel as 256 rows
+// (default 1: tiles of at most 128 rows run swapped, see grouped_gemm_pair.cu).
+static bool gemm_swap_tails() {
+  static const bool v = [] {
+    const char* e = std::getenv("MOE_B200_GEMM_SWAP");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return v;
+}
+
 // Tile walk order: 0 (default) = the reference's expert, tile_m, tile_n fastest
 // (measured ~1 % faster on BASELINE configs 2/3 than 1 = expert, tile_n, tile_m
 // fastest).  MOE_B200_GEMM_ORDER overrides.
@@ -484,6 +494,12 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
   p.aux_out = aux_out;
   p.ld_aux = ld_aux;
   p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0, nullptr};
+  // Tiles of at most 128 rows (an expert's tail) run swapped on the CTA pair when
+  // the epilogue is elementwise on the product alone (no row scale, auxiliary
+  // operands or combine push).
+  p.swap_tails = use_pair && gemm_swap_tails() && !pushing && row_scale == nullptr &&
+                 aux_in == nullptr && aux_out == nullptr &&
+                 (activation == MOE_ACT_NONE || activation == MOE_ACT_GELU);
 
   // The pair kernel stores C through a {N, m_total} map in 32x32 boxes (64-byte swizzle).
   CUtensorMap tc;

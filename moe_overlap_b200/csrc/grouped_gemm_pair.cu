@@ -23,6 +23,14 @@
 //            quadrant and every SM sub-partition runs two epilogue warps.  Each
 //            warp stages 32x32 bf16 chunks in its own 2 KiB of shared memory and
 //            writes them with TMA bulk stores (rows inside the tile's expert only).
+// Swapped tails: a tile of at most 128 rows (an expert's last rows) would leave
+// the second CTA's 128 rows of a 256-row MMA empty.  With swap_tails such a tile
+// is computed transposed instead: the 256 weight columns take the MMA's M side
+// (128 per CTA, the same B stage as usual, now the MMA's A operand) and the tile's
+// rows its N side (N = 128: 64 rows from each CTA's A stage), so the tensor work
+// of the tile halves.  Each CTA's TMEM then holds its 128 output columns in its
+// lanes and the tile's rows in 128 accumulator columns; the epilogue stores
+// them transposed (plain or GELU epilogues only).
 // No load uses cluster multicast; the pair exchanges only barrier arrivals and
 // the tile ring entries through shared::cluster addresses.
 #include <algorithm>
@@ -71,6 +79,46 @@ struct Ctrl {
 __host__ __device__ constexpr size_t smem_bytes(int num_experts) {
   return 1024 + size_t(STAGES) * (A_STAGE_BYTES + B_STAGE_BYTES) + size_t(NUM_EPI_WARPS) * EPI_STAGE_BYTES +
          ((sizeof(Ctrl) + 15) / 16) * 16 + size_t(3) * 4 * (num_experts + 1);
+}
+
+// Epilogue of a swapped tile: TMEM lane (32*quad + lane) of this CTA holds output
+// column n_cta + 32*quad + lane, accumulator column j the tile's row j.  The warp
+// covers rows [r_first, r_first + 64) in two 32-row chunks; lane pairs swap values
+// so that each thread stores two adjacent columns of one row (4 bytes), and the
+// 32 lanes of a warp store 64 contiguous bytes of a row per instruction.
+template <bool BF16>
+__device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, int quad, int row0,
+                                              int rows, int r_first, int n_cta, const Params& p) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int col = n_cta + quad * 32 + lane;
+  const bool odd = (lane & 1) != 0;
+  const int pair_col = col - (odd ? 1 : 0);  // first column of the pair this thread stores
+  const bool col_ok = pair_col < p.n;        // n is a multiple of 8: col + 1 < n as well
+  const bool gelu = p.activation == MOE_ACT_GELU;
+#pragma unroll 1
+  for (int ch = 0; ch < 2; ++ch) {
+    const int rbase = r_first + 32 * ch;
+    if (rbase >= rows) break;  // warp-uniform
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_lane_base + uint32_t(rbase), r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+      if (gelu) {
+        v0 = gelu_erf(v0);
+        v1 = gelu_erf(v1);
+      }
+      // even lane: row j, columns (col, col+1); odd lane: row j+1, columns (col-1, col)
+      const float mine_other = odd ? v0 : v1;
+      const float theirs = __shfl_xor_sync(0xffffffffu, mine_other, 1);
+      const int rr = rbase + j + (odd ? 1 : 0);
+      const uint32_t packed = odd ? pack2<BF16>(theirs, v1) : pack2<BF16>(v0, theirs);
+      if (col_ok && rr < rows)
+        *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.c) + (int64_t(row0) + rr) * p.ldc +
+                                     pair_col) = packed;
+    }
+  }
 }
 
 // 144 registers: with 10 warps, SM sub-partitions 0 and 1 hold three of them
@@ -186,7 +234,10 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
           qphase ^= 1;
         }
         if (s.z < 0) break;
-        const int row_a = s.x + static_cast<int>(crank) * BM_CTA;
+        // A swapped tile takes 64 rows from each CTA (the MMA's N side); the box
+        // still loads 128, of which the MMA reads the first 64.
+        const bool swapped = p.swap_tails && s.y <= BM_CTA;
+        const int row_a = s.x + static_cast<int>(crank) * (swapped ? BM_CTA / 2 : BM_CTA);
         const int n_b = s.z + static_cast<int>(crank) * BN_CTA;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(smem_u32(&ctrl->empty[stage]), phase ^ 1, abort_flag)) {
@@ -226,6 +277,8 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
     // ---------------------------------------------------- MMA (leader only) --
     if (leader && lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
+      // swapped tile: weights as A (M = 256 columns), the tile's rows as B (N = 128)
+      constexpr uint32_t idesc_sw = idesc_f16(BF16, BM, BM_CTA, B_MN_MAJOR, false);
       int stage = 0;
       uint32_t phase = 0;
       int q = 0;
@@ -252,6 +305,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const bool swapped = p.swap_tails && s.y <= BM_CTA;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(smem_u32(&ctrl->full[stage]), phase, abort_flag)) {
             failed = true;
@@ -269,7 +323,10 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
             } else {
               bdesc = smem_desc_sw128(b_base + kk * UMMA_K * 2, 16, 1024);
             }
-            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if (swapped)
+              umma_f16_pair(d_tmem, bdesc, adesc, idesc_sw, (kb | kk) != 0 ? 1u : 0u);
+            else
+              umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           issued_any = true;
           const uint32_t e_local = smem_u32(&ctrl->empty[stage]);
@@ -327,11 +384,16 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
         break;
       }
       tc_fence_after();
+      if (!PUSH && p.swap_tails && s.y <= BM_CTA) {
+        store_swapped<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), lane, quad,
+                            s.x, s.y, col_half * 64, s.z + static_cast<int>(crank) * BN_CTA, p);
+      } else {
       const int rows_here = min(int(BM_CTA), max(0, s.y - static_cast<int>(crank) * int(BM_CTA)));
       store_accumulator<BF16, PUSH>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,
                               lane, s.x + static_cast<int>(crank) * BM_CTA, rows_here, s.z, p,
                               col_half * 4, 4, p.c_tma ? &tmap_c : nullptr,
                               smem_u32(sEpi + (warp - 2) * EPI_STAGE_BYTES));
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->tempty[acc]), 0));
