@@ -312,6 +312,51 @@ MOE_API int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* topk_
                                 int32_t* status, void* stream);
 
 /*
+ * Dispatch with an FP8 payload: DeepEP's dispatch of an (x_fp8, x_scales) pair
+ * (thirdParty/DeepEP/deep_ep/buffer.py:338-342, per-128 scales copied with each
+ * row at csrc/kernels/intranode.cu:397-402).  x_fp8: [num_tokens][hidden] e4m3
+ * bytes; x_scales: [num_tokens][hidden/128] float; hidden % 128 == 0.  Same
+ * phases, layout, metadata and arguments as moe_ep_dispatch (expert_alignment 1,
+ * no scale_rows); both arrays are copied unchanged, so a row crosses NVLink in
+ * hidden + hidden/32 bytes instead of 2 * hidden.  In the receive slot the e4m3
+ * rows are at views.recv_x as [cap_rows][hidden] bytes and their scales at
+ * views.recv_x + cap_rows * hidden as [cap_rows][hidden/128] float.
+ */
+MOE_API int32_t moe_ep_dispatch_fp8(moe_ep_t ep, const void* x_fp8, const float* x_scales,
+                                    const int64_t* topk_idx, const float* topk_weights,
+                                    int32_t num_tokens, int32_t topk, int32_t slot, uint64_t epoch,
+                                    int32_t num_blocks, int32_t pad_rows, uint64_t wait_ns,
+                                    int32_t* status, void* stream);
+/* Its scatter phase alone (after moe_ep_dispatch_begin; moe_ep_dispatch_end follows). */
+MOE_API int32_t moe_ep_dispatch_fp8_scatter(moe_ep_t ep, const void* x_fp8, const float* x_scales,
+                                            const int64_t* topk_idx, const float* topk_weights,
+                                            int32_t num_tokens, int32_t topk, int32_t slot,
+                                            uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
+                                            uint64_t wait_ns, int32_t* status, void* stream);
+
+/*
+ * Per-128-column e4m3 quantisation of bf16 rows, as DeepEP's per_token_cast_to_fp8
+ * (thirdParty/DeepEP/tests/utils.py:50-58) defines it: for each row and group of
+ * 128 columns, amax = max|x| clamped to 1e-4, out = e4m3(x * (1/amax * 448)) with
+ * round-to-nearest-even and saturation, scale = amax / 448.  x: [rows][hidden]
+ * bf16 (row stride ldx elements); out_fp8: [rows][hidden] bytes (stride ld_out);
+ * out_scales: [rows][hidden/128] float (stride ld_scales).  hidden % 128 == 0.
+ */
+MOE_API int32_t moe_fp8_quantize(const void* x, int64_t ldx, int64_t rows, int32_t hidden,
+                                 void* out_fp8, int64_t ld_out, float* out_scales,
+                                 int64_t ld_scales, void* stream);
+
+/*
+ * The inverse, as DeepEP's per_token_cast_back (tests/utils.py:61-75):
+ * out = bf16(float(x_fp8) * scale) for rows [0, rows), where rows = rows_max or,
+ * when rows_dev (a device int32) is given, min(rows_max, *rows_dev) read on the
+ * device (e.g. the received count, the last of a dispatch's expert_offsets).
+ */
+MOE_API int32_t moe_fp8_dequantize(const void* x_fp8, int64_t ldx, const float* scales,
+                                   int64_t ld_scales, const int32_t* rows_dev, int64_t rows_max,
+                                   int32_t hidden, void* out, int64_t ld_out, void* stream);
+
+/*
  * Cached re-dispatch (DeepEP's dispatch given a handle: deep_ep/buffer.py:383-390,
  * deep_ep.cpp:588-600): new rows x for the tokens and top-k choices of the most
  * recent dispatch, which went into src_slot, pushed into the other slot `slot` at

@@ -14,6 +14,7 @@ from .gemm import (
     tile_list,
 )
 from ._lib import MoeError, check_status
+from .fp8 import dequantize_fp8, quantize_fp8
 from .router import router_topk
 
 __all__ = [
@@ -24,6 +25,8 @@ __all__ = [
     "reference_grouped_gemm",
     "tile_list",
     "router_topk",
+    "quantize_fp8",
+    "dequantize_fp8",
     "MoeError",
     "check_status",
 ]

@@ -122,6 +122,18 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_dispatch": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
                _i32, _i32, _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch_fp8": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # ep, x_fp8, scales, idx, w
+               _i32, _i32, _i32, _u64, _i32, _i32,  # T, k, slot, epoch, blocks, pad_rows
+               _u64, _c_void_p, _c_void_p]),  # wait_ns, status, stream
+    "moe_ep_dispatch_fp8_scatter": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32,
+               _i32, _u64, _c_void_p, _c_void_p]),
+    "moe_fp8_quantize": (
+        _i32, [_c_void_p, _i64, _i64, _i32, _c_void_p, _i64, _c_void_p, _i64, _c_void_p]),
+    "moe_fp8_dequantize": (
+        _i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i32, _c_void_p, _i64,
+               _c_void_p]),
     "moe_ep_dispatch_cached_begin": (_i32, [_c_void_p, _i32, _u64, _c_void_p]),
     "moe_ep_dispatch_cached_scatter": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _u64, _i32,

@@ -135,6 +135,12 @@ struct Params {
   int32_t* status;
   // dispatch
   const __nv_bfloat16* x;
+  // FP8 payload (fp8 != 0): e4m3 rows [T, hidden] and float scales [T, hidden/128]
+  // instead of x; each receive row then holds hidden bytes at recv_x + row * hidden
+  // and its scales at recv_x + cap_rows * hidden + row * hidden / 32 bytes.
+  const uint8_t* x8;
+  const float* x_scales;
+  int fp8;
   const int64_t* topk_idx;
   const float* topk_w;
   int num_tokens, topk;
@@ -387,8 +393,10 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
   const SlotLayout sl = slot_of(p);
   if (!overflow) {
     for (int t = blockIdx.x * (kCommThreads / 32) + warp; t < p.num_tokens; t += warps_total) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
+      const uint4* src = p.fp8 ? reinterpret_cast<const uint4*>(p.x8 + static_cast<int64_t>(t) * p.hidden)
+                               : reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
       uint4* dst[8];
+      float* dsc[8];  // FP8 payload: the row's scales on the owner
       float dscale[8];
       int nd = 0;
       for (int j = 0; j < p.topk; ++j) {
@@ -405,7 +413,14 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
                         p.rank_in_block[a];
         uint8_t* peer = p.peers[d];
         dscale[nd] = p.topk_w[a];
-        dst[nd++] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+        if (p.fp8) {
+          dsc[nd] = at<float>(peer, sl.recv_x + static_cast<uint64_t>(p.cap_rows) * p.hidden) +
+                    static_cast<int64_t>(row) * (p.hidden / 128);
+          dst[nd++] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * (p.hidden / 16);
+        } else {
+          dsc[nd] = nullptr;
+          dst[nd++] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+        }
         if (lane < p.topk) {
           at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
               (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
@@ -422,21 +437,30 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
           p.cb_pos[a] = cb_row;
         }
       }
+      if (p.fp8) {
+        // e4m3 row (hidden bytes) and its hidden/128 scales, copied unchanged.
+        const int nsc = p.hidden / 128;
+        for (int i = lane; i < nsc; i += 32) {
+          const float sc = p.x_scales[static_cast<int64_t>(t) * nsc + i];
+          for (int q = 0; q < nd; ++q) dsc[q][i] = sc;
+        }
+      }
+      const int nv_row = p.fp8 ? p.hidden / 16 : nvec;  // 16-byte vectors per payload row
       // Each lane loads 4 x 16 B per pass (2 KB of a row per warp)
       // before storing anything, so every load of the pass is in flight at once.
       constexpr int U = 4;
-      for (int base = 0; base < nvec; base += 32 * U) {
+      for (int base = 0; base < nv_row; base += 32 * U) {
         uint4 v[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int i = base + u * 32 + lane;
-          if (i < nvec) v[u] = __ldg(src + i);
+          if (i < nv_row) v[u] = __ldg(src + i);
         }
         for (int q = 0; q < nd; ++q) {
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (i < nvec) dst[q][i] = p.scale_rows ? scale_bf16x8(v[u], dscale[q]) : v[u];
+            if (i < nv_row) dst[q][i] = p.scale_rows ? scale_bf16x8(v[u], dscale[q]) : v[u];
           }
         }
       }
@@ -1058,20 +1082,30 @@ extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64
   return check_launch();
 }
 
-extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
-                                           const float* topk_weights, int32_t num_tokens,
-                                           int32_t topk, int32_t slot, uint64_t epoch,
-                                           int32_t num_blocks, int32_t pad_rows,
-                                           int32_t expert_alignment, int32_t scale_rows,
-                                           uint64_t wait_ns, int32_t* status, void* stream_) {
+// The scatter phase with a bf16 payload (x) or, when x8 is set, an FP8 payload
+// (e4m3 rows x8 and their per-128 scales x_scales).
+static int32_t dispatch_scatter_impl(moe_ep_t ep, const void* x, bool fp8, const void* x8,
+                                     const float* x_scales, const int64_t* topk_idx,
+                                     const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                     int32_t slot, uint64_t epoch, int32_t num_blocks,
+                                     int32_t pad_rows, int32_t expert_alignment,
+                                     int32_t scale_rows, uint64_t wait_ns, int32_t* status,
+                                     void* stream_) {
   using namespace moe::ep;
   if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
       expert_alignment < 1 || expert_alignment > 4096)
     return MOE_ERR_INVALID_ARG;
+  if (fp8 && (ep->hidden % 128 != 0 || expert_alignment != 1 || scale_rows ||
+              (num_tokens > 0 && (x8 == nullptr || x_scales == nullptr)) || !moe::aligned16(x8) ||
+              reinterpret_cast<uintptr_t>(x_scales) % 4 != 0))
+    return MOE_ERR_INVALID_ARG;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   Params p = base_params(ep, slot, epoch, wait_ns, status);
   p.x = static_cast<const __nv_bfloat16*>(x);
+  p.x8 = static_cast<const uint8_t*>(x8);
+  p.x_scales = x_scales;
+  p.fp8 = fp8 ? 1 : 0;
   p.topk_idx = topk_idx;
   p.topk_w = topk_weights;
   p.num_tokens = num_tokens;
@@ -1091,6 +1125,17 @@ extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int
     return MOE_ERR_CUDA;
   scatter_kernel<<<num_blocks, kCommThreads, 0, stream>>>(p);
   return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                           const float* topk_weights, int32_t num_tokens,
+                                           int32_t topk, int32_t slot, uint64_t epoch,
+                                           int32_t num_blocks, int32_t pad_rows,
+                                           int32_t expert_alignment, int32_t scale_rows,
+                                           uint64_t wait_ns, int32_t* status, void* stream) {
+  return dispatch_scatter_impl(ep, x, false, nullptr, nullptr, topk_idx, topk_weights, num_tokens, topk,
+                               slot, epoch, num_blocks, pad_rows, expert_alignment, scale_rows,
+                               wait_ns, status, stream);
 }
 
 extern "C" int32_t moe_ep_dispatch_end(moe_ep_t ep, int32_t slot, uint64_t epoch, uint64_t wait_ns,
@@ -1300,6 +1345,35 @@ extern "C" int32_t moe_ep_dispatch(moe_ep_t ep, const void* x, const int64_t* to
     rc = moe_ep_dispatch_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
                                  num_blocks, pad_rows, expert_alignment, scale_rows, wait_ns,
                                  status, stream);
+  if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
+  return rc;
+}
+
+extern "C" int32_t moe_ep_dispatch_fp8_scatter(moe_ep_t ep, const void* x_fp8, const float* x_scales,
+                                               const int64_t* topk_idx, const float* topk_weights,
+                                               int32_t num_tokens, int32_t topk, int32_t slot,
+                                               uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
+                                               uint64_t wait_ns, int32_t* status, void* stream) {
+  return dispatch_scatter_impl(ep, nullptr, true, x_fp8, x_scales, topk_idx, topk_weights,
+                               num_tokens, topk, slot, epoch, num_blocks, pad_rows, 1, 0, wait_ns,
+                               status, stream);
+}
+
+extern "C" int32_t moe_ep_dispatch_fp8(moe_ep_t ep, const void* x_fp8, const float* x_scales,
+                                       const int64_t* topk_idx, const float* topk_weights,
+                                       int32_t num_tokens, int32_t topk, int32_t slot,
+                                       uint64_t epoch, int32_t num_blocks, int32_t pad_rows,
+                                       uint64_t wait_ns, int32_t* status, void* stream) {
+  // Checked before the begin phase raises this rank's count flag (see moe_ep_dispatch).
+  if (ep == nullptr || num_blocks < 1 || ep->hidden % 128 != 0 ||
+      (num_tokens > 0 && (x_fp8 == nullptr || x_scales == nullptr)) || !moe::aligned16(x_fp8) ||
+      reinterpret_cast<uintptr_t>(x_scales) % 4 != 0)
+    return MOE_ERR_INVALID_ARG;
+  int rc = moe_ep_dispatch_begin(ep, x_fp8, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
+                                 status, stream);
+  if (rc == MOE_OK)
+    rc = moe_ep_dispatch_fp8_scatter(ep, x_fp8, x_scales, topk_idx, topk_weights, num_tokens, topk,
+                                     slot, epoch, num_blocks, pad_rows, wait_ns, status, stream);
   if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
   return rc;
 }

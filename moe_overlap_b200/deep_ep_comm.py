@@ -237,7 +237,8 @@ class DeepEPDispatcher:
         expert offsets and metadata, and with ``scale_rows`` that dispatch's
         weights.  The result carries a new handle for the combine.
         """
-        if x.dtype != torch.bfloat16:
+        if isinstance(x, (tuple, list)) or x.dtype != torch.bfloat16:
+            # the reference wrapper's bf16-only contract; FP8 goes through dispatch_fp8
             raise RuntimeError("This baseline expects BF16 path (tensor), not FP8 tuple.")
         if x.dim() != 2 or x.size(1) != self.hidden_size:
             raise ValueError(f"x must be [num_tokens, {self.hidden_size}]")
@@ -307,6 +308,82 @@ class DeepEPDispatcher:
         kcols = views.recv_topk_idx.stride(0)
         return DispatchResult(
             recv_x=views.recv_x[:rows],
+            recv_topk_idx=views.recv_topk_idx.as_strided((rows, topk), (kcols, 1)),
+            recv_topk_weights=views.recv_topk_weights.as_strided((rows, topk), (kcols, 1)),
+            handle=handle,
+            event=EventOverlap(event),
+            expert_offsets=offs,
+            recv_src=views.recv_src[:rows],
+        )
+
+    def dispatch_fp8(self, x: Tuple[torch.Tensor, torch.Tensor], topk_idx: torch.Tensor,
+                     topk_weights: torch.Tensor, previous_event: Optional[object] = None, *,
+                     exact_size: Optional[bool] = None, num_sms: Optional[int] = None,
+                     pad_rows: Optional[bool] = None, inline: bool = False) -> DispatchResult:
+        """Dispatch with an FP8 payload, as DeepEP's ``Buffer.dispatch`` takes one.
+
+        ``x`` is the pair (x_fp8 ``[T, H]`` float8_e4m3fn, x_scales ``[T, H/128]``
+        float32) of ``fp8.quantize_fp8`` (thirdParty/DeepEP/deep_ep/buffer.py:338-342);
+        both are moved unchanged, so each row crosses NVLink in H + H/32 bytes
+        instead of 2H.  ``recv_x`` of the result is the pair (recv_fp8 ``[n, H]``,
+        recv_scales ``[n, H/128]``), views of the receive slot in the same
+        expert-ordered layout, metadata and offsets as ``dispatch``;
+        ``fp8.dequantize_fp8`` rebuilds bf16 rows from them.  The reference's
+        wrapper (src/deep_ep_comm.py:97-98) takes bf16 only, so ``dispatch`` keeps
+        refusing a tuple and the FP8 form has its own name.
+        """
+        if not isinstance(x, (tuple, list)) or len(x) != 2:
+            raise ValueError("dispatch_fp8 takes x as the pair (x_fp8, x_scales)")
+        x8, sc = x
+        if x8.dtype != torch.float8_e4m3fn or x8.dim() != 2 or x8.size(1) != self.hidden_size:
+            raise ValueError(f"x_fp8 must be float8_e4m3fn [num_tokens, {self.hidden_size}]")
+        if self.hidden_size % 128 != 0:
+            raise ValueError("an FP8 payload needs a hidden size that is a multiple of 128")
+        if sc.dtype != torch.float32 or sc.shape != (x8.shape[0], self.hidden_size // 128):
+            raise ValueError(f"x_scales must be float32 [num_tokens, {self.hidden_size // 128}]")
+        self._require_on_device(x_fp8=x8, x_scales=sc, topk_idx=topk_idx, topk_weights=topk_weights)
+        if topk_idx.dim() != 2 or topk_idx.shape[0] != x8.shape[0] or topk_weights.shape != topk_idx.shape:
+            raise ValueError("topk_idx and topk_weights must be [num_tokens, top_k]")
+        num_tokens, topk = topk_idx.shape
+        if num_tokens > self.max_tokens or topk > self.max_topk:
+            raise ValueError(
+                f"dispatch of {num_tokens} tokens x top-{topk} exceeds the dispatcher's capacity "
+                f"({self.max_tokens} x {self.max_topk}); raise MOE_B200_MAX_TOKENS / MOE_B200_MAX_TOPK")
+        if len(self._outstanding) >= 2:
+            raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
+        if num_sms is not None and int(num_sms) < 1:
+            raise ValueError("num_sms must be at least 1")
+        exact = self.exact_size if exact_size is None else exact_size
+        if exact and self._device_epochs:
+            raise ValueError("exact_size needs host epochs; with device epochs use expert_offsets")
+        _lib.check_status(self.device)
+        self._epoch += 1
+        epoch, slot = self._epoch, self._epoch % 2
+        stream = self._enter_comm(previous_event, inline)
+        with torch.cuda.stream(stream):
+            xc = x8.contiguous()
+            if xc.data_ptr() % 16 != 0:
+                xc = xc.clone()
+            scc = sc.contiguous()
+            ic = topk_idx.to(torch.int64).contiguous()
+            wc = topk_weights.to(torch.float32).contiguous()
+            pad = (not exact) if pad_rows is None else bool(pad_rows)
+            self._ep.dispatch_fp8(xc, scc, ic, wc, slot, 0 if self._device_epochs else epoch,
+                                  num_sms or self.num_sms, pad, self.wait_ns, self._status)
+            offs = self._ep.slots[slot].expert_offsets
+            event = torch.cuda.Event()
+            event.record(stream)
+        if not inline and not torch.cuda.is_current_stream_capturing():
+            for t in (x8, sc, topk_idx, topk_weights):
+                t.record_stream(self.comm_stream)
+        views = self._ep.slots[slot]
+        rows = self._ep.received_rows(slot, epoch) if exact else views.recv_x.shape[0]
+        handle = DispatchHandle(slot, epoch, num_tokens, topk, ic, wc, xc, rows if exact else None,
+                                stream=stream, event=event)
+        self._outstanding.append(handle)
+        kcols = views.recv_topk_idx.stride(0)
+        return DispatchResult(
+            recv_x=(views.recv_fp8[:rows], views.recv_scales[:rows]),
             recv_topk_idx=views.recv_topk_idx.as_strided((rows, topk), (kcols, 1)),
             recv_topk_weights=views.recv_topk_weights.as_strided((rows, topk), (kcols, 1)),
             handle=handle,

@@ -67,6 +67,9 @@ class SlotViews:
     expert_offsets: torch.Tensor   # [E_local + 1] int32
     send_pos: torch.Tensor         # [max_tokens * max_topk] int32
     host_info: ctypes.Array        # mapped host {epoch, rows}
+    # FP8 payload of a moe_ep_dispatch_fp8, in the same bytes as recv_x (H % 128 == 0)
+    recv_fp8: torch.Tensor | None = None     # [cap, H] float8_e4m3fn
+    recv_scales: torch.Tensor | None = None  # [cap, H/128] float32
 
 
 class Endpoint:
@@ -102,7 +105,15 @@ class Endpoint:
         def raw(ptr, nbytes):
             return device_bytes(int(ptr), int(nbytes), dev, self)
 
+        fp8_rows = fp8_scales = None
+        if h % 128 == 0 and cap > 0:
+            area = raw(v.recv_x, cap * h * 2)
+            fp8_rows = area[:cap * h].view(torch.float8_e4m3fn).view(cap, h)
+            fp8_scales = area[cap * h:cap * h + cap * (h // 128) * 4].view(torch.float32) \
+                .view(cap, h // 128)
         return SlotViews(
+            recv_fp8=fp8_rows,
+            recv_scales=fp8_scales,
             recv_x=raw(v.recv_x, cap * h * 2).view(torch.bfloat16).view(cap, h),
             expert_out=raw(v.expert_out, cap * h * 2).view(torch.bfloat16).view(cap, h),
             recv_topk_idx=raw(v.recv_topk_idx, cap * k * 8).view(torch.int64).view(cap, k),
@@ -238,6 +249,18 @@ class Endpoint:
                                      self._stream()),
             "moe_ep_dispatch")
 
+    def dispatch_fp8(self, x_fp8, x_scales, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows,
+                     wait_ns, status):
+        """Dispatch of an e4m3 payload with its per-128 scales (moe_ep_dispatch_fp8)."""
+        self._on_device(x_fp8, x_scales, topk_idx, topk_w)
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_fp8(self.handle, x_fp8.data_ptr(), x_scales.data_ptr(),
+                                         topk_idx.data_ptr(), topk_w.data_ptr(), t, k, slot, epoch,
+                                         num_blocks, 1 if pad_rows else 0, wait_ns,
+                                         status.data_ptr(), self._stream()),
+            "moe_ep_dispatch_fp8")
+
     def topk_weight_grad(self, grad_out, topk_idx, slot, out, num_blocks):
         self._on_device(grad_out, topk_idx, out)
         t, k = topk_idx.shape
@@ -352,6 +375,27 @@ class LocalGroup:
         for r, ep in enumerate(self.eps):
             ep.dispatch_scatter(xs[r], idxs[r], ws[r], slot, epoch, self.num_blocks, pad_rows,
                                 self.wait_ns, self.status, expert_alignment, scale_rows)
+        for ep in self.eps:
+            ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
+        return slot, epoch
+
+    def dispatch_fp8(self, xqs, scales, idxs, ws, pad_rows: bool = False):
+        """Every rank's FP8 dispatch (e4m3 rows xqs[r], per-128 scales scales[r])."""
+        self.epoch += 1
+        slot, epoch = self.epoch % 2, self._kernel_epoch(self.epoch)
+        for r, ep in enumerate(self.eps):
+            ep.dispatch_begin(xqs[r], idxs[r], ws[r], slot, epoch, self.status)
+        lib = self.eps[0].lib
+        for r, ep in enumerate(self.eps):
+            t, k = idxs[r].shape
+            # the scatter phase alone (the begin phase ran for every rank above)
+            _lib.check_call(
+                lib.moe_ep_dispatch_fp8_scatter(ep.handle, xqs[r].data_ptr(), scales[r].data_ptr(),
+                                                idxs[r].data_ptr(), ws[r].data_ptr(), t, k, slot,
+                                                epoch, self.num_blocks, 1 if pad_rows else 0,
+                                                self.wait_ns, self.status.data_ptr(),
+                                                ep._stream()),
+                "moe_ep_dispatch_fp8_scatter")
         for ep in self.eps:
             ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
         return slot, epoch

@@ -32,6 +32,7 @@ import torch
 import torch.distributed as dist
 
 from .deep_ep_comm import DeepEPDispatcher
+from .fp8 import dequantize_fp8, quantize_fp8
 from .gemm import grouped_gemm, grouped_gemm_wgrad
 from .router import router_topk
 
@@ -89,7 +90,7 @@ class MoELayer:
                  micro_batch_size: int = 4096, use_atomic_queue: bool = True,
                  max_recv_rows: Optional[int] = None, training: bool = False,
                  taper_chunks: bool = False, fused_combine: Optional[bool] = None,
-                 enable_nvtx: bool = False):
+                 enable_nvtx: bool = False, dispatch_fp8: bool = False):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         # NVTX ranges named as the reference's (deepep_dispatch_chunk_i,
         # expert_compute_chunk_i, deepep_combine_chunk_i; train_moe_baseline.py:364-413)
@@ -110,6 +111,13 @@ class MoELayer:
         # against 1.592 / 1.590 ms), and its longer GEMM hides the same exposure.
         self.fused_combine = bool(fused_combine) if fused_combine is not None else False
         self.use_atomic = use_atomic_queue
+        # FP8 dispatch payload (forward only): each chunk is quantised per 128
+        # columns (e4m3 + float scales, DeepEP's FP8 format), dispatched in that form
+        # and dequantised to bf16 on the owner before its up-projection.
+        if dispatch_fp8 and (training or hidden_size % 128 != 0):
+            raise ValueError("dispatch_fp8 needs the forward path and a hidden size that is a "
+                             "multiple of 128")
+        self.dispatch_fp8 = bool(dispatch_fp8)
         self.device = torch.device("cuda", torch.cuda.current_device())
         dev, bf16 = self.device, torch.bfloat16
         self.router_w = torch.zeros(num_experts, hidden_size, dtype=bf16, device=dev)
@@ -165,14 +173,28 @@ class MoELayer:
             logits = torch.matmul(x.to(torch.bfloat16), self.router_w.detach().t())
             return router_topk(logits, self.top_k, bias=self.router_b, renormalize=self.renormalize)
 
+    def _dispatch(self, xs, idx, w, **kw):
+        """One chunk's dispatch: bf16 rows, or with ``dispatch_fp8`` the chunk quantised
+        to e4m3 + per-128 scales on the current stream and dispatched in that form."""
+        if not self.dispatch_fp8:
+            return self.dispatcher.dispatch(xs, idx, w, **kw)
+        kw.pop("timeline", None)
+        return self.dispatcher.dispatch_fp8(quantize_fp8(xs), idx, w, **kw)
+
     def _experts(self, res) -> Optional[torch.Tensor]:
         """GEMM1 (+GELU) and GEMM2 on the current stream.
 
         With ``fused_combine`` GEMM2's epilogue pushes each row straight to its
         source rank (DeepEPDispatcher.expert_gemm_push) and None is returned;
-        otherwise the expert-output rows are written locally and returned."""
+        otherwise the expert-output rows are written locally and returned.
+        An FP8 receive payload is first dequantised into the slot's expert-output
+        rows, which GEMM1 reads before GEMM2 overwrites them."""
         kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
-        grouped_gemm(res.recv_x, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
+        a = res.recv_x
+        if isinstance(a, tuple):
+            buf = self.dispatcher.expert_out_buffer(res.handle)
+            a = dequantize_fp8(a[0], a[1], out=buf[:a[0].shape[0]], rows=res.expert_offsets[-1:])
+        grouped_gemm(a, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
                      activation="gelu", **kw)
         if self.fused_combine:
             self.dispatcher.expert_gemm_push(self.h, self.w2.transpose(1, 2), res.handle, **kw)
@@ -234,9 +256,9 @@ class MoELayer:
         # the solo grid; the others run one block per SM beside the GEMMs.
         nv = self.enable_nvtx
         with nvtx_range("deepep_dispatch_chunk_0", nv):
-            cur = disp.dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
-                                w[chunks[0][0]:chunks[0][1]], pad_rows=False,
-                                num_sms=self.solo_comm_blocks)
+            cur = self._dispatch(x[chunks[0][0]:chunks[0][1]], idx[chunks[0][0]:chunks[0][1]],
+                                 w[chunks[0][0]:chunks[0][1]], pad_rows=False,
+                                 num_sms=self.solo_comm_blocks)
         self._timeline_mark(timeline, "dispatch0_end", disp.comm_stream)
         for i, (s, e) in enumerate(chunks):
             # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
@@ -253,7 +275,7 @@ class MoELayer:
             if i + 1 < len(chunks):
                 ns, ne = chunks[i + 1]
                 with nvtx_range(f"deepep_dispatch_chunk_{i + 1}", nv):
-                    nxt = disp.dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
+                    nxt = self._dispatch(x[ns:ne], idx[ns:ne], w[ns:ne], pad_rows=False)
                 self._timeline_mark(timeline, f"dispatch{i + 1}_end", disp.comm_stream)
             last = i + 1 == len(chunks)
             with nvtx_range(f"deepep_combine_chunk_{i}", nv):
@@ -304,7 +326,7 @@ class MoELayer:
             return r
 
         for s, e in chunks:
-            res = timed("dispatch_ms", lambda: disp.dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False))
+            res = timed("dispatch_ms", lambda: self._dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False))
             res.event.current_stream_wait()
             y = timed("experts_ms", lambda: self._experts(res))
             timed("combine_ms", lambda: self._combine(y, res.handle, out=out[s:e]))
@@ -336,8 +358,8 @@ class MoELayer:
         self._sync_all()
         if host_cover_cycles > 0:
             torch.cuda._sleep(int(host_cover_cycles))
-        res = disp.dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False,
-                            num_sms=self.solo_comm_blocks, timeline=marks_d)
+        res = self._dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False,
+                             num_sms=self.solo_comm_blocks, timeline=marks_d)
         res.event.current_stream_wait()
         y = self._experts(res)
         self._sync_all()

@@ -106,6 +106,30 @@ def dispatch(xs, topk_idxs, topk_weights, num_experts: int, expert_alignment: in
     return recv, send_pos
 
 
+def dispatch_fp8(xqs, scales, topk_idxs, topk_weights, num_experts: int):
+    """Dispatch of an FP8 payload (DeepEP's (x_fp8, x_scales) pair,
+    thirdParty/DeepEP/deep_ep/buffer.py:338-342): the same receive layout and
+    metadata as ``dispatch``, with each receive row holding its source token's
+    e4m3 bytes and per-128 scales unchanged (intranode.cu:397-402 copies the
+    scales next to the row).  ``recv[d]`` gains ``x_fp8`` [n, H] uint8 and
+    ``x_scales`` [n, H/128] float32 (zero on rows without a source).
+    """
+    zeros = [np.zeros((np.asarray(q).shape[0], 1), dtype=np.uint16) for q in xqs]
+    recv, send_pos = dispatch(zeros, topk_idxs, topk_weights, num_experts)
+    for d in recv:
+        n = d["src_rank"].shape[0]
+        h = np.asarray(xqs[0]).shape[1]
+        d["x_fp8"] = np.zeros((n, h), dtype=np.uint8)
+        d["x_scales"] = np.zeros((n, h // 128), dtype=np.float32)
+        for row in range(n):
+            r, t = int(d["src_rank"][row]), int(d["src_token"][row])
+            if r >= 0:
+                d["x_fp8"][row] = xqs[r][t]
+                d["x_scales"][row] = scales[r][t]
+        del d["x"]
+    return recv, send_pos
+
+
 def dispatch_cached(xs, topk_idxs, topk_weights, num_experts: int, src_recv, src_send_pos,
                     scale_rows: bool = False):
     """Cached re-dispatch (DeepEP's dispatch given a handle,
