@@ -121,6 +121,50 @@ __device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, in
   }
 }
 
+// The MMA issuer's k-block loop for one tile (leader CTA, one thread): waits for
+// each stage's data, issues its four 16-deep MMAs into the accumulator at d_tmem
+// and commits the stage back to both CTAs' producers.  SWAPPED issues the swapped
+// form (B stage as the MMA's A operand with M = 256, the A stage's first 64 rows
+// as its B operand with N = 128).  Returns false when a wait gave up.
+template <bool BF16, bool B_MN_MAJOR, bool SWAPPED>
+__device__ __forceinline__ bool issue_tile(Ctrl* ctrl, uint8_t* sA, uint8_t* sB, uint32_t d_tmem,
+                                           int num_kb, int& stage, uint32_t& phase,
+                                           const volatile int* abort_flag, bool& issued_any) {
+  constexpr uint32_t idesc = SWAPPED ? idesc_f16(BF16, BM, BM_CTA, B_MN_MAJOR, false)
+                                     : idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
+  for (int kb = 0; kb < num_kb; ++kb) {
+    if (!mbar_wait_cluster(smem_u32(&ctrl->full[stage]), phase, abort_flag)) return false;
+    tc_fence_after();
+    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+    const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+    // The descriptors of the four 16-deep steps differ only in the start address
+    // (bits 0-13, in 16-byte units): +32 bytes per step along a K-major row, +16
+    // rows of 128 bytes per step down an MN-major slab.  Stage buffers end well
+    // below 2^18 bytes, so the field never carries into the next one.
+    const uint64_t adesc0 = smem_desc_sw128(a_base, 16, 1024);
+    const uint64_t bdesc0 = B_MN_MAJOR ? smem_desc_sw128(b_base, B_SLAB_BYTES, 1024)
+                                       : smem_desc_sw128(b_base, 16, 1024);
+#pragma unroll
+    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+      const uint64_t adesc = adesc0 + uint64_t(kk * (UMMA_K * 2 / 16));
+      const uint64_t bdesc = bdesc0 + uint64_t(B_MN_MAJOR ? kk * (UMMA_K * 128 / 16) : kk * (UMMA_K * 2 / 16));
+      if constexpr (SWAPPED)
+        umma_f16_pair(d_tmem, bdesc, adesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+      else
+        umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+    }
+    issued_any = true;
+    const uint32_t e_local = smem_u32(&ctrl->empty[stage]);
+    umma_commit_pair(e_local);
+    umma_commit_pair(mapa_shared(e_local, 1));
+    if (++stage == STAGES) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+  return true;
+}
+
 // 144 registers: with 10 warps, SM sub-partitions 0 and 1 hold three of them
 // (3 x 32 x 144 = 13,824 of their 16,384 registers), which leaves room for one
 // warp per sub-partition of a 4-warp exchange block at <= 80 registers, so the
@@ -276,9 +320,6 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA (leader only) --
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
-      // swapped tile: weights as A (M = 256 columns), the tile's rows as B (N = 128)
-      constexpr uint32_t idesc_sw = idesc_f16(BF16, BM, BM_CTA, B_MN_MAJOR, false);
       int stage = 0;
       uint32_t phase = 0;
       int q = 0;
@@ -306,37 +347,13 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
         const bool swapped = p.swap_tails && s.y <= BM_CTA;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_cluster(smem_u32(&ctrl->full[stage]), phase, abort_flag)) {
-            failed = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint64_t adesc = smem_desc_sw128(a_base + kk * UMMA_K * 2, 16, 1024);
-            uint64_t bdesc;
-            if constexpr (B_MN_MAJOR) {
-              bdesc = smem_desc_sw128(b_base + kk * UMMA_K * 128, B_SLAB_BYTES, 1024);
-            } else {
-              bdesc = smem_desc_sw128(b_base + kk * UMMA_K * 2, 16, 1024);
-            }
-            if (swapped)
-              umma_f16_pair(d_tmem, bdesc, adesc, idesc_sw, (kb | kk) != 0 ? 1u : 0u);
-            else
-              umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
-          }
-          issued_any = true;
-          const uint32_t e_local = smem_u32(&ctrl->empty[stage]);
-          umma_commit_pair(e_local);
-          umma_commit_pair(mapa_shared(e_local, 1));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
+        // Two instantiations of the k-block loop, so that the usual tile's loop
+        // carries no per-MMA choice between the two operand arrangements.
+        const bool ok = swapped ? issue_tile<BF16, B_MN_MAJOR, true>(ctrl, sA, sB, d_tmem, num_kb, stage,
+                                                                   phase, abort_flag, issued_any)
+                                : issue_tile<BF16, B_MN_MAJOR, false>(ctrl, sA, sB, d_tmem, num_kb, stage,
+                                                                    phase, abort_flag, issued_any);
+        if (!ok) failed = true;
         if (failed) break;
         const uint32_t tf_local = smem_u32(&ctrl->tfull[acc]);
         umma_commit_pair(tf_local);
