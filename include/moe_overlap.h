@@ -256,6 +256,9 @@ typedef struct {
   int64_t* host_info;         /* mapped host [2]: {epoch, rows received} after scatter */
   int64_t cap_rows;
   int32_t max_topk;
+  uint32_t* arrived;          /* [num_experts/world] rows of each local expert landed in an
+                                 expert-ordered dispatch (peers add to it)            */
+  int32_t* expected;          /* [num_experts/world] rows of each local expert expected  */
 } moe_ep_views_t;
 
 /* Allocates this rank's endpoint: a symmetric buffer holding two slots of
@@ -355,6 +358,55 @@ MOE_API int32_t moe_fp8_quantize(const void* x, int64_t ldx, int64_t rows, int32
 MOE_API int32_t moe_fp8_dequantize(const void* x_fp8, int64_t ldx, const float* scales,
                                    int64_t ld_scales, const int32_t* rows_dev, int64_t rows_max,
                                    int32_t hidden, void* out, int64_t ld_out, void* stream);
+
+/*
+ * Expert-ordered dispatch, for a GEMM that starts an expert's tiles as soon as
+ * that expert's rows have landed instead of after the whole dispatch.  The same
+ * receive layout, metadata, offsets and send positions as moe_ep_dispatch
+ * (expert_alignment 1, bf16 rows, no scale_rows); the phases differ in:
+ *   ordered_begin    also records, for each of this rank's rows, the (token, slot)
+ *                    it carries, and clears this rank's arrival counters of the slot
+ *                    (before its count flag is raised, so no peer can add early);
+ *   ordered_scatter  every rank pushes its rows expert by expert (local expert
+ *                    index first, then owner), and after every few rows adds the
+ *                    number delivered to the owner's arrival counter of that
+ *                    expert; it also stores each local expert's expected row count;
+ *   end              moe_ep_dispatch_end (all rows landed), as before.
+ * moe_ep_dispatch_ordered runs the three.  No counterpart in DeepEP, whose
+ * receiver learns of rows only through its per-channel queues.
+ */
+MOE_API int32_t moe_ep_dispatch_ordered_begin(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                              const float* topk_weights, int32_t num_tokens,
+                                              int32_t topk, int32_t slot, uint64_t epoch,
+                                              int32_t* status, void* stream);
+MOE_API int32_t moe_ep_dispatch_ordered_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                                const float* topk_weights, int32_t num_tokens,
+                                                int32_t topk, int32_t slot, uint64_t epoch,
+                                                int32_t num_blocks, int32_t pad_rows,
+                                                uint64_t wait_ns, int32_t* status, void* stream);
+MOE_API int32_t moe_ep_dispatch_ordered(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                        const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                        int32_t slot, uint64_t epoch, int32_t num_blocks,
+                                        int32_t pad_rows, uint64_t wait_ns, int32_t* status,
+                                        void* stream);
+
+/*
+ * The grouped GEMM over the receive rows of an expert-ordered dispatch into
+ * `slot` (A = the slot's bf16 rows, K = hidden, offsets = its expert_offsets),
+ * C = act(A @ B[e]) with act none or GELU, as moe_grouped_gemm.  It may be
+ * enqueued as soon as this rank's ordered_scatter has been enqueued before it
+ * (this rank's expected counts and offsets come from that kernel): the GEMM's
+ * producer waits, per expert and bounded by wait_ns, until the expert's arrival
+ * counter reaches its expected count, so its tiles start while later experts'
+ * rows are still in flight.  An expired wait records MOE_ERR_TIMEOUT in
+ * `status` and the kernel returns.  Replaces, for this path, the grouped GEMM
+ * after a complete dispatch in src/train_moe_baseline.py:376-399.
+ */
+MOE_API int32_t moe_ep_expert_gemm(moe_ep_t ep, int32_t slot, const void* b, int64_t b_stride_e,
+                                   int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                                   int64_t n, int32_t activation, int32_t num_sms,
+                                   int32_t use_atomic_queue, int32_t* work_counter,
+                                   uint64_t wait_ns, int32_t* status, void* stream);
 
 /*
  * Cached re-dispatch (DeepEP's dispatch given a handle: deep_ep/buffer.py:383-390,

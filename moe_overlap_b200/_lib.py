@@ -134,6 +134,19 @@ SIGNATURES: dict[str, tuple] = {
     "moe_fp8_dequantize": (
         _i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i32, _c_void_p, _i64,
                _c_void_p]),
+    "moe_ep_dispatch_ordered_begin": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _c_void_p,
+               _c_void_p]),
+    "moe_ep_dispatch_ordered_scatter": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
+               _u64, _c_void_p, _c_void_p]),
+    "moe_ep_dispatch_ordered": (
+        _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _u64, _i32, _i32,
+               _u64, _c_void_p, _c_void_p]),
+    "moe_ep_expert_gemm": (
+        _i32, [_c_void_p, _i32, _c_void_p, _i64, _i64, _i64,  # ep, slot, b, strides e/k/n
+               _c_void_p, _i64, _i64, _i32, _i32, _i32, _c_void_p,  # c, ldc, n, act, sms, atomic, ctr
+               _u64, _c_void_p, _c_void_p]),  # wait_ns, status, stream
     "moe_ep_dispatch_cached_begin": (_i32, [_c_void_p, _i32, _u64, _c_void_p]),
     "moe_ep_dispatch_cached_scatter": (
         _i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _u64, _i32,

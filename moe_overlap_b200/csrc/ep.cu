@@ -97,6 +97,8 @@ struct SymLayout {
   uint64_t count_flag;  // [2][world] uint64
   uint64_t data_flag;   // [2][world] uint64
   uint64_t ready_flag;  // [2][world] uint64
+  uint64_t arrived;     // [2][num_experts / world] uint32: rows of each local expert that
+                        // have landed here in an expert-ordered dispatch (peers add to it)
   uint64_t bytes;
 };
 
@@ -116,6 +118,8 @@ struct Endpoint {
   CUtensorMap* d_cb_maps = nullptr; // [2][world] TMA store maps of every rank's cb (per slot)
   int32_t* offsets[2] = {};         // [per_rank+1] receiver expert offsets
   int32_t* my_counts = nullptr;     // [E]
+  int32_t* order = nullptr;         // [max_tokens*max_topk] assignment of each cb row
+  int32_t* expected[2] = {};        // [per_rank] rows of each local expert (before alignment)
   unsigned int* done_ctr = nullptr; // blocks finished in the current scatter
   uint64_t* epoch_ctr = nullptr;    // device-side epoch counter (epoch 0 = use it)
   uint64_t* slot_epoch = nullptr;   // [2] epoch the last dispatch into each slot drew
@@ -150,6 +154,9 @@ struct Params {
   int32_t* cb_pos;
   int32_t* offsets_out;
   int32_t* my_counts;
+  int32_t* order;        // expert-ordered dispatch: assignment of each of this rank's cb rows
+  int32_t* expected_out; // expert-ordered dispatch: rows of each local expert, for the GEMM
+  int ordered;           // count phase: also build `order` and clear the arrival counters
   unsigned int* done_ctr;
   uint64_t* epoch_ctr;
   uint64_t* slot_epoch;
@@ -275,6 +282,31 @@ __global__ void count_kernel(Params p) {
     p.my_counts[e] = run;
   }
   __syncthreads();
+  if (p.ordered) {
+    // Expert-ordered dispatch: the assignment behind each of this rank's cb rows
+    // (global expert order, then (token, slot) order), so that the scatter can walk
+    // the rows expert by expert; and this rank's arrival counters for the slot start
+    // again from zero, before any peer can see the count flag raised below.
+    __shared__ int base_sh[kMaxExperts];
+    if (threadIdx.x == 0) {
+      int run = 0;
+      for (int e = 0; e < E; ++e) {
+        base_sh[e] = run;
+        run += p.my_counts[e];
+      }
+    }
+    uint32_t* arrived = at<uint32_t>(p.peers[p.rank], p.lay.arrived) + p.slot * p.per_rank;
+    for (int le = threadIdx.x; le < p.per_rank; le += blockDim.x) arrived[le] = 0;
+    __syncthreads();
+    const int total = p.num_tokens * p.topk;
+    for (int a = threadIdx.x; a < total; a += blockDim.x) {
+      const int64_t v = p.topk_idx[a];
+      if (v < 0 || v >= E) continue;
+      const int e = static_cast<int>(v);
+      const int blk = a / kAssignPerLayoutBlock;
+      p.order[base_sh[e] + p.block_hist[blk * E + e] + p.rank_in_block[a]] = a;
+    }
+  }
   for (int d = 0; d < p.world; ++d) {
     int32_t* dst = at<int32_t>(p.peers[d], slot_of(p).counts) + p.rank * E;
     for (int e = threadIdx.x; e < E; e += blockDim.x) dst[e] = p.my_counts[e];
@@ -504,6 +536,172 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
       p.send_pos[a] = -1;
   }
 
+  // Last block to finish tells every rank that this rank's rows have landed.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(p.done_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < p.world; ++d)
+        st_release_sys(at<uint64_t>(p.peers[d], p.lay.data_flag) + p.slot * p.world + p.rank,
+                       kernel_epoch(p));
+    }
+  }
+}
+
+// ------------------------------------------------------ expert-ordered scatter --
+// The same rows, receive layout and metadata as scatter_kernel, pushed expert by
+// expert so that an owner can start multiplying an expert's rows as soon as they
+// have all landed, while later experts are still in flight.  Each rank walks its
+// rows (the cb order: global expert, then (token, slot)) with its experts visited
+// in (local expert, owner) order, so every owner's first expert goes first.  A
+// warp copies R consecutive rows, then fences and adds, per expert among them,
+// the number of rows it delivered to the owner's arrival counter of that local
+// expert (a system-scope atomic over NVLink).  The owner's GEMM waits until a
+// counter reaches that expert's row count (moe_ep_expert_gemm).
+constexpr int kOrderedRowsPerWarp = 4;
+
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_kernel(Params p) {
+  __shared__ CountView cv;
+  __shared__ int vbase[kMaxExperts + 1];  // first walk position of each (local expert, owner) segment
+  __shared__ int vexp[kMaxExperts];       // global expert of each segment
+  if (threadIdx.x == 0) {
+    cv.overflow = 0;
+    cv.fail = 0;
+    cv.recv_total = 0;
+  }
+  __syncthreads();
+  if (!wait_all_flags(p, p.lay.count_flag, &cv.fail)) {
+    if (threadIdx.x == 0) record_status(p.status, MOE_ERR_TIMEOUT);
+    return;
+  }
+  build_count_view(p, cv);
+  const int E = p.num_experts;
+  if (threadIdx.x == 0) {
+    const int32_t* mine = at<const int32_t>(p.peers[p.rank], slot_of(p).counts) + p.rank * E;
+    int run = 0, seg = 0;
+    for (int le = 0; le < p.per_rank; ++le)
+      for (int d = 0; d < p.world; ++d, ++seg) {
+        const int e = d * p.per_rank + le;
+        vbase[seg] = run;
+        vexp[seg] = e;
+        run += mine[e];
+      }
+    vbase[E] = run;
+  }
+  __syncthreads();
+  const bool overflow = cv.overflow != 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && overflow) record_status(p.status, MOE_ERR_CAPACITY);
+  if (blockIdx.x == 0) {
+    for (int le = threadIdx.x; le <= p.per_rank; le += blockDim.x) {
+      const int e = p.rank * p.per_rank + le;
+      p.offsets_out[le] = overflow ? 0 : (le < p.per_rank ? cv.exp_base[e] : cv.recv_total);
+      if (le < p.per_rank) p.expected_out[le] = overflow ? 0 : cv.exp_count[e];
+    }
+    if (threadIdx.x == 0 && p.host_info != nullptr) {
+      volatile int64_t* hi = p.host_info + 2 * p.slot;
+      hi[1] = overflow ? -1 : cv.recv_total;
+      __threadfence_system();
+      hi[0] = static_cast<int64_t>(kernel_epoch(p));
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (kCommThreads / 32);
+  const int nvec = p.hidden / 8;
+  const SlotLayout sl = slot_of(p);
+  const int total_rows = vbase[E];
+  if (!overflow) {
+    for (int c = blockIdx.x * (kCommThreads / 32) + warp; c * kOrderedRowsPerWarp < total_rows;
+         c += warps_total) {
+      const int v0 = c * kOrderedRowsPerWarp;
+      const int v1 = min(v0 + kOrderedRowsPerWarp, total_rows);
+      int seg = 0;
+      for (int lo = 0, hi = E; hi - lo > 1;) {  // vbase[seg] <= v0 < vbase[seg + 1]
+        const int mid = (lo + hi) >> 1;
+        if (vbase[mid] <= v0) lo = mid; else hi = mid;
+        seg = lo;
+      }
+      int run_seg = -1, run_n = 0;
+      for (int v = v0; v <= v1; ++v) {
+        if (v < v1)
+          while (vbase[seg + 1] <= v) ++seg;  // empty segments are skipped
+        // Close the run of rows of one expert before a new expert (or the end).
+        if (run_n > 0 && (v == v1 || seg != run_seg)) {
+          __threadfence_system();
+          __syncwarp();
+          if (lane == 0) {
+            const int e = vexp[run_seg];
+            const int d = e / p.per_rank;
+            __threadfence_system();
+            atomicAdd_system(at<unsigned int>(p.peers[d], p.lay.arrived) + p.slot * p.per_rank +
+                                 (e - d * p.per_rank),
+                             static_cast<unsigned int>(run_n));
+          }
+          run_n = 0;
+        }
+        if (v == v1) break;
+        const int e = vexp[seg];
+        const int off = v - vbase[seg];
+        const int cb_row = cv.my_base[e] + off;
+        const int a = p.order[cb_row];
+        const int t = a / p.topk, j = a - t * p.topk;
+        const int d = e / p.per_rank;
+        const int row = cv.exp_base[e] + cv.my_prefix[e] + off;
+        uint8_t* peer = p.peers[d];
+        if (lane < p.topk) {
+          at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
+              (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
+          at<float>(peer, sl.topk_w)[static_cast<int64_t>(row) * p.max_topk + lane] =
+              (lane == j) ? p.topk_w[a] : 0.0f;
+        }
+        if (lane == 0) {
+          at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
+          at<int32_t>(peer, sl.dst)[row] = cb_row;
+          p.send_pos[a] = row;
+          p.cb_pos[a] = cb_row;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
+        uint4* dst = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+        constexpr int U = 4;
+        for (int base = 0; base < nvec; base += 32 * U) {
+          uint4 vv[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int i = base + u * 32 + lane;
+            if (i < nvec) vv[u] = __ldg(src + i);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int i = base + u * 32 + lane;
+            if (i < nvec) dst[i] = vv[u];
+          }
+        }
+        if (run_n == 0) run_seg = seg;
+        ++run_n;
+      }
+    }
+    // (token, slot) pairs with no expert: no receive row.
+    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < p.num_tokens * p.topk;
+         a += gridDim.x * blockDim.x) {
+      const int64_t ev = p.topk_idx[a];
+      if (ev < 0 || ev >= E) p.send_pos[a] = -1;
+    }
+    if (p.pad_rows) {
+      uint8_t* me = p.peers[p.rank];
+      const int64_t first = cv.recv_total;
+      const int64_t n = (p.cap_rows - first) * p.max_topk;
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+           i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        at<int64_t>(me, sl.topk_idx)[first * p.max_topk + i] = -1;
+        at<float>(me, sl.topk_w)[first * p.max_topk + i] = 0.0f;
+      }
+    }
+  } else {
+    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < p.num_tokens * p.topk;
+         a += gridDim.x * blockDim.x)
+      p.send_pos[a] = -1;
+  }
   // Last block to finish tells every rank that this rank's rows have landed.
   __threadfence_system();
   __syncthreads();
@@ -852,6 +1050,8 @@ static SymLayout plan(int world, int num_experts, int hidden, int max_topk, int6
   off = align_up(off + 2ull * world * 8, 256);
   L.ready_flag = off;
   off = align_up(off + 2ull * world * 8, 256);
+  L.arrived = off;
+  off = align_up(off + 2ull * (num_experts / world) * 4, 256);
   L.bytes = off;
   return L;
 }
@@ -933,6 +1133,13 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   }
   const uint64_t o_cnt = off;
   off = align_up(off + uint64_t(num_experts) * 4, 256);
+  const uint64_t o_order = off;
+  off = align_up(off + uint64_t(assigns) * 4, 256);
+  uint64_t o_expected[2];
+  for (int s = 0; s < 2; ++s) {
+    o_expected[s] = off;
+    off = align_up(off + uint64_t(ep->per_rank) * 4, 256);
+  }
   const uint64_t o_done = off;
   off = align_up(off + 256, 256);
   const uint64_t o_maps = off;
@@ -966,6 +1173,8 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
     ep->offsets[s] = reinterpret_cast<int32_t*>(ep->scratch + o_offs[s]);
   }
   ep->my_counts = reinterpret_cast<int32_t*>(ep->scratch + o_cnt);
+  ep->order = reinterpret_cast<int32_t*>(ep->scratch + o_order);
+  for (int s = 0; s < 2; ++s) ep->expected[s] = reinterpret_cast<int32_t*>(ep->scratch + o_expected[s]);
   ep->done_ctr = reinterpret_cast<unsigned int*>(ep->scratch + o_done);
   ep->epoch_ctr = reinterpret_cast<uint64_t*>(ep->scratch + o_done + 8);
   ep->slot_epoch = reinterpret_cast<uint64_t*>(ep->scratch + o_done + 16);
@@ -1049,13 +1258,15 @@ extern "C" int32_t moe_ep_views(moe_ep_t ep, int32_t slot, moe_ep_views_t* v) {
   v->host_info = ep->host_info + 2 * slot;
   v->cap_rows = ep->cap_rows;
   v->max_topk = ep->max_topk;
+  v->arrived = reinterpret_cast<uint32_t*>(ep->sym + ep->lay.arrived) + slot * ep->per_rank;
+  v->expected = ep->expected[slot];
   return MOE_OK;
 }
 
-extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64_t* topk_idx,
-                                         const float* topk_weights, int32_t num_tokens,
-                                         int32_t topk, int32_t slot, uint64_t epoch,
-                                         int32_t* status, void* stream_) {
+static int32_t dispatch_begin_impl(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                   const float* topk_weights, int32_t num_tokens, int32_t topk,
+                                   int32_t slot, uint64_t epoch, int32_t* status, void* stream_,
+                                   bool ordered) {
   using namespace moe::ep;
   if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 ||
       num_tokens > ep->max_tokens || topk < 1 || topk > ep->max_topk ||
@@ -1072,6 +1283,8 @@ extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64
   p.block_hist = ep->block_hist;
   p.rank_in_block = ep->rank_in_block;
   p.my_counts = ep->my_counts;
+  p.order = ep->order;
+  p.ordered = ordered ? 1 : 0;
   const int64_t assigns = int64_t(num_tokens) * topk;
   p.num_layout_blocks = static_cast<int>((assigns + kAssignPerLayoutBlock - 1) / kAssignPerLayoutBlock);
   if (p.num_layout_blocks > 0) {
@@ -1079,6 +1292,55 @@ extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64
     if (int rc = check_launch(); rc != MOE_OK) return rc;
   }
   count_kernel<<<1, 256, 0, stream>>>(p);
+  return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_begin(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                         const float* topk_weights, int32_t num_tokens,
+                                         int32_t topk, int32_t slot, uint64_t epoch,
+                                         int32_t* status, void* stream) {
+  return dispatch_begin_impl(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch, status,
+                             stream, false);
+}
+
+extern "C" int32_t moe_ep_dispatch_ordered_begin(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                                 const float* topk_weights, int32_t num_tokens,
+                                                 int32_t topk, int32_t slot, uint64_t epoch,
+                                                 int32_t* status, void* stream) {
+  return dispatch_begin_impl(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch, status,
+                             stream, true);
+}
+
+extern "C" int32_t moe_ep_dispatch_ordered_scatter(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                                   const float* topk_weights, int32_t num_tokens,
+                                                   int32_t topk, int32_t slot, uint64_t epoch,
+                                                   int32_t num_blocks, int32_t pad_rows,
+                                                   uint64_t wait_ns, int32_t* status, void* stream_) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 || num_tokens < 0 || num_tokens > ep->max_tokens ||
+      topk < 1 || topk > ep->max_topk || num_blocks < 1 ||
+      (num_tokens > 0 && (x == nullptr || topk_idx == nullptr || topk_weights == nullptr)) ||
+      !moe::aligned16(x))
+    return MOE_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  Params p = base_params(ep, slot, epoch, wait_ns, status);
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.topk_idx = topk_idx;
+  p.topk_w = topk_weights;
+  p.num_tokens = num_tokens;
+  p.topk = topk;
+  p.send_pos = ep->send_pos[slot];
+  p.cb_pos = ep->cb_pos[slot];
+  p.offsets_out = ep->offsets[slot];
+  p.expected_out = ep->expected[slot];
+  p.order = ep->order;
+  p.done_ctr = ep->done_ctr;
+  p.pad_rows = pad_rows ? 1 : 0;
+  p.align = 1;
+  p.host_info = ep->host_info;
+  if (cudaMemsetAsync(ep->done_ctr, 0, sizeof(unsigned int), stream) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  scatter_ordered_kernel<<<num_blocks, kCommThreads, 0, stream>>>(p);
   return check_launch();
 }
 
@@ -1299,6 +1561,43 @@ extern "C" int32_t moe_ep_push_gemm(moe_ep_t ep, const void* a, int64_t lda, con
   Params p = base_params(ep, slot, epoch, 0, nullptr);
   ready_kernel<<<1, 64, 0, stream>>>(p);
   return check_launch();
+}
+
+extern "C" int32_t moe_ep_dispatch_ordered(moe_ep_t ep, const void* x, const int64_t* topk_idx,
+                                           const float* topk_weights, int32_t num_tokens,
+                                           int32_t topk, int32_t slot, uint64_t epoch,
+                                           int32_t num_blocks, int32_t pad_rows, uint64_t wait_ns,
+                                           int32_t* status, void* stream) {
+  // Checked before the begin phase raises this rank's count flag (see moe_ep_dispatch).
+  if (num_blocks < 1) return MOE_ERR_INVALID_ARG;
+  int rc = moe_ep_dispatch_ordered_begin(ep, x, topk_idx, topk_weights, num_tokens, topk, slot,
+                                         epoch, status, stream);
+  if (rc == MOE_OK)
+    rc = moe_ep_dispatch_ordered_scatter(ep, x, topk_idx, topk_weights, num_tokens, topk, slot, epoch,
+                                         num_blocks, pad_rows, wait_ns, status, stream);
+  if (rc == MOE_OK) rc = moe_ep_dispatch_end(ep, slot, epoch, wait_ns, status, stream);
+  return rc;
+}
+
+extern "C" int32_t moe_ep_expert_gemm(moe_ep_t ep, int32_t slot, const void* b, int64_t b_stride_e,
+                                      int64_t b_stride_k, int64_t b_stride_n, void* c, int64_t ldc,
+                                      int64_t n, int32_t activation, int32_t num_sms,
+                                      int32_t use_atomic_queue, int32_t* work_counter,
+                                      uint64_t wait_ns, int32_t* status, void* stream) {
+  using namespace moe::ep;
+  if (ep == nullptr || slot < 0 || slot > 1 ||
+      (activation != MOE_ACT_NONE && activation != MOE_ACT_GELU))
+    return MOE_ERR_INVALID_ARG;
+  const SymLayout& L = ep->lay;
+  moe::gg::ArrivalWait arrival;
+  arrival.arrived = reinterpret_cast<const uint32_t*>(ep->sym + L.arrived) + slot * ep->per_rank;
+  arrival.expected = ep->expected[slot];
+  arrival.wait_ns = wait_ns;
+  return moe::gg::grouped_gemm_launch(
+      ep->sym + L.slot[slot].recv_x, ep->hidden, b, b_stride_e, b_stride_k, b_stride_n, c, ldc,
+      ep->offsets[slot], 0, ep->cap_rows, ep->hidden, n, ep->per_rank, MOE_DTYPE_BF16, activation,
+      num_sms, use_atomic_queue, work_counter, nullptr, nullptr, nullptr, 0, status,
+      static_cast<cudaStream_t>(stream), nullptr, &arrival);
 }
 
 extern "C" int32_t moe_ep_dispatch_layout(const int64_t* topk_idx, int32_t num_tokens,

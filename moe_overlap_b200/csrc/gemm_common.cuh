@@ -26,6 +26,14 @@ struct PushTarget {
   const CUtensorMap* maps; // [world] TMA store maps of each rank's combine rows, or null
 };
 
+// Expert-ordered dispatch: the rows of local expert e are all present once
+// arrived[e] >= expected[e] (peers add to arrived[e] as their rows land).
+struct ArrivalWait {
+  const uint32_t* arrived;  // [num_experts] arrival counters (this GPU's memory)
+  const int32_t* expected;  // [num_experts] rows of each expert
+  uint64_t wait_ns;         // bound on each wait
+};
+
 struct Params {
   void* c;
   int64_t ldc;
@@ -48,7 +56,26 @@ struct Params {
   int c_tma;               // the CTA-pair kernel may store C through its TMA store map
   int swap_tails;          // the CTA-pair kernel computes tiles of <= 128 rows swapped
   PushTarget push;         // combine push instead of C (push.src != null)
+  ArrivalWait arrival;     // arrival.arrived != null: wait for each expert's rows
 };
+
+// Producer side of an expert-ordered dispatch: returns once every row of `expert`
+// has landed (then visible to the TMA loads that follow), or false after
+// p.arrival.wait_ns.  Without arrival counters it returns at once.
+__device__ __forceinline__ bool wait_expert_rows(const Params& p, int expert) {
+  if (p.arrival.arrived == nullptr) return true;
+  const uint32_t need = static_cast<uint32_t>(max(0, p.arrival.expected[expert]));
+  const uint32_t* ctr = p.arrival.arrived + expert;
+  if (ld_acquire_sys_u32(ctr) < need) {
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_sys_u32(ctr) < need) {
+      if (global_timer_ns() - t0 > p.arrival.wait_ns) return false;
+      __nanosleep(64);
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
 
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
@@ -284,7 +311,7 @@ int grouped_gemm_launch(const void* a, int64_t lda, const void* b, int64_t b_str
                         int32_t activation, int32_t num_sms, int32_t use_atomic_queue,
                         int32_t* work_counter, const float* row_scale, const void* aux_in,
                         void* aux_out, int64_t ld_aux, int32_t* status, cudaStream_t stream,
-                        const PushTarget* push);
+                        const PushTarget* push, const ArrivalWait* arrival = nullptr);
 
 // Launches the 2-SM (CTA pair) kernel; grid must be even.  `tc` is the 2-D {N, m_total}
 // store map of C (32x32 boxes, 64-byte swizzle), used when p.c_tma is set.

@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int q = 0;
       uint32_t qphase = 0;
       int issued[STAGES] = {0, 0, 0, 0};
+      int ready_expert = -1;  // rows of this expert are known to have landed
       bool failed = false;
       for (int iter = 0;; ++iter) {
         const int t = p.use_atomic ? atomicAdd(p.work_counter, 1)
@@ -161,6 +162,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (++q == QDEPTH) {
           q = 0;
           qphase ^= 1;
+        }
+        if (tc.expert != ready_expert) {
+          if (!wait_expert_rows(p, tc.expert)) {
+            failed = true;
+            break;
+          }
+          ready_expert = tc.expert;
         }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(&ctrl->empty[stage]), phase ^ 1, abort_flag)) {
@@ -397,7 +405,7 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
                                  int32_t activation, int32_t num_sms, int32_t use_atomic_queue,
                                  int32_t* work_counter, const float* row_scale, const void* aux_in,
                                  void* aux_out, int64_t ld_aux, int32_t* status, cudaStream_t stream,
-                                 const PushTarget* push) {
+                                 const PushTarget* push, const ArrivalWait* arrival) {
   using namespace moe::gg;
   const bool pushing = push != nullptr && push->src != nullptr;
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_F16) return MOE_ERR_INVALID_ARG;
@@ -494,6 +502,7 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
   p.aux_out = aux_out;
   p.ld_aux = ld_aux;
   p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0, nullptr};
+  p.arrival = arrival != nullptr ? *arrival : ArrivalWait{nullptr, nullptr, 0};
   // Tiles of at most 128 rows (an expert's tail) run swapped on the CTA pair when
   // the epilogue is elementwise on the product alone (no row scale, auxiliary
   // operands or combine push).

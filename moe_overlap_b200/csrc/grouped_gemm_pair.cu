@@ -243,6 +243,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
       uint32_t phase = 0;
       int q = 0;
       uint32_t qphase = 0;
+      int ready_expert = -1;
       bool failed = false;
       const int pair_id = static_cast<int>(cluster_id_x());
       const int npairs = static_cast<int>(nclusters_x());
@@ -278,6 +279,13 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
           qphase ^= 1;
         }
         if (s.z < 0) break;
+        if (s.w != ready_expert) {  // expert-ordered dispatch: this expert's rows have landed
+          if (!wait_expert_rows(p, s.w)) {
+            failed = true;
+            break;
+          }
+          ready_expert = s.w;
+        }
         // A swapped tile takes 64 rows from each CTA (the MMA's N side); the box
         // still loads 128, of which the MMA reads the first 64.
         const bool swapped = p.swap_tails && s.y <= BM_CTA;

@@ -339,6 +339,25 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool is_bf16, int m, int n, boo
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// ------------------------------------------------- cross-GPU flag reads --
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's earlier generic-proxy accesses (e.g. an acquire of rows
+// another GPU wrote) before its later async-proxy ones (TMA loads of those rows).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ----------------------------------------------------------- status word --
 // Records the first device-side error into the caller's status word (device
 // memory or mapped pinned host memory); plain volatile store so it also works

@@ -71,6 +71,7 @@ class DispatchHandle:
     combined: bool = False
     stream: Optional[torch.cuda.Stream] = None  # where the dispatch ran, and its end
     event: Optional[torch.cuda.Event] = None
+    ordered: bool = False  # expert-ordered: expert_gemm may start before every row landed
 
 
 @dataclass
@@ -221,8 +222,15 @@ class DeepEPDispatcher:
                  exact_size: Optional[bool] = None, expert_alignment: int = 1,
                  scale_rows: bool = False, num_sms: Optional[int] = None,
                  pad_rows: Optional[bool] = None, inline: bool = False,
-                 timeline: Optional[list] = None) -> DispatchResult:
+                 timeline: Optional[list] = None, ordered: bool = False) -> DispatchResult:
         """Sends each token's row to the ranks owning its top-k experts.
+
+        With ``ordered`` the rows travel expert by expert and each owner counts,
+        per local expert, the rows that have landed; ``extra["scatter_event"]`` of
+        the result marks the end of this rank's sending, and ``expert_gemm`` enqueued
+        behind it starts each expert's tiles as soon as that expert's rows are all
+        here (``event`` still marks every row landed).  Same rows, layout and
+        metadata as the default; bf16 rows without ``expert_alignment``/``scale_rows``.
 
         ``timeline`` (a list) receives (phase, CUDA event) pairs recorded on the
         exchange stream: ``start``, then one after each of the dispatch's three
@@ -262,6 +270,8 @@ class DeepEPDispatcher:
             raise RuntimeError("at most two dispatches may be outstanding; combine the oldest first")
         if not 1 <= int(expert_alignment) <= 4096:
             raise ValueError("expert_alignment must be in [1, 4096]")
+        if ordered and (int(expert_alignment) != 1 or scale_rows):
+            raise ValueError("an ordered dispatch takes neither expert_alignment nor scale_rows")
         if num_sms is not None and int(num_sms) < 1:
             raise ValueError("num_sms must be at least 1")
         exact = self.exact_size if exact_size is None else exact_size
@@ -282,7 +292,23 @@ class DeepEPDispatcher:
             # views read like DeepEP's.  Callers that use expert_offsets can skip it.
             pad = (not exact) if pad_rows is None else bool(pad_rows)
             kepoch, blocks = 0 if self._device_epochs else epoch, num_sms or self.num_sms
-            if timeline is None:
+            scatter_event = None
+            if ordered:
+                if timeline is not None:
+                    _mark(timeline, "start", stream)
+                self._ep.dispatch_ordered_begin(xc, ic, wc, slot, kepoch, self._status)
+                if timeline is not None:
+                    _mark(timeline, "layout_count", stream)
+                self._ep.dispatch_ordered_scatter(xc, ic, wc, slot, kepoch, blocks, pad, self.wait_ns,
+                                                  self._status)
+                scatter_event = torch.cuda.Event()
+                scatter_event.record(stream)
+                if timeline is not None:
+                    _mark(timeline, "scatter", stream)
+                self._ep.dispatch_end(slot, kepoch, self.wait_ns, self._status)
+                if timeline is not None:
+                    _mark(timeline, "wait", stream)
+            elif timeline is None:
                 self._ep.dispatch(xc, ic, wc, slot, kepoch, blocks, pad, self.wait_ns,
                                   self._status, expert_alignment, scale_rows)
             else:  # the same three launches, with an event before and after each
@@ -303,7 +329,7 @@ class DeepEPDispatcher:
         views = self._ep.slots[slot]
         rows = self._ep.received_rows(slot, epoch) if exact else views.recv_x.shape[0]
         handle = DispatchHandle(slot, epoch, num_tokens, topk, ic, wc, xc, rows if exact else None,
-                                stream=stream, event=event)
+                                stream=stream, event=event, ordered=ordered)
         self._outstanding.append(handle)
         kcols = views.recv_topk_idx.stride(0)
         return DispatchResult(
@@ -314,7 +340,43 @@ class DeepEPDispatcher:
             event=EventOverlap(event),
             expert_offsets=offs,
             recv_src=views.recv_src[:rows],
+            extra={"scatter_event": EventOverlap(scatter_event)} if ordered else {},
         )
+
+    def expert_gemm(self, handle: DispatchHandle, weight: torch.Tensor, out: torch.Tensor, *,
+                    activation: Optional[str] = None, num_sms: Optional[int] = None,
+                    use_atomic_queue: bool = True,
+                    work_counter: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``out = act(recv_x @ weight[e])`` over an ordered dispatch's receive rows, on
+        the caller's stream, each expert's tiles starting once its rows have landed.
+
+        Enqueue it behind the dispatch's ``extra["scatter_event"]`` (this rank's own
+        rows and expected counts are then in place); the kernel itself waits for
+        the peers' rows, expert by expert.  ``weight`` is ``[E_local, hidden, N]``
+        (strided views such as ``w1.transpose(1, 2)`` accepted) and ``out`` has one
+        row per receive row (``[max_recv_rows, N]``); ``activation`` None or "gelu".
+        """
+        if not isinstance(handle, DispatchHandle) or not handle.ordered:
+            raise RuntimeError("expert_gemm needs the handle of an ordered dispatch")
+        self._check_slot_live(handle)
+        self._require_on_device(weight=weight, out=out, work_counter=work_counter)
+        if weight.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+            raise ValueError("expert_gemm expects bf16 weights and output")
+        if weight.dim() != 3 or weight.shape[0] != self.experts_per_rank or \
+                weight.shape[1] != self.hidden_size:
+            raise ValueError(f"weight must be [{self.experts_per_rank}, {self.hidden_size}, N]")
+        n = weight.shape[2]
+        if out.dim() != 2 or out.shape[1] != n or out.shape[0] < self.max_recv_rows or \
+                out.stride(1) != 1 or out.stride(0) % 8 != 0 or out.data_ptr() % 16 != 0:
+            raise ValueError(f"out must be a bf16 [>= {self.max_recv_rows}, {n}] tensor with "
+                             "16-byte aligned rows")
+        _lib.check_status(self.device)
+        if use_atomic_queue and work_counter is None:
+            work_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        sms = num_sms or torch.cuda.get_device_properties(self.device).multi_processor_count
+        self._ep.expert_gemm(handle.slot, weight, out, activation, sms, use_atomic_queue,
+                             work_counter, self.wait_ns, self._status)
+        return out
 
     def dispatch_fp8(self, x: Tuple[torch.Tensor, torch.Tensor], topk_idx: torch.Tensor,
                      topk_weights: torch.Tensor, previous_event: Optional[object] = None, *,

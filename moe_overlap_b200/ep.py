@@ -49,6 +49,8 @@ class _Views(ctypes.Structure):
         ("host_info", ctypes.c_void_p),
         ("cap_rows", ctypes.c_int64),
         ("max_topk", ctypes.c_int32),
+        ("arrived", ctypes.c_void_p),
+        ("expected", ctypes.c_void_p),
     ]
 
 
@@ -67,6 +69,8 @@ class SlotViews:
     expert_offsets: torch.Tensor   # [E_local + 1] int32
     send_pos: torch.Tensor         # [max_tokens * max_topk] int32
     host_info: ctypes.Array        # mapped host {epoch, rows}
+    arrived: torch.Tensor | None = None   # [E_local] int32 view: rows landed per local expert
+    expected: torch.Tensor | None = None  # [E_local] int32: rows expected per local expert
     # FP8 payload of a moe_ep_dispatch_fp8, in the same bytes as recv_x (H % 128 == 0)
     recv_fp8: torch.Tensor | None = None     # [cap, H] float8_e4m3fn
     recv_scales: torch.Tensor | None = None  # [cap, H/128] float32
@@ -112,6 +116,8 @@ class Endpoint:
             fp8_scales = area[cap * h:cap * h + cap * (h // 128) * 4].view(torch.float32) \
                 .view(cap, h // 128)
         return SlotViews(
+            arrived=raw(v.arrived, self.experts_per_rank * 4).view(torch.int32),
+            expected=raw(v.expected, self.experts_per_rank * 4).view(torch.int32),
             recv_fp8=fp8_rows,
             recv_scales=fp8_scales,
             recv_x=raw(v.recv_x, cap * h * 2).view(torch.bfloat16).view(cap, h),
@@ -249,6 +255,42 @@ class Endpoint:
                                      self._stream()),
             "moe_ep_dispatch")
 
+    def dispatch_ordered_begin(self, x, topk_idx, topk_w, slot, epoch, status):
+        """Begin phase of an expert-ordered dispatch (moe_ep_dispatch_ordered_begin)."""
+        self._on_device(x, topk_idx, topk_w)
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_ordered_begin(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                                   topk_w.data_ptr(), t, k, slot, epoch,
+                                                   status.data_ptr(), self._stream()),
+            "moe_ep_dispatch_ordered_begin")
+
+    def dispatch_ordered_scatter(self, x, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows,
+                                 wait_ns, status):
+        """Scatter phase of an expert-ordered dispatch (moe_ep_dispatch_ordered_scatter)."""
+        self._on_device(x, topk_idx, topk_w)
+        t, k = topk_idx.shape
+        _lib.check_call(
+            self.lib.moe_ep_dispatch_ordered_scatter(self.handle, x.data_ptr(), topk_idx.data_ptr(),
+                                                     topk_w.data_ptr(), t, k, slot, epoch,
+                                                     num_blocks, 1 if pad_rows else 0, wait_ns,
+                                                     status.data_ptr(), self._stream()),
+            "moe_ep_dispatch_ordered_scatter")
+
+    def expert_gemm(self, slot, b, out, activation, num_sms, use_atomic, work_counter, wait_ns,
+                    status) -> None:
+        """GEMM over ``slot``'s receive rows that starts each expert once its rows have
+        landed (moe_ep_expert_gemm); ``b`` [E_local, hidden, N], ``out`` [cap, N]."""
+        self._on_device(b, out, work_counter)
+        act = {None: _lib.MOE_ACT_NONE, "none": _lib.MOE_ACT_NONE, "gelu": _lib.MOE_ACT_GELU}[activation]
+        _lib.check_call(
+            self.lib.moe_ep_expert_gemm(self.handle, slot, b.data_ptr(), b.stride(0), b.stride(1),
+                                        b.stride(2), out.data_ptr(), out.stride(0), out.shape[1], act,
+                                        int(num_sms), 1 if use_atomic else 0,
+                                        work_counter.data_ptr() if work_counter is not None else None,
+                                        wait_ns, status.data_ptr(), self._stream()),
+            "moe_ep_expert_gemm")
+
     def dispatch_fp8(self, x_fp8, x_scales, topk_idx, topk_w, slot, epoch, num_blocks, pad_rows,
                      wait_ns, status):
         """Dispatch of an e4m3 payload with its per-128 scales (moe_ep_dispatch_fp8)."""
@@ -377,6 +419,21 @@ class LocalGroup:
                                 self.wait_ns, self.status, expert_alignment, scale_rows)
         for ep in self.eps:
             ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
+        return slot, epoch
+
+    def dispatch_ordered(self, xs, idxs, ws, pad_rows: bool = False, end: bool = True):
+        """Every rank's expert-ordered dispatch (arrival counters for expert_gemm);
+        with ``end=False`` the final wait for every peer's rows is left out."""
+        self.epoch += 1
+        slot, epoch = self.epoch % 2, self._kernel_epoch(self.epoch)
+        for r, ep in enumerate(self.eps):
+            ep.dispatch_ordered_begin(xs[r], idxs[r], ws[r], slot, epoch, self.status)
+        for r, ep in enumerate(self.eps):
+            ep.dispatch_ordered_scatter(xs[r], idxs[r], ws[r], slot, epoch, self.num_blocks, pad_rows,
+                                        self.wait_ns, self.status)
+        if end:
+            for ep in self.eps:
+                ep.dispatch_end(slot, epoch, self.wait_ns, self.status)
         return slot, epoch
 
     def dispatch_fp8(self, xqs, scales, idxs, ws, pad_rows: bool = False):

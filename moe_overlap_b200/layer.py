@@ -90,7 +90,8 @@ class MoELayer:
                  micro_batch_size: int = 4096, use_atomic_queue: bool = True,
                  max_recv_rows: Optional[int] = None, training: bool = False,
                  taper_chunks: bool = False, fused_combine: Optional[bool] = None,
-                 enable_nvtx: bool = False, dispatch_fp8: bool = False):
+                 enable_nvtx: bool = False, dispatch_fp8: bool = False,
+                 overlap_tiles: bool = False):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         # NVTX ranges named as the reference's (deepep_dispatch_chunk_i,
         # expert_compute_chunk_i, deepep_combine_chunk_i; train_moe_baseline.py:364-413)
@@ -118,6 +119,12 @@ class MoELayer:
             raise ValueError("dispatch_fp8 needs the forward path and a hidden size that is a "
                              "multiple of 128")
         self.dispatch_fp8 = bool(dispatch_fp8)
+        # Tile-granular overlap of each dispatch with its up-projection: expert-ordered
+        # dispatch, and GEMM1 (DeepEPDispatcher.expert_gemm) enqueued as soon as this
+        # rank's rows are sent; its tiles start expert by expert as their rows land.
+        if overlap_tiles and (training or dispatch_fp8):
+            raise ValueError("overlap_tiles is a forward option for bf16 dispatches")
+        self.overlap_tiles = bool(overlap_tiles)
         self.device = torch.device("cuda", torch.cuda.current_device())
         dev, bf16 = self.device, torch.bfloat16
         self.router_w = torch.zeros(num_experts, hidden_size, dtype=bf16, device=dev)
@@ -177,7 +184,7 @@ class MoELayer:
         """One chunk's dispatch: bf16 rows, or with ``dispatch_fp8`` the chunk quantised
         to e4m3 + per-128 scales on the current stream and dispatched in that form."""
         if not self.dispatch_fp8:
-            return self.dispatcher.dispatch(xs, idx, w, **kw)
+            return self.dispatcher.dispatch(xs, idx, w, ordered=self.overlap_tiles, **kw)
         kw.pop("timeline", None)
         return self.dispatcher.dispatch_fp8(quantize_fp8(xs), idx, w, **kw)
 
@@ -194,8 +201,12 @@ class MoELayer:
         if isinstance(a, tuple):
             buf = self.dispatcher.expert_out_buffer(res.handle)
             a = dequantize_fp8(a[0], a[1], out=buf[:a[0].shape[0]], rows=res.expert_offsets[-1:])
-        grouped_gemm(a, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
-                     activation="gelu", **kw)
+        if getattr(res.handle, "ordered", False):
+            self.dispatcher.expert_gemm(res.handle, self.w1.transpose(1, 2), self.h,
+                                        activation="gelu", **kw)
+        else:
+            grouped_gemm(a, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
+                         activation="gelu", **kw)
         if self.fused_combine:
             self.dispatcher.expert_gemm_push(self.h, self.w2.transpose(1, 2), res.handle, **kw)
             return None
@@ -265,7 +276,8 @@ class MoELayer:
             # starts them as soon as this chunk's rows have landed, and the host
             # time spent enqueuing the next dispatch overlaps them.
             with torch.cuda.stream(self.compute_stream), nvtx_range(f"expert_compute_chunk_{i}", nv):
-                cur.event.current_stream_wait()
+                # An ordered dispatch's GEMM may start once this rank's rows are sent.
+                cur.extra.get("scatter_event", cur.event).current_stream_wait()
                 self._timeline_mark(timeline, f"gemm{i}_start", self.compute_stream)
                 y = self._experts(cur)
                 self._timeline_mark(timeline, f"gemm{i}_end", self.compute_stream)

@@ -49,6 +49,16 @@ def main() -> None:
     ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -30))) - 7)
     assert float(np.mean(diff > ulp * 1.0001)) <= 0.01
     assert stats.load_cv >= 0.0
+    # The same layer with tile-granular overlap (expert-ordered dispatch, GEMM tiles
+    # waiting per expert for rows that arrive over NVLink) gives the same bits.
+    over = MoELayer(H, Fd, E, K, group=dist.group.WORLD, micro_batch_size=256, num_comm_sms=8,
+                    overlap_tiles=True).init_random(seed=11)
+    for _ in range(2):
+        out2, _ = over(x.to(dev), routing=(probs, idx, w))
+        torch.cuda.synchronize()
+        _lib.check_status(dev)
+        assert torch.equal(out2, out), "tile-overlap layer differs from the layer"
+    over.close()
     layer.close()
     dist.barrier()
     dist.destroy_process_group()
