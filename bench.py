@@ -116,6 +116,11 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--nvtx", action="store_true",
                     help="layer workloads: NVTX ranges per chunk, named as the reference's "
                          "(deepep_dispatch_chunk_i, expert_compute_chunk_i, deepep_combine_chunk_i)")
+    ap.add_argument("--overlap-tiles", choices=["auto", "on", "off"], default="auto",
+                    help="layer workloads: expert-ordered dispatch with GEMM tiles that start per "
+                         "expert as its rows land (auto: the layer's default)")
+    ap.add_argument("--dispatch-fp8", action="store_true",
+                    help="layer forward workloads: dispatch tokens as e4m3 + per-128 scales")
     ap.add_argument("--taper", action="store_true",
                     help="layer workloads: quarter-size first/last chunks instead of equal chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
@@ -490,6 +495,9 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                      taper_chunks=args.taper,
                      fused_combine=None if args.combine == "auto" else args.combine == "push",
                      enable_nvtx=args.nvtx,
+                     dispatch_fp8=args.dispatch_fp8,
+                     **({} if args.overlap_tiles == "auto"
+                        else {"overlap_tiles": args.overlap_tiles == "on"}),
                      ).init_random(std=0.02, seed=0)
     bias_info = None
     if cfg["zipf_bias"]:
@@ -642,6 +650,8 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                    "cuda_graph_note": graph_note,
                    "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                    else "pull",
+                   "overlap_tiles": layer.overlap_tiles, "dispatch_payload":
+                       "fp8 e4m3 + per-128 scales" if layer.dispatch_fp8 else "bf16",
                    "comm_sms": args.comm_sms, "gate_bias": bias_info,
                    "realised_expert_share": [round(v, 4) for v in realised_share],
                    "rows_received_per_rank": [int(v) for v in recv_rows.tolist()],

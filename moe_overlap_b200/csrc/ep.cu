@@ -283,29 +283,10 @@ __global__ void count_kernel(Params p) {
   }
   __syncthreads();
   if (p.ordered) {
-    // Expert-ordered dispatch: the assignment behind each of this rank's cb rows
-    // (global expert order, then (token, slot) order), so that the scatter can walk
-    // the rows expert by expert; and this rank's arrival counters for the slot start
-    // again from zero, before any peer can see the count flag raised below.
-    __shared__ int base_sh[kMaxExperts];
-    if (threadIdx.x == 0) {
-      int run = 0;
-      for (int e = 0; e < E; ++e) {
-        base_sh[e] = run;
-        run += p.my_counts[e];
-      }
-    }
+    // Expert-ordered dispatch: this rank's arrival counters for the slot start again
+    // from zero, before any peer can see the count flag raised below.
     uint32_t* arrived = at<uint32_t>(p.peers[p.rank], p.lay.arrived) + p.slot * p.per_rank;
     for (int le = threadIdx.x; le < p.per_rank; le += blockDim.x) arrived[le] = 0;
-    __syncthreads();
-    const int total = p.num_tokens * p.topk;
-    for (int a = threadIdx.x; a < total; a += blockDim.x) {
-      const int64_t v = p.topk_idx[a];
-      if (v < 0 || v >= E) continue;
-      const int e = static_cast<int>(v);
-      const int blk = a / kAssignPerLayoutBlock;
-      p.order[base_sh[e] + p.block_hist[blk * E + e] + p.rank_in_block[a]] = a;
-    }
   }
   for (int d = 0; d < p.world; ++d) {
     int32_t* dst = at<int32_t>(p.peers[d], slot_of(p).counts) + p.rank * E;
@@ -317,6 +298,41 @@ __global__ void count_kernel(Params p) {
     uint64_t* f = at<uint64_t>(p.peers[threadIdx.x], p.lay.count_flag) + p.slot * p.world + p.rank;
     st_release_sys(f, epoch_sh);
   }
+}
+
+// Expert-ordered dispatch: the assignment behind each of this rank's cb rows
+// (global expert order, then (token, slot) order), so that the scatter can walk
+// its rows expert by expert.  One thread per assignment; each block first forms
+// the exclusive prefix of this rank's per-expert counts (one warp scan).
+__global__ void __launch_bounds__(256) order_kernel(Params p) {
+  __shared__ int base_sh[kMaxExperts];
+  const int E = p.num_experts;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int per = (E + 31) / 32;
+    const int beg = min(E, lane * per), end = min(E, beg + per);
+    int local = 0;
+    for (int e = beg; e < end; ++e) local += p.my_counts[e];
+    int incl = local;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
+    }
+    int run = incl - local;
+    for (int e = beg; e < end; ++e) {
+      base_sh[e] = run;
+      run += p.my_counts[e];
+    }
+  }
+  __syncthreads();
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= p.num_tokens * p.topk) return;
+  const int64_t v = p.topk_idx[a];
+  if (v < 0 || v >= E) return;
+  const int e = static_cast<int>(v);
+  const int blk = a / kAssignPerLayoutBlock;
+  p.order[base_sh[e] + p.block_hist[blk * E + e] + p.rank_in_block[a]] = a;
 }
 
 __device__ __forceinline__ uint4 scale_bf16x8(const uint4& v, float s) {
@@ -556,11 +572,11 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
 // have all landed, while later experts are still in flight.  Each rank walks its
 // rows (the cb order: global expert, then (token, slot)) with its experts visited
 // in (local expert, owner) order, so every owner's first expert goes first.  A
-// warp copies R consecutive rows, then fences and adds, per expert among them,
+// warp copies 8 consecutive rows, then fences and adds, per expert among them,
 // the number of rows it delivered to the owner's arrival counter of that local
 // expert (a system-scope atomic over NVLink).  The owner's GEMM waits until a
 // counter reaches that expert's row count (moe_ep_expert_gemm).
-constexpr int kOrderedRowsPerWarp = 4;
+constexpr int kOrderedRowsPerWarp = 8;
 
 __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_kernel(Params p) {
   __shared__ CountView cv;
@@ -1292,6 +1308,8 @@ static int32_t dispatch_begin_impl(moe_ep_t ep, const void* x, const int64_t* to
     if (int rc = check_launch(); rc != MOE_OK) return rc;
   }
   count_kernel<<<1, 256, 0, stream>>>(p);
+  if (int rc = check_launch(); rc != MOE_OK || !ordered || assigns == 0) return rc;
+  order_kernel<<<static_cast<int>((assigns + 255) / 256), 256, 0, stream>>>(p);
   return check_launch();
 }
 
