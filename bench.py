@@ -562,6 +562,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         dist.barrier(group=group)
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    layer._device_align()  # every rank's first forward starts at the same device time
     start.record()
     for _ in range(steps):
         if graph is not None:
@@ -590,6 +591,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
             dist.barrier(group=group)
         torch.cuda.synchronize(device)
         torch.cuda._sleep(3_000_000)
+        layer._device_align()  # the ranks' marks share a device-time origin
         layer(x, routing=routing, timeline=marks)
         torch.cuda.synchronize(device)
         mine = {n: round(marks[0][1].elapsed_time(ev), 4) for n, ev in marks[1:]}
@@ -986,6 +988,45 @@ class GemmRun:
             setattr(self, name, None)
 
 
+def cublas_same_shape(run: GemmRun, steps: int, warmup: int) -> dict:
+    """cuBLAS (through torch) on this workload's shape, timed like the grouped GEMM:
+    a batched GEMM when every expert has the same rows (config 2), else the per-expert
+    torch.matmul loop that the reference's CPU path also runs (config 3).  A library
+    reference point for the roofline, not the product path."""
+    import torch
+
+    counts, k, n = run.counts, run.wl["k"], run.wl["n"]
+    out = torch.empty(run.rows, n, dtype=run.a.dtype, device=run.device)
+    if len(set(counts)) == 1:
+        e, m = len(counts), counts[0]
+        a3, c3 = run.a.view(e, m, k), out.view(e, m, n)
+        fn, form = (lambda: torch.bmm(a3, run.b, out=c3)), "torch.bmm (cuBLAS batched GEMM)"
+    else:
+        offs = [0]
+        for c in counts:
+            offs.append(offs[-1] + int(c))
+
+        def fn():
+            for ex in range(len(counts)):
+                if offs[ex + 1] > offs[ex]:
+                    torch.matmul(run.a[offs[ex]:offs[ex + 1]], run.b[ex], out=out[offs[ex]:offs[ex + 1]])
+        form = "per-expert torch.matmul loop (cuBLAS)"
+    for _ in range(max(3, warmup)):
+        fn()
+        run.flush.fill_(1)
+    evs = []
+    for i in range(steps):
+        run.flush.fill_(i & 0xFF)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(run.stream)
+        fn()
+        s1.record(run.stream)
+        evs.append((s0, s1))
+    torch.cuda.synchronize(run.device)
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    return {"form": form, "tflops": round(run.flops / (ms / 1e3) / 1e12, 2), "ms_per_launch": round(ms, 5)}
+
+
 def measure_e2e(run: GemmRun, steps: int, warmup: int, world: int) -> dict:
     """The headline metric end to end through ``persistent_grouped_gemm``.
 
@@ -1114,6 +1155,9 @@ def main() -> None:
     value = world * run.flops * args.steps / (res["total_ms"] / 1e3) / 1e12
     e2e = None if args.no_e2e else measure_e2e(run, args.steps, args.warmup, world)
     roofline = run.roofline(res["launch_ms"])
+    lib_ref = cublas_same_shape(run, args.steps, args.warmup)
+    lib_ref["ours_over_cublas"] = round(roofline["achieved"] / lib_ref["tflops"], 4)
+    roofline["cublas_same_shape"] = lib_ref
     run.release()
     torch.cuda.empty_cache()
 
@@ -1131,6 +1175,9 @@ def main() -> None:
             "roofline": r3.roofline(t3["launch_ms"]),
             "clocks": t3["clocks"],
         }
+        lib3 = cublas_same_shape(r3, args.steps, args.warmup)
+        lib3["ours_over_cublas"] = round(extras["gemm_cfg3"]["roofline"]["achieved"] / lib3["tflops"], 4)
+        extras["gemm_cfg3"]["roofline"]["cublas_same_shape"] = lib3
         r3.release()
         del r3
         torch.cuda.empty_cache()

@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
         }
         const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
         uint4* dst = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
-        constexpr int U = 4;
+        constexpr int U = 8;  // a 4 KB row in one pass: every load of the row in flight at once
         for (int base = 0; base < nvec; base += 32 * U) {
           uint4 vv[U];
 #pragma unroll

@@ -314,7 +314,9 @@ class MoELayer:
         delay of ``host_cover_cycles`` SM cycles (~1 ms), started before its
         events, so the host's enqueueing of the phase (argument checks and
         several launches) happens while the GPU is busy and the events time the
-        phase's device work only, as it runs inside the pipelined forward.
+        phase's device work only, as it runs inside the pipelined forward; a
+        one-element all-reduce after the delay lines the ranks up on the device, so
+        a phase's time does not include another rank's late start.
         """
         x = x.to(torch.bfloat16).contiguous()
         _, idx, w = routing
@@ -329,6 +331,7 @@ class MoELayer:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             if host_cover_cycles > 0:
                 torch.cuda._sleep(int(host_cover_cycles))
+            self._device_align()
             start.record()
             r = fn()
             torch.cuda.current_stream(self.device).wait_stream(disp.comm_stream)
@@ -356,7 +359,8 @@ class MoELayer:
         peer's rows) and, after its expert GEMMs, its combine (ready flag, pull +
         reduce) run with a device synchronisation and, across ranks, a barrier
         before each, behind a device-side delay of ``host_cover_cycles`` SM cycles
-        so the host's enqueueing is not timed.  Both use the grid of the forward's
+        so the host's enqueueing is not timed, and a device-side all-reduce that
+        lines the ranks up.  Both use the grid of the forward's
         unoverlapped phases (four blocks per SM).  Returns this rank's times:
         ``dispatch_layout_count``, ``dispatch_scatter``, ``dispatch_wait``,
         ``combine_ready``, ``combine_pull``.  The scatter includes the wait for
@@ -370,6 +374,7 @@ class MoELayer:
         self._sync_all()
         if host_cover_cycles > 0:
             torch.cuda._sleep(int(host_cover_cycles))
+        self._device_align()
         res = self._dispatch(x[s:e], idx[s:e], w[s:e], pad_rows=False,
                              num_sms=self.solo_comm_blocks, timeline=marks_d)
         res.event.current_stream_wait()
@@ -377,6 +382,7 @@ class MoELayer:
         self._sync_all()
         if host_cover_cycles > 0:
             torch.cuda._sleep(int(host_cover_cycles))
+        self._device_align()
         out = torch.empty(e - s, self.hidden, dtype=torch.bfloat16, device=self.device)
         if y is None:  # fused combine push: the transfer ran inside the GEMM
             _, ev = self._combine(None, res.handle, out=out, num_sms=self.solo_comm_blocks)
@@ -390,6 +396,15 @@ class MoELayer:
             for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
                 times[prefix + name] = a.elapsed_time(b)
         return times
+
+    def _device_align(self) -> None:
+        """A one-element all-reduce on the current stream: every rank's work enqueued
+        after it starts when the slowest rank has reached it, so timed phases begin at
+        the same device time on every GPU instead of one host barrier's skew apart."""
+        if self.world > 1:
+            if getattr(self, "_align_buf", None) is None:
+                self._align_buf = torch.zeros(1, dtype=torch.float32, device=self.device)
+            dist.all_reduce(self._align_buf, group=self.group)
 
     def _sync_all(self) -> None:
         torch.cuda.synchronize(self.device)
