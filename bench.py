@@ -108,6 +108,9 @@ def parse_args() -> argparse.Namespace:
                     help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-graph", action="store_true",
                     help="layer workloads: time eager steps instead of a captured CUDA graph")
+    ap.add_argument("--graph-multi", action="store_true",
+                    help="layer forward workloads with N > 1: replay a captured CUDA graph on every "
+                         "rank too (default: eager forwards across GPUs)")
     ap.add_argument("--combine", choices=["auto", "push", "pull"], default="auto",
                     help="layer workloads: GEMM-fused combine push, or GEMM into expert_out + pull "
                          "combine (auto: the layer's default, pull)")
@@ -542,7 +545,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
     # epochs); across GPUs they run eagerly, so that a capture problem on one rank
     # cannot leave the others waiting.
     graph, graph_note = None, None
-    if world == 1 and graph_ok:
+    if graph_ok and (world == 1 or getattr(args, "graph_multi", False)):
         try:
             from moe_overlap_b200.layer import ForwardGraph
 
@@ -579,6 +582,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     step_ms = float(t.item())
+    graph_used = graph is not None
     del graph
 
     marks_by_rank = None
@@ -648,7 +652,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         "config": {"workload": name, "description": cfg["desc"],
                    "tokens_per_rank": T, "micro_batch": args.micro_batch,
                    "chunks": [e - s for s, e in layer.chunk_plan(T)],
-                   "cuda_graph": world == 1 and graph_ok and graph_note is None,
+                   "cuda_graph": graph_used,
                    "cuda_graph_note": graph_note,
                    "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                    else "pull",

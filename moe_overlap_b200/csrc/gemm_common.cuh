@@ -313,11 +313,13 @@ int grouped_gemm_launch(const void* a, int64_t lda, const void* b, int64_t b_str
                         void* aux_out, int64_t ld_aux, int32_t* status, cudaStream_t stream,
                         const PushTarget* push, const ArrivalWait* arrival = nullptr);
 
-// Launches the 2-SM (CTA pair) kernel; grid must be even.  `tc` is the 2-D {N, m_total}
+// Launches the 2-SM (CTA pair) kernel; grid must be even.  `ta_half` is A's map with
+// 64-row boxes (the rows a swapped tile reads per CTA); `tc` is the 2-D {N, m_total}
 // store map of C (32x32 boxes, 64-byte swizzle), used when p.c_tma is set.
 // Returns a MOE_* code.
-int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                       const CUtensorMap& tc, const Params& p, int grid, cudaStream_t stream);
+int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& ta_half,
+                       const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, int grid,
+                       cudaStream_t stream);
 
 }  // namespace gg
 }  // namespace moe

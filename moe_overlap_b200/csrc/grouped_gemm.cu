@@ -461,12 +461,14 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
   if (use_pair) grid &= ~1;
   const CUtensorMapDataType dt =
       dtype == MOE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, ta_half, tb;
   {
     const uint64_t dims[2] = {uint64_t(k), uint64_t(m_total)};
     const uint64_t strides[1] = {uint64_t(lda) * 2};
     const uint32_t box[2] = {BK, BM};
     if (int rc = encode_tiled(&ta, dt, 2, a, dims, strides, box); rc != MOE_OK) return rc;
+    const uint32_t box_half[2] = {BK, BM / 2};  // the 64 rows a swapped pair tile reads per CTA
+    if (int rc = encode_tiled(&ta_half, dt, 2, a, dims, strides, box_half); rc != MOE_OK) return rc;
   }
   {
     const int64_t se = num_experts > 1 ? b_stride_e : b_inner_stride * (b_mn ? k : n);
@@ -527,7 +529,7 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
       cudaMemsetAsync(work_counter, 0, sizeof(int32_t), stream) != cudaSuccess)
     return MOE_ERR_CUDA;
   const bool bf16 = dtype == MOE_DTYPE_BF16;
-  if (use_pair) return launch_pair_kernel(bf16, b_mn, ta, tb, tc, p, grid, stream);
+  if (use_pair) return launch_pair_kernel(bf16, b_mn, ta, ta_half, tb, tc, p, grid, stream);
   if (bf16 && b_mn) return launch<true, true>(ta, tb, p, grid, stream);
   if (bf16 && !b_mn) return launch<true, false>(ta, tb, p, grid, stream);
   if (!bf16 && b_mn) return launch<false, true>(ta, tb, p, grid, stream);

@@ -27,8 +27,8 @@
 // the second CTA's 128 rows of a 256-row MMA empty.  With swap_tails such a tile
 // is computed transposed instead: the 256 weight columns take the MMA's M side
 // (128 per CTA, the same B stage as usual, now the MMA's A operand) and the tile's
-// rows its N side (N = 128: 64 rows from each CTA's A stage), so the tensor work
-// of the tile halves.  Each CTA's TMEM then holds its 128 output columns in its
+// rows its N side (N = 128: 64 rows from each CTA, loaded through a 64-row map), so
+// the tensor work of the tile halves and its A traffic too.  Each CTA's TMEM then holds its 128 output columns in its
 // lanes and the tile's rows in 128 accumulator columns; the epilogue stores
 // them transposed (plain or GELU epilogues only).
 // No load uses cluster multicast; the pair exchanges only barrier arrivals and
@@ -60,6 +60,8 @@ constexpr int A_STAGE_BYTES = BM_CTA * BK * 2;  // 16 KiB
 constexpr int B_STAGE_BYTES = BK * BN_CTA * 2;  // 16 KiB
 constexpr int B_SLAB_BYTES = BK * 64 * 2;       // one 64-column slab of an N-major B stage
 constexpr uint32_t PAIR_TX_BYTES = 2 * (A_STAGE_BYTES + B_STAGE_BYTES);
+// A swapped tile loads only the 64 rows per CTA that its MMA reads.
+constexpr uint32_t PAIR_TX_BYTES_SWAPPED = 2 * (A_STAGE_BYTES / 2 + B_STAGE_BYTES);
 constexpr int EPI_STAGE_BYTES = 32 * 32 * 2;  // one 32x32 bf16 chunk per epilogue warp
 constexpr uint32_t TMEM_COLS = 2 * BN;
 
@@ -173,6 +175,7 @@ __device__ __forceinline__ bool issue_tile(Ctrl* ctrl, uint8_t* sA, uint8_t* sB,
 template <bool BF16, bool B_MN_MAJOR, bool PUSH>
 __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                             const __grid_constant__ CUtensorMap tmap_a_half,
                              const __grid_constant__ CUtensorMap tmap_b,
                              const __grid_constant__ CUtensorMap tmap_c, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -214,6 +217,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_a_half);
       tma_prefetch_desc(&tmap_b);
     }
     build_tile_prefix(p.offsets, p.offsets_int64, p.num_experts, p.m_total, BM, tiles_n,
@@ -286,10 +290,12 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
           }
           ready_expert = s.w;
         }
-        // A swapped tile takes 64 rows from each CTA (the MMA's N side); the box
-        // still loads 128, of which the MMA reads the first 64.
+        // A swapped tile takes 64 rows from each CTA (the MMA's N side), loaded
+        // through the 64-row map into the first half of the A stage.
         const bool swapped = p.swap_tails && s.y <= BM_CTA;
         const int row_a = s.x + static_cast<int>(crank) * (swapped ? BM_CTA / 2 : BM_CTA);
+        const CUtensorMap* map_a = swapped ? &tmap_a_half : &tmap_a;
+        const uint32_t stage_tx = swapped ? PAIR_TX_BYTES_SWAPPED : PAIR_TX_BYTES;
         const int n_b = s.z + static_cast<int>(crank) * BN_CTA;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(smem_u32(&ctrl->empty[stage]), phase ^ 1, abort_flag)) {
@@ -297,9 +303,9 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
             break;
           }
           const uint32_t full_local = smem_u32(&ctrl->full[stage]);
-          if (leader) mbar_arrive_expect_tx(full_local, PAIR_TX_BYTES);
+          if (leader) mbar_arrive_expect_tx(full_local, stage_tx);
           const uint32_t full_leader = mapa_shared(full_local, 0);
-          tma_load_2d_pair(smem_u32(sA + stage * A_STAGE_BYTES), &tmap_a, full_leader, kb * BK, row_a);
+          tma_load_2d_pair(smem_u32(sA + stage * A_STAGE_BYTES), map_a, full_leader, kb * BK, row_a);
           const uint32_t b_dst = smem_u32(sB + stage * B_STAGE_BYTES);
           if constexpr (B_MN_MAJOR) {
 #pragma unroll
@@ -445,8 +451,8 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
 }
 
 template <bool BF16, bool B_MN, bool PUSH = false>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
-           int grid, cudaStream_t stream) {
+int launch(const CUtensorMap& ta, const CUtensorMap& ta_half, const CUtensorMap& tb,
+           const CUtensorMap& tc, const Params& p, int grid, cudaStream_t stream) {
   auto kern = grouped_gemm_pair_kernel<BF16, B_MN, PUSH>;
   static std::once_flag once[kMaxDevices];
   int dev = 0;
@@ -457,24 +463,25 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
                                     static_cast<int>(smem_bytes(kMaxExperts)));
   });
   if (attr_err != cudaSuccess) return MOE_ERR_CUDA;
-  kern<<<grid, NUM_THREADS, smem_bytes(p.num_experts), stream>>>(ta, tb, tc, p);
+  kern<<<grid, NUM_THREADS, smem_bytes(p.num_experts), stream>>>(ta, ta_half, tb, tc, p);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
 }  // namespace pair
 
-int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                       const CUtensorMap& tc, const Params& p, int grid, cudaStream_t stream) {
+int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& ta_half,
+                       const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, int grid,
+                       cudaStream_t stream) {
   if (grid < 2 || grid % 2 != 0) return MOE_ERR_INVALID_ARG;
   if (p.push.src != nullptr) {  // combine push (bf16 only)
     if (!bf16) return MOE_ERR_INVALID_ARG;
-    return b_mn ? pair::launch<true, true, true>(ta, tb, tc, p, grid, stream)
-                : pair::launch<true, false, true>(ta, tb, tc, p, grid, stream);
+    return b_mn ? pair::launch<true, true, true>(ta, ta_half, tb, tc, p, grid, stream)
+                : pair::launch<true, false, true>(ta, ta_half, tb, tc, p, grid, stream);
   }
-  if (bf16 && b_mn) return pair::launch<true, true>(ta, tb, tc, p, grid, stream);
-  if (bf16 && !b_mn) return pair::launch<true, false>(ta, tb, tc, p, grid, stream);
-  if (!bf16 && b_mn) return pair::launch<false, true>(ta, tb, tc, p, grid, stream);
-  return pair::launch<false, false>(ta, tb, tc, p, grid, stream);
+  if (bf16 && b_mn) return pair::launch<true, true>(ta, ta_half, tb, tc, p, grid, stream);
+  if (bf16 && !b_mn) return pair::launch<true, false>(ta, ta_half, tb, tc, p, grid, stream);
+  if (!bf16 && b_mn) return pair::launch<false, true>(ta, ta_half, tb, tc, p, grid, stream);
+  return pair::launch<false, false>(ta, ta_half, tb, tc, p, grid, stream);
 }
 
 }  // namespace gg
