@@ -108,9 +108,6 @@ def parse_args() -> argparse.Namespace:
                     help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-graph", action="store_true",
                     help="layer workloads: time eager steps instead of a captured CUDA graph")
-    ap.add_argument("--graph-multi", action="store_true",
-                    help="layer forward workloads with N > 1: replay a captured CUDA graph on every "
-                         "rank too (default: eager forwards across GPUs)")
     ap.add_argument("--combine", choices=["auto", "push", "pull"], default="auto",
                     help="layer workloads: GEMM-fused combine push, or GEMM into expert_out + pull "
                          "combine (auto: the layer's default, pull)")
@@ -492,23 +489,30 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
 
     cfg = LAYER_WORKLOADS[name]
     T, H, Fd, E, K = cfg["tokens"], cfg["hidden"], cfg["ffn"], cfg["experts"], cfg["top_k"]
-    layer = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
-                     router_bias=cfg["zipf_bias"], num_comm_sms=args.comm_sms,
-                     micro_batch_size=args.micro_batch,
-                     taper_chunks=args.taper,
-                     fused_combine=None if args.combine == "auto" else args.combine == "push",
-                     enable_nvtx=args.nvtx,
-                     dispatch_fp8=args.dispatch_fp8,
-                     **({} if args.overlap_tiles == "auto"
-                        else {"overlap_tiles": args.overlap_tiles == "on"}),
-                     ).init_random(std=0.02, seed=0)
-    bias_info = None
+    bias_info, bias = None, None
     if cfg["zipf_bias"]:
         rw, _, _ = random_weights(E, H, Fd, 0.02, 0)
         bias, iters, err = zipf_gate_bias(rw.to(torch.bfloat16).float().numpy(), E, K)
-        layer.router_b.copy_(torch.from_numpy(bias))
         bias_info = {"fit": "per-expert, Zipf(1.0) target shares", "iterations": iters,
                      "max_rel_share_error_on_sample": round(err, 3)}
+
+    def build_layer():
+        """Collective: every rank builds the layer (and its dispatcher) together."""
+        lay = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
+                       router_bias=cfg["zipf_bias"], num_comm_sms=args.comm_sms,
+                       micro_batch_size=args.micro_batch,
+                       taper_chunks=args.taper,
+                       fused_combine=None if args.combine == "auto" else args.combine == "push",
+                       enable_nvtx=args.nvtx,
+                       dispatch_fp8=args.dispatch_fp8,
+                       **({} if args.overlap_tiles == "auto"
+                          else {"overlap_tiles": args.overlap_tiles == "on"}),
+                       ).init_random(std=0.02, seed=0)
+        if bias is not None:
+            lay.router_b.copy_(torch.from_numpy(bias))
+        return lay
+
+    layer = build_layer()
     g = torch.Generator().manual_seed(1000 + rank)
     x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(device)
     routing = layer.route(x)
@@ -541,11 +545,13 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         layer(x, routing=routing)
     torch.cuda.synchronize(device)
     mo.check_status(device, sync=True)
-    # On one GPU the timed forwards replay one CUDA graph (device-drawn exchange
-    # epochs); across GPUs they run eagerly, so that a capture problem on one rank
-    # cannot leave the others waiting.
+    # The timed forwards replay one CUDA graph per rank (device-drawn exchange epochs),
+    # so host launch overhead and host stalls stay out of the device's schedule.  The
+    # ranks agree on the outcome: if any rank's capture fails, every rank rebuilds the
+    # layer (fresh dispatchers, host epochs) and times eager forwards instead.
     graph, graph_note = None, None
-    if graph_ok and (world == 1 or getattr(args, "graph_multi", False)):
+    if graph_ok:
+        ok = 1
         try:
             from moe_overlap_b200.layer import ForwardGraph
 
@@ -555,8 +561,22 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
             torch.cuda.synchronize(device)
             mo.check_status(device, sync=True)
         except Exception as exc:  # report and time eager forwards instead
+            ok = 0
             graph = None
             graph_note = f"capture failed ({type(exc).__name__}: {exc})"[:240]
+            torch.cuda.synchronize(device)
+        if world > 1:
+            flag = torch.tensor([ok], dtype=torch.int32, device=device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+            if int(flag.item()) == 0 and ok:
+                graph_note = "capture failed on another rank"
+            ok = int(flag.item())
+        if not ok:
+            graph = None
+            layer.close()
+            layer = build_layer()
+            for _ in range(max(3, warmup)):
+                layer(x, routing=routing)
             torch.cuda.synchronize(device)
 
     sampler = ClockSampler(device)
@@ -564,24 +584,26 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
     if world > 1:
         dist.barrier(group=group)
     torch.cuda.synchronize(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     layer._device_align()  # every rank's first forward starts at the same device time
-    start.record()
-    for _ in range(steps):
+    marks[0].record()
+    for i in range(steps):
         if graph is not None:
             graph.replay()
         else:
             layer(x, routing=routing)
-    end.record()
+        marks[i + 1].record()
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier(group=group)
     clocks = sampler.stop()
     mo.check_status(device, sync=True)
-    t = torch.tensor([start.elapsed_time(end) / steps], dtype=torch.float64, device=device)
+    per_step = [marks[i].elapsed_time(marks[i + 1]) for i in range(steps)]
+    t = torch.tensor([marks[0].elapsed_time(marks[-1]) / steps, statistics.median(per_step)],
+                     dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-    step_ms = float(t.item())
+    step_ms, median_ms = float(t[0].item()), float(t[1].item())
     graph_used = graph is not None
     del graph
 
@@ -649,6 +671,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         "steps": steps,
         "warmup": max(3, warmup),
         "ms_per_step": round(step_ms, 4),
+        "ms_per_step_median": round(median_ms, 4),
         "config": {"workload": name, "description": cfg["desc"],
                    "tokens_per_rank": T, "micro_batch": args.micro_batch,
                    "chunks": [e - s for s, e in layer.chunk_plan(T)],

@@ -572,11 +572,12 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
 // have all landed, while later experts are still in flight.  Each rank walks its
 // rows (the cb order: global expert, then (token, slot)) with its experts visited
 // in (local expert, owner) order, so every owner's first expert goes first.  A
-// warp copies 8 consecutive rows, then fences and adds, per expert among them,
+// warp copies 2 consecutive rows (their lookups and loads in flight together), then
+// fences and adds, per expert among them,
 // the number of rows it delivered to the owner's arrival counter of that local
 // expert (a system-scope atomic over NVLink).  The owner's GEMM waits until a
 // counter reaches that expert's row count (moe_ep_expert_gemm).
-constexpr int kOrderedRowsPerWarp = 8;
+constexpr int kOrderedRowsPerWarp = 2;
 
 __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_kernel(Params p) {
   __shared__ CountView cv;
@@ -628,39 +629,41 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
   const SlotLayout sl = slot_of(p);
   const int total_rows = vbase[E];
   if (!overflow) {
-    for (int c = blockIdx.x * (kCommThreads / 32) + warp; c * kOrderedRowsPerWarp < total_rows;
-         c += warps_total) {
-      const int v0 = c * kOrderedRowsPerWarp;
-      const int v1 = min(v0 + kOrderedRowsPerWarp, total_rows);
-      int seg = 0;
-      for (int lo = 0, hi = E; hi - lo > 1;) {  // vbase[seg] <= v0 < vbase[seg + 1]
-        const int mid = (lo + hi) >> 1;
-        if (vbase[mid] <= v0) lo = mid; else hi = mid;
-        seg = lo;
-      }
-      int run_seg = -1, run_n = 0;
-      for (int v = v0; v <= v1; ++v) {
-        if (v < v1)
-          while (vbase[seg + 1] <= v) ++seg;  // empty segments are skipped
-        // Close the run of rows of one expert before a new expert (or the end).
-        if (run_n > 0 && (v == v1 || seg != run_seg)) {
-          __threadfence_system();
-          __syncwarp();
-          if (lane == 0) {
-            const int e = vexp[run_seg];
-            const int d = e / p.per_rank;
-            __threadfence_system();
-            atomicAdd_system(at<unsigned int>(p.peers[d], p.lay.arrived) + p.slot * p.per_rank +
-                                 (e - d * p.per_rank),
-                             static_cast<unsigned int>(run_n));
-          }
-          run_n = 0;
+    constexpr int R = kOrderedRowsPerWarp;
+    for (int c = blockIdx.x * (kCommThreads / 32) + warp; c * R < total_rows; c += warps_total) {
+      const int v0 = c * R;
+      const int nr = min(R, total_rows - v0);
+      // Lane r (< nr) resolves walk position v0 + r: its segment, offset, assignment and
+      // weight, so the chunk's lookups are in flight together; then every lane reads them.
+      int my_seg = 0, my_off = 0, my_a = 0;
+      float my_w = 0.0f;
+      if (lane < nr) {
+        const int v = v0 + lane;
+        int lo = 0;
+        for (int hi = E; hi - lo > 1;) {  // vbase[lo] <= v < vbase[lo + 1]
+          const int mid = (lo + hi) >> 1;
+          if (vbase[mid] <= v) lo = mid; else hi = mid;
         }
-        if (v == v1) break;
-        const int e = vexp[seg];
-        const int off = v - vbase[seg];
+        my_seg = lo;
+        my_off = v - vbase[lo];
+        my_a = p.order[cv.my_base[vexp[lo]] + my_off];
+        my_w = p.topk_w[my_a];
+      }
+      const uint4* src[R];
+      uint4* dst[R];
+      int seg_of[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int sg = __shfl_sync(0xffffffffu, my_seg, r);
+        const int off = __shfl_sync(0xffffffffu, my_off, r);
+        const int a = __shfl_sync(0xffffffffu, my_a, r);
+        const float w = __shfl_sync(0xffffffffu, my_w, r);
+        seg_of[r] = sg;
+        src[r] = nullptr;
+        dst[r] = nullptr;
+        if (r >= nr) continue;
+        const int e = vexp[sg];
         const int cb_row = cv.my_base[e] + off;
-        const int a = p.order[cb_row];
         const int t = a / p.topk, j = a - t * p.topk;
         const int d = e / p.per_rank;
         const int row = cv.exp_base[e] + cv.my_prefix[e] + off;
@@ -669,7 +672,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
           at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
               (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
           at<float>(peer, sl.topk_w)[static_cast<int64_t>(row) * p.max_topk + lane] =
-              (lane == j) ? p.topk_w[a] : 0.0f;
+              (lane == j) ? w : 0.0f;
         }
         if (lane == 0) {
           at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
@@ -677,24 +680,43 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
           p.send_pos[a] = row;
           p.cb_pos[a] = cb_row;
         }
-        const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
-        uint4* dst = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
-        constexpr int U = 8;  // a 4 KB row in one pass: every load of the row in flight at once
-        for (int base = 0; base < nvec; base += 32 * U) {
-          uint4 vv[U];
+        src[r] = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
+        dst[r] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+      }
+      // Both rows' loads of a pass are in flight before any store.
+      constexpr int U = 4;
+      for (int base = 0; base < nvec; base += 32 * U) {
+        uint4 vv[R][U];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (i < nvec) vv[u] = __ldg(src + i);
+            if (r < nr && i < nvec) vv[r][u] = __ldg(src[r] + i);
           }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (i < nvec) dst[i] = vv[u];
+            if (r < nr && i < nvec) dst[r][i] = vv[r][u];
           }
+      }
+      // Count the delivered rows on their owners, per expert (1 or 2 atomics).
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_system();
+        for (int r = 0; r < nr;) {
+          int n = 1;
+          while (r + n < nr && seg_of[r + n] == seg_of[r]) ++n;
+          const int e = vexp[seg_of[r]];
+          const int d = e / p.per_rank;
+          atomicAdd_system(at<unsigned int>(p.peers[d], p.lay.arrived) + p.slot * p.per_rank +
+                               (e - d * p.per_rank),
+                           static_cast<unsigned int>(n));
+          r += n;
         }
-        if (run_n == 0) run_seg = seg;
-        ++run_n;
       }
     }
     // (token, slot) pairs with no expert: no receive row.
