@@ -104,6 +104,9 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--comm-sms", type=int, default=148,
                     help="layer workloads: blocks of the dispatch/combine kernels (one per SM "
                          "by default; they run beside the persistent GEMM CTAs)")
+    ap.add_argument("--solo-blocks", type=int, default=0,
+                    help="layer workloads: blocks of the exchange phases that run alone (default "
+                         "four per SM)")
     ap.add_argument("--micro-batch", type=int, default=4096,
                     help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-graph", action="store_true",
@@ -505,6 +508,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                        fused_combine=None if args.combine == "auto" else args.combine == "push",
                        enable_nvtx=args.nvtx,
                        dispatch_fp8=args.dispatch_fp8,
+                       solo_comm_blocks=args.solo_blocks or None,
                        **({} if args.overlap_tiles == "auto"
                           else {"overlap_tiles": args.overlap_tiles == "on"}),
                        ).init_random(std=0.02, seed=0)

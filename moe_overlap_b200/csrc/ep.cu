@@ -572,17 +572,18 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
 // have all landed, while later experts are still in flight.  Each rank walks its
 // rows (the cb order: global expert, then (token, slot)) with its experts visited
 // in (local expert, owner) order, so every owner's first expert goes first.  A
-// warp copies 2 consecutive rows (their lookups and loads in flight together), then
-// fences and adds, per expert among them,
-// the number of rows it delivered to the owner's arrival counter of that local
-// expert (a system-scope atomic over NVLink).  The owner's GEMM waits until a
+// block copies a contiguous range of that walk in batches of up to 64 rows, then
+// fences and adds, per expert among them, the number of rows it delivered to the
+// owner's arrival counter of that local expert (a system-scope atomic over NVLink).  The owner's GEMM waits until a
 // counter reaches that expert's row count (moe_ep_expert_gemm).
-constexpr int kOrderedRowsPerWarp = 2;
+constexpr int kOrderedBatch = 64;  // rows per lookup / fence batch of a block
 
 __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_kernel(Params p) {
   __shared__ CountView cv;
   __shared__ int vbase[kMaxExperts + 1];  // first walk position of each (local expert, owner) segment
   __shared__ int vexp[kMaxExperts];       // global expert of each segment
+  __shared__ int batch_seg[kOrderedBatch], batch_off[kOrderedBatch], batch_a[kOrderedBatch];
+  __shared__ float batch_w[kOrderedBatch];
   if (threadIdx.x == 0) {
     cv.overflow = 0;
     cv.fail = 0;
@@ -629,40 +630,34 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
   const SlotLayout sl = slot_of(p);
   const int total_rows = vbase[E];
   if (!overflow) {
-    constexpr int R = kOrderedRowsPerWarp;
-    for (int c = blockIdx.x * (kCommThreads / 32) + warp; c * R < total_rows; c += warps_total) {
-      const int v0 = c * R;
-      const int nr = min(R, total_rows - v0);
-      // Lane r (< nr) resolves walk position v0 + r: its segment, offset, assignment and
-      // weight, so the chunk's lookups are in flight together; then every lane reads them.
-      int my_seg = 0, my_off = 0, my_a = 0;
-      float my_w = 0.0f;
-      if (lane < nr) {
-        const int v = v0 + lane;
+    // Each block walks one contiguous range of the walk, in batches of up to
+    // kOrderedBatch rows: the batch's lookups first (one thread per row), then the
+    // rows (one warp per row), then one fence and, per expert in the batch, one
+    // arrival add on the owner.  Low-numbered blocks hold the first experts.
+    const int per_block = (total_rows + gridDim.x - 1) / gridDim.x;
+    const int v_begin = min(total_rows, static_cast<int>(blockIdx.x) * per_block);
+    const int v_end = min(total_rows, v_begin + per_block);
+    for (int vb = v_begin; vb < v_end; vb += kOrderedBatch) {
+      const int n = min(kOrderedBatch, v_end - vb);
+      if (threadIdx.x < n) {
+        const int v = vb + threadIdx.x;
         int lo = 0;
         for (int hi = E; hi - lo > 1;) {  // vbase[lo] <= v < vbase[lo + 1]
           const int mid = (lo + hi) >> 1;
           if (vbase[mid] <= v) lo = mid; else hi = mid;
         }
-        my_seg = lo;
-        my_off = v - vbase[lo];
-        my_a = p.order[cv.my_base[vexp[lo]] + my_off];
-        my_w = p.topk_w[my_a];
+        const int off = v - vbase[lo];
+        const int a = p.order[cv.my_base[vexp[lo]] + off];
+        batch_seg[threadIdx.x] = lo;
+        batch_off[threadIdx.x] = off;
+        batch_a[threadIdx.x] = a;
+        batch_w[threadIdx.x] = p.topk_w[a];
       }
-      const uint4* src[R];
-      uint4* dst[R];
-      int seg_of[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int sg = __shfl_sync(0xffffffffu, my_seg, r);
-        const int off = __shfl_sync(0xffffffffu, my_off, r);
-        const int a = __shfl_sync(0xffffffffu, my_a, r);
-        const float w = __shfl_sync(0xffffffffu, my_w, r);
-        seg_of[r] = sg;
-        src[r] = nullptr;
-        dst[r] = nullptr;
-        if (r >= nr) continue;
-        const int e = vexp[sg];
+      __syncthreads();
+      for (int r = warp; r < n; r += kCommThreads / 32) {
+        const int e = vexp[batch_seg[r]];
+        const int off = batch_off[r];
+        const int a = batch_a[r];
         const int cb_row = cv.my_base[e] + off;
         const int t = a / p.topk, j = a - t * p.topk;
         const int d = e / p.per_rank;
@@ -672,7 +667,7 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
           at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
               (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
           at<float>(peer, sl.topk_w)[static_cast<int64_t>(row) * p.max_topk + lane] =
-              (lane == j) ? w : 0.0f;
+              (lane == j) ? batch_w[r] : 0.0f;
         }
         if (lane == 0) {
           at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
@@ -680,44 +675,40 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
           p.send_pos[a] = row;
           p.cb_pos[a] = cb_row;
         }
-        src[r] = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
-        dst[r] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
-      }
-      // Both rows' loads of a pass are in flight before any store.
-      constexpr int U = 4;
-      for (int base = 0; base < nvec; base += 32 * U) {
-        uint4 vv[R][U];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
+        const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
+        uint4* dst = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+        constexpr int U = 8;  // a 4 KB row in one pass
+        for (int base = 0; base < nvec; base += 32 * U) {
+          uint4 vv[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (r < nr && i < nvec) vv[r][u] = __ldg(src[r] + i);
+            if (i < nvec) vv[u] = __ldg(src + i);
           }
-#pragma unroll
-        for (int r = 0; r < R; ++r)
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (r < nr && i < nvec) dst[r][i] = vv[r][u];
+            if (i < nvec) dst[i] = vv[u];
           }
+        }
       }
-      // Count the delivered rows on their owners, per expert (1 or 2 atomics).
+      // The batch's rows are visible everywhere before their owners count them.
       __threadfence_system();
-      __syncwarp();
-      if (lane == 0) {
+      __syncthreads();
+      if (threadIdx.x == 0) {
         __threadfence_system();
-        for (int r = 0; r < nr;) {
-          int n = 1;
-          while (r + n < nr && seg_of[r + n] == seg_of[r]) ++n;
-          const int e = vexp[seg_of[r]];
+        for (int r = 0; r < n;) {
+          int m = 1;
+          while (r + m < n && batch_seg[r + m] == batch_seg[r]) ++m;
+          const int e = vexp[batch_seg[r]];
           const int d = e / p.per_rank;
           atomicAdd_system(at<unsigned int>(p.peers[d], p.lay.arrived) + p.slot * p.per_rank +
                                (e - d * p.per_rank),
-                           static_cast<unsigned int>(n));
-          r += n;
+                           static_cast<unsigned int>(m));
+          r += m;
         }
       }
+      __syncthreads();  // the next batch reuses the batch arrays
     }
     // (token, slot) pairs with no expert: no receive row.
     for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < p.num_tokens * p.topk;

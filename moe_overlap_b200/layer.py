@@ -91,7 +91,7 @@ class MoELayer:
                  max_recv_rows: Optional[int] = None, training: bool = False,
                  taper_chunks: bool = False, fused_combine: Optional[bool] = None,
                  enable_nvtx: bool = False, dispatch_fp8: bool = False,
-                 overlap_tiles: bool = False):
+                 overlap_tiles: bool = False, solo_comm_blocks: Optional[int] = None):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         # NVTX ranges named as the reference's (deepep_dispatch_chunk_i,
         # expert_compute_chunk_i, deepep_combine_chunk_i; train_moe_baseline.py:364-413)
@@ -143,7 +143,7 @@ class MoELayer:
         self.gemm_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         # Exchange blocks when nothing runs beside them (the training path waits for
         # each exchange phase): four 128-thread blocks per SM.
-        self.solo_comm_blocks = 4 * self.gemm_sms
+        self.solo_comm_blocks = int(solo_comm_blocks) if solo_comm_blocks else 4 * self.gemm_sms
         self.h = torch.empty(self.dispatcher.max_recv_rows, ffn_size, dtype=bf16, device=dev)
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
         # When a list, the training path appends (phase, event) pairs recorded on
