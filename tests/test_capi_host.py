@@ -204,6 +204,35 @@ def test_cached_dispatch_entry_points_reject_bad_arguments_on_host():
                                           10**9, None, None) == bad, (src_slot, slot)
 
 
+def test_fp8_and_ordered_entry_points_reject_bad_arguments_on_host():
+    """The FP8 payload, the expert-ordered dispatch and its waiting GEMM check their
+    arguments (no endpoint, bad slot, hidden size, alignment, activation) before any
+    CUDA call and return MOE_ERR_INVALID_ARG."""
+    lib = _lib.load()
+    bad = _lib.MOE_ERR_INVALID_ARG
+    assert lib.moe_ep_dispatch_fp8(None, None, None, None, None, 4, 2, 0, 1, 8, 0, 10**9, None,
+                                   None) == bad
+    assert lib.moe_ep_dispatch_fp8_scatter(None, None, None, None, None, 4, 2, 0, 1, 8, 0, 10**9,
+                                           None, None) == bad
+    assert lib.moe_ep_dispatch_ordered(None, None, None, None, 4, 2, 0, 1, 8, 0, 10**9, None,
+                                       None) == bad
+    assert lib.moe_ep_dispatch_ordered_begin(None, None, None, None, 4, 2, 0, 1, None, None) == bad
+    assert lib.moe_ep_dispatch_ordered_scatter(None, None, None, None, 4, 2, 0, 1, 8, 0, 10**9,
+                                               None, None) == bad
+    for slot, act in ((0, _lib.MOE_ACT_NONE), (2, _lib.MOE_ACT_NONE), (0, _lib.MOE_ACT_DGELU)):
+        assert lib.moe_ep_expert_gemm(None, slot, None, 0, 0, 0, None, 0, 64, act, 148, 1, None,
+                                      10**9, None, None) == bad
+    # quantise / dequantise: hidden not a multiple of 128, strides too small, misaligned
+    assert lib.moe_fp8_quantize(None, 200, 4, 200, None, 200, None, 2, None) == bad
+    assert lib.moe_fp8_quantize(None, 100, 4, 256, None, 256, None, 2, None) == bad
+    assert lib.moe_fp8_quantize(4, 256, 4, 256, 16, 256, 32, 2, None) == bad  # x not 8-aligned
+    assert lib.moe_fp8_dequantize(None, 256, None, 1, None, 4, 256, None, 256, None) == bad
+    assert lib.moe_fp8_dequantize(None, 200, None, 2, None, 4, 200, None, 200, None) == bad
+    # zero rows is a no-op
+    assert lib.moe_fp8_quantize(None, 256, 0, 256, None, 256, None, 2, None) == _lib.MOE_OK
+    assert lib.moe_fp8_dequantize(None, 256, None, 2, None, 0, 256, None, 256, None) == _lib.MOE_OK
+
+
 C_CLIENT = r"""
 #include <stdio.h>
 #include <string.h>
