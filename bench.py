@@ -104,6 +104,9 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--comm-sms", type=int, default=148,
                     help="layer workloads: blocks of the dispatch/combine kernels (one per SM "
                          "by default; they run beside the persistent GEMM CTAs)")
+    ap.add_argument("--placement", choices=["contiguous", "strided"], default="contiguous",
+                    help="layer workloads: which experts each rank holds (contiguous: the "
+                         "reference's sharding; strided: rank r holds r, r+N, ...)")
     ap.add_argument("--solo-blocks", type=int, default=0,
                     help="layer workloads: blocks of the exchange phases that run alone (default "
                          "four per SM)")
@@ -509,6 +512,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                        enable_nvtx=args.nvtx,
                        dispatch_fp8=args.dispatch_fp8,
                        solo_comm_blocks=args.solo_blocks or None,
+                       expert_placement=args.placement,
                        **({} if args.overlap_tiles == "auto"
                           else {"overlap_tiles": args.overlap_tiles == "on"}),
                        ).init_random(std=0.02, seed=0)
@@ -524,7 +528,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
 
     def row_matrix(sel):
         """rows[src, dst] of the assignments in ``sel`` over all ranks."""
-        owner = sel // layer.experts_per_rank
+        owner = layer._slots(sel) // layer.experts_per_rank
         rows_to = torch.bincount(owner[sel >= 0].reshape(-1), minlength=world).double()
         if world > 1:
             gathered = [torch.zeros_like(rows_to) for _ in range(world)]
@@ -683,6 +687,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                    "cuda_graph_note": graph_note,
                    "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                    else "pull",
+                   "expert_placement": args.placement,
                    "overlap_tiles": layer.overlap_tiles, "dispatch_payload":
                        "fp8 e4m3 + per-128 scales" if layer.dispatch_fp8 else "bf16",
                    "comm_sms": args.comm_sms, "gate_bias": bias_info,

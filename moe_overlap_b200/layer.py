@@ -63,6 +63,31 @@ class RouterStats:
     load_cv: float
 
 
+def expert_placement_order(num_experts: int, world: int, placement="contiguous") -> list:
+    """Global expert id held by each placement slot; rank r owns slots
+    [r * E/W, (r + 1) * E/W), in that order, as its local experts.
+
+    ``"contiguous"`` is the reference's sharding (rank r holds experts r*E/W ..,
+    src/train_moe_baseline.py:136-137).  ``"strided"`` deals the experts out like
+    cards (rank r holds r, r + W, r + 2W, ...), which spreads a skew that follows
+    the expert ids (e.g. a Zipf gate with expert 0 hottest) over the ranks.  A
+    sequence gives the order itself (a permutation of the expert ids).
+    """
+    if num_experts % world != 0:
+        raise ValueError(f"num_experts ({num_experts}) must be divisible by world_size ({world})")
+    per = num_experts // world
+    if isinstance(placement, str):
+        if placement == "contiguous":
+            return list(range(num_experts))
+        if placement == "strided":
+            return [le * world + r for r in range(world) for le in range(per)]
+        raise ValueError(f"unknown expert placement {placement!r}")
+    order = [int(e) for e in placement]
+    if sorted(order) != list(range(num_experts)):
+        raise ValueError("an expert placement must be a permutation of the expert ids")
+    return order
+
+
 def random_weights(num_experts: int, hidden: int, ffn: int, std: float = 0.02, seed: int = 0):
     """(router [E, H], w1 [E, F, H], w2 [E, H, F]) fp32 CPU tensors, N(0, std), seeded."""
     g = torch.Generator().manual_seed(seed)
@@ -91,7 +116,8 @@ class MoELayer:
                  max_recv_rows: Optional[int] = None, training: bool = False,
                  taper_chunks: bool = False, fused_combine: Optional[bool] = None,
                  enable_nvtx: bool = False, dispatch_fp8: bool = False,
-                 overlap_tiles: bool = False, solo_comm_blocks: Optional[int] = None):
+                 overlap_tiles: bool = False, solo_comm_blocks: Optional[int] = None,
+                 expert_placement="contiguous"):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         # NVTX ranges named as the reference's (deepep_dispatch_chunk_i,
         # expert_compute_chunk_i, deepep_combine_chunk_i; train_moe_baseline.py:364-413)
@@ -102,7 +128,19 @@ class MoELayer:
         if num_experts % self.world != 0:
             raise ValueError(f"num_routed_experts ({num_experts}) must be divisible by world_size ({self.world})")
         self.experts_per_rank = num_experts // self.world
-        self.expert_offset = self.rank * self.experts_per_rank
+        # Which global experts this rank holds (expert_placement_order); the exchange
+        # sees placement slots, so a non-contiguous placement is a relabelling of the
+        # router's ids before each dispatch, and the weights follow it.
+        order = expert_placement_order(num_experts, self.world, expert_placement)
+        per = self.experts_per_rank
+        self.local_experts = order[self.rank * per:(self.rank + 1) * per]
+        self._slot_of_expert = None
+        if order != list(range(num_experts)):
+            slot_of = [0] * num_experts
+            for slot, e in enumerate(order):
+                slot_of[e] = slot
+            self._slot_of_expert = torch.tensor(slot_of, dtype=torch.int64,
+                                                device=torch.device("cuda", torch.cuda.current_device()))
         self.renormalize = renormalize
         self.micro = max(1, int(micro_batch_size))
         self.taper = taper_chunks
@@ -154,17 +192,16 @@ class MoELayer:
     def init_random(self, std: float = 0.02, seed: int = 0) -> "MoELayer":
         """N(0, std) weights drawn on the CPU: every rank draws all experts and keeps its own."""
         rw, w1, w2 = random_weights(self.num_experts, self.hidden, self.ffn, std, seed)
-        lo, hi = self.expert_offset, self.expert_offset + self.experts_per_rank
+        mine = torch.tensor(self.local_experts, dtype=torch.int64)
         self.router_w.copy_(rw.to(torch.bfloat16))
-        self.w1.copy_(w1[lo:hi].to(torch.bfloat16))
-        self.w2.copy_(w2[lo:hi].to(torch.bfloat16))
+        self.w1.copy_(w1[mine].to(torch.bfloat16))
+        self.w2.copy_(w2[mine].to(torch.bfloat16))
         return self
 
     def load_reference_state_dict(self, sd: dict) -> "MoELayer":
         """Weights from a single-process SimpleMoE state_dict (global expert ids)."""
         self.router_w.copy_(sd["router.weight"].to(torch.bfloat16))
-        for le in range(self.experts_per_rank):
-            e = self.expert_offset + le
+        for le, e in enumerate(self.local_experts):
             self.w1[le].copy_(sd[f"routed_experts.{e}.w1.weight"].to(torch.bfloat16))
             self.w2[le].copy_(sd[f"routed_experts.{e}.w2.weight"].to(torch.bfloat16))
         return self
@@ -180,9 +217,17 @@ class MoELayer:
             logits = torch.matmul(x.to(torch.bfloat16), self.router_w.detach().t())
             return router_topk(logits, self.top_k, bias=self.router_b, renormalize=self.renormalize)
 
+    def _slots(self, idx: torch.Tensor) -> torch.Tensor:
+        """The router's global expert ids as placement slots (unchanged for the
+        reference's contiguous placement; -1 stays -1)."""
+        if self._slot_of_expert is None:
+            return idx
+        return torch.where(idx >= 0, self._slot_of_expert[idx.clamp_min(0)], idx)
+
     def _dispatch(self, xs, idx, w, **kw):
         """One chunk's dispatch: bf16 rows, or with ``dispatch_fp8`` the chunk quantised
         to e4m3 + per-128 scales on the current stream and dispatched in that form."""
+        idx = self._slots(idx)
         if not self.dispatch_fp8:
             return self.dispatcher.dispatch(xs, idx, w, ordered=self.overlap_tiles, **kw)
         kw.pop("timeline", None)
@@ -454,8 +499,8 @@ class MoELayer:
         if x.shape[0] > self.micro:
             raise ValueError("training forward runs the batch as one chunk: raise micro_batch_size")
         x = x.to(torch.bfloat16).contiguous()
-        res = disp.dispatch(x, idx, w.float(), exact_size=False, pad_rows=False, inline=True,
-                            expert_alignment=TRAIN_ALIGNMENT,
+        res = disp.dispatch(x, self._slots(idx), w.float(), exact_size=False, pad_rows=False,
+                            inline=True, expert_alignment=TRAIN_ALIGNMENT,
                             num_sms=self.solo_comm_blocks)
         res.event.current_stream_wait()
         self._mark("fwd_dispatch")

@@ -59,6 +59,17 @@ def main() -> None:
         _lib.check_status(dev)
         assert torch.equal(out2, out), "tile-overlap layer differs from the layer"
     over.close()
+    # Strided expert placement (rank r holds experts r, r + W, ...): the same layer
+    # with its experts dealt out differently, against the same oracle bound.
+    strided = MoELayer(H, Fd, E, K, group=dist.group.WORLD, micro_batch_size=256, num_comm_sms=8,
+                       expert_placement="strided").init_random(seed=11)
+    out3, _ = strided(x.to(dev), routing=(probs, idx, w))
+    torch.cuda.synchronize()
+    _lib.check_status(dev)
+    got3 = bf16_bits_to_f32(to_storage(out3.cpu())).astype(np.float64)
+    diff3 = np.abs(got3 - ref)
+    assert bool(np.all(diff3 <= bound)), float((diff3 / bound).max())
+    strided.close()
     layer.close()
     dist.barrier()
     dist.destroy_process_group()

@@ -159,3 +159,25 @@ def test_forward_timeline_marks_every_phase_in_order(cuda_device):
     for i in range(chunks):
         assert ev[f"gemm{i}_start"].elapsed_time(ev[f"gemm{i}_end"]) >= 0.0
     layer.close()
+
+
+def test_permuted_expert_placement_gives_the_same_output(cuda_device):
+    """A layer holding its experts in another order (relabelled before each dispatch,
+    weights following) computes every row exactly as before: same bits."""
+    from moe_overlap_b200.layer import MoELayer
+
+    tokens, hidden, ffn, experts, topk = 1024, 256, 512, 8, 2
+    g = torch.Generator().manual_seed(51)
+    x = torch.randn(tokens, hidden, generator=g).to(torch.bfloat16).to(cuda_device)
+    base = MoELayer(hidden, ffn, experts, topk, micro_batch_size=512, num_comm_sms=8).init_random(0.05, 8)
+    perm = MoELayer(hidden, ffn, experts, topk, micro_batch_size=512, num_comm_sms=8,
+                    expert_placement=[5, 2, 7, 0, 1, 6, 3, 4]).init_random(0.05, 8)
+    try:
+        routing = base.route(x)
+        want, _ = base(x, routing=routing)
+        got, _ = perm(x, routing=routing)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    finally:
+        base.close()
+        perm.close()

@@ -126,3 +126,24 @@ def test_oracle_topk_takes_the_lowest_ids_for_a_nan_row():
         probs, idx, _ = ol.topk_from_logits(z, 3, renormalize=True)
     assert idx[1].tolist() == [0, 1, 2]
     assert np.isnan(probs[1]).all() and np.isfinite(probs[[0, 2]]).all()
+
+
+def test_expert_placement_orders():
+    """Placement slots -> global experts: the reference's contiguous sharding, the
+    strided one, explicit permutations, and the refusals."""
+    import pytest
+
+    from moe_overlap_b200.layer import expert_placement_order
+
+    assert expert_placement_order(16, 2) == list(range(16))
+    strided = expert_placement_order(16, 4, "strided")
+    assert strided[:4] == [0, 4, 8, 12] and strided[4:8] == [1, 5, 9, 13]
+    assert sorted(strided) == list(range(16))
+    assert expert_placement_order(16, 1, "strided") == list(range(16))
+    assert expert_placement_order(4, 2, [3, 2, 1, 0]) == [3, 2, 1, 0]
+    with pytest.raises(ValueError):
+        expert_placement_order(16, 3)
+    with pytest.raises(ValueError):
+        expert_placement_order(4, 2, [0, 0, 1, 2])
+    with pytest.raises(ValueError):
+        expert_placement_order(4, 2, "round-robin")
