@@ -104,9 +104,11 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--comm-sms", type=int, default=148,
                     help="layer workloads: blocks of the dispatch/combine kernels (one per SM "
                          "by default; they run beside the persistent GEMM CTAs)")
-    ap.add_argument("--placement", choices=["contiguous", "strided"], default="contiguous",
+    ap.add_argument("--placement", choices=["contiguous", "strided", "balanced"],
+                    default="contiguous",
                     help="layer workloads: which experts each rank holds (contiguous: the "
-                         "reference's sharding; strided: rank r holds r, r+N, ...)")
+                         "reference's sharding; strided: rank r holds r, r+N, ...; balanced: "
+                         "longest-first by the gate's target expert shares)")
     ap.add_argument("--solo-blocks", type=int, default=0,
                     help="layer workloads: blocks of the exchange phases that run alone (default "
                          "four per SM)")
@@ -502,6 +504,14 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         bias_info = {"fit": "per-expert, Zipf(1.0) target shares", "iterations": iters,
                      "max_rel_share_error_on_sample": round(err, 3)}
 
+    placement = args.placement
+    if placement == "balanced":
+        from moe_overlap_b200.layer import balanced_placement
+
+        # the gate's target shares: Zipf(1.0) over expert ids with the biased gate, else even
+        shares = [1.0 / (e + 1) for e in range(E)] if cfg["zipf_bias"] else [1.0] * E
+        placement = balanced_placement(shares, world)
+
     def build_layer():
         """Collective: every rank builds the layer (and its dispatcher) together."""
         lay = MoELayer(H, Fd, E, K, group=group, renormalize=cfg["renorm"],
@@ -512,7 +522,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                        enable_nvtx=args.nvtx,
                        dispatch_fp8=args.dispatch_fp8,
                        solo_comm_blocks=args.solo_blocks or None,
-                       expert_placement=args.placement,
+                       expert_placement=placement,
                        **({} if args.overlap_tiles == "auto"
                           else {"overlap_tiles": args.overlap_tiles == "on"}),
                        ).init_random(std=0.02, seed=0)
@@ -687,7 +697,8 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                    "cuda_graph_note": graph_note,
                    "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                    else "pull",
-                   "expert_placement": args.placement,
+                   "expert_placement": args.placement if args.placement != "balanced"
+                   else {"balanced": placement},
                    "overlap_tiles": layer.overlap_tiles, "dispatch_payload":
                        "fp8 e4m3 + per-128 scales" if layer.dispatch_fp8 else "bf16",
                    "comm_sms": args.comm_sms, "gate_bias": bias_info,

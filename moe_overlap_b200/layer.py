@@ -88,6 +88,26 @@ def expert_placement_order(num_experts: int, world: int, placement="contiguous")
     return order
 
 
+def balanced_placement(loads, world: int) -> list:
+    """A placement order (for ``expert_placement``) that evens out the expected rows
+    per rank: experts taken from the heaviest ``loads[e]`` down, each given to the
+    rank with the least load so far among those with a free slot (longest
+    processing time first, E/W experts per rank).  Ties go to the lower rank, so
+    the result is deterministic and the same on every rank."""
+    loads = [float(v) for v in loads]
+    num_experts = len(loads)
+    if world < 1 or num_experts % world != 0:
+        raise ValueError(f"num_experts ({num_experts}) must be divisible by world_size ({world})")
+    per = num_experts // world
+    held = [[] for _ in range(world)]
+    total = [0.0] * world
+    for e in sorted(range(num_experts), key=lambda i: (-loads[i], i)):
+        r = min((r for r in range(world) if len(held[r]) < per), key=lambda r: (total[r], r))
+        held[r].append(e)
+        total[r] += loads[e]
+    return [e for r in range(world) for e in held[r]]
+
+
 def random_weights(num_experts: int, hidden: int, ffn: int, std: float = 0.02, seed: int = 0):
     """(router [E, H], w1 [E, F, H], w2 [E, H, F]) fp32 CPU tensors, N(0, std), seeded."""
     g = torch.Generator().manual_seed(seed)

@@ -147,3 +147,24 @@ def test_expert_placement_orders():
         expert_placement_order(4, 2, [0, 0, 1, 2])
     with pytest.raises(ValueError):
         expert_placement_order(4, 2, "round-robin")
+
+
+def test_balanced_placement_evens_out_zipf_loads():
+    """Longest-first placement of Zipf(1.0) expert loads: every rank gets E/W experts,
+    and the busiest rank's share drops below the contiguous and strided placements'."""
+    from moe_overlap_b200.layer import balanced_placement, expert_placement_order
+
+    loads = [1.0 / (e + 1) for e in range(16)]
+    total = sum(loads)
+
+    def busiest(order, world):
+        per = 16 // world
+        return max(sum(loads[e] for e in order[r * per:(r + 1) * per]) for r in range(world)) / total
+
+    for world in (1, 2, 4, 8):
+        order = balanced_placement(loads, world)
+        assert sorted(order) == list(range(16))
+        assert busiest(order, world) <= busiest(expert_placement_order(16, world), world) + 1e-12
+        assert busiest(order, world) <= busiest(expert_placement_order(16, world, "strided"), world) + 1e-12
+    assert abs(busiest(balanced_placement(loads, 2), 2) - 0.5) < 0.05
+    assert balanced_placement(loads, 2) == balanced_placement(loads, 2)  # deterministic
