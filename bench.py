@@ -480,7 +480,8 @@ def init_group(world: int, device):
 
 
 def measure_layer(args, name: str, rank: int, world: int, device, group, steps: int,
-                  warmup: int, timeline: bool = False, graph_ok: bool = True) -> dict:
+                  warmup: int, timeline: bool = False, graph_ok: bool = True,
+                  placement_override: str | None = None) -> dict:
     """MoE-layer forward (or config 4's forward) over every rank.
 
     Returns the measurement as a dict (the same on every rank; every rank takes
@@ -504,7 +505,8 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         bias_info = {"fit": "per-expert, Zipf(1.0) target shares", "iterations": iters,
                      "max_rel_share_error_on_sample": round(err, 3)}
 
-    placement = args.placement
+    placement_name = placement_override or args.placement
+    placement = placement_name
     if placement == "balanced":
         from moe_overlap_b200.layer import balanced_placement
 
@@ -697,7 +699,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                    "cuda_graph_note": graph_note,
                    "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                    else "pull",
-                   "expert_placement": args.placement if args.placement != "balanced"
+                   "expert_placement": placement_name if placement_name != "balanced"
                    else {"balanced": placement},
                    "overlap_tiles": layer.overlap_tiles, "dispatch_payload":
                        "fp8 e4m3 + per-128 scales" if layer.dispatch_fp8 else "bf16",
@@ -1235,6 +1237,20 @@ def main() -> None:
             ep.pop(key, None)
         extras["ep_layer"] = ep
         torch.cuda.empty_cache()
+        if world > 1:
+            # The same layer with its experts placed by expected load instead of the
+            # reference's contiguous blocks (the Zipf gate puts the hot experts on rank 0).
+            bal = measure_layer(args, "ep_layer", rank, world, device, group,
+                                steps=min(args.steps, 20), warmup=args.warmup,
+                                placement_override="balanced")
+            extras["ep_layer_balanced_placement"] = {
+                k: bal[k] for k in ("value", "unit", "ms_per_step", "ms_per_step_median",
+                                    "communication_hidden_ratio", "serial_phase_ms",
+                                    "expert_gemm_tflops")}
+            extras["ep_layer_balanced_placement"]["config"] = {
+                k: bal["config"][k] for k in ("expert_placement", "rows_received_per_rank",
+                                              "cuda_graph", "parallelism")}
+            torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
