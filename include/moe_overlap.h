@@ -364,13 +364,17 @@ MOE_API int32_t moe_fp8_dequantize(const void* x_fp8, int64_t ldx, const float* 
  * that expert's rows have landed instead of after the whole dispatch.  The same
  * receive layout, metadata, offsets and send positions as moe_ep_dispatch
  * (expert_alignment 1, bf16 rows, no scale_rows); the phases differ in:
- *   ordered_begin    also records, for each of this rank's rows, the (token, slot)
- *                    it carries, and clears this rank's arrival counters of the slot
- *                    (before its count flag is raised, so no peer can add early);
- *   ordered_scatter  every rank pushes its rows expert by expert (local expert
- *                    index first, then owner), and after every few rows adds the
- *                    number delivered to the owner's arrival counter of that
- *                    expert; it also stores each local expert's expected row count;
+ *   ordered_begin    also builds the sending order of this rank's tokens: by the
+ *                    earliest of each token's experts in the walk (local expert
+ *                    index first, then owner), and clears this rank's arrival
+ *                    counters of the slot (before its count flag is raised, so no
+ *                    peer can add early);
+ *   ordered_scatter  every rank pushes its tokens in that order, each token's rows
+ *                    to all their owners from one read of the token, and after
+ *                    every batch of tokens adds the rows delivered to the owners'
+ *                    arrival counters of those experts; it also stores each local
+ *                    expert's expected row count.  It takes the tokens of the
+ *                    slot's last ordered_begin (MOE_ERR_INVALID_ARG otherwise);
  *   end              moe_ep_dispatch_end (all rows landed), as before.
  * moe_ep_dispatch_ordered runs the three.  No counterpart in DeepEP, whose
  * receiver learns of rows only through its per-channel queues.

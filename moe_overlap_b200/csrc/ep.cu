@@ -118,7 +118,11 @@ struct Endpoint {
   CUtensorMap* d_cb_maps = nullptr; // [2][world] TMA store maps of every rank's cb (per slot)
   int32_t* offsets[2] = {};         // [per_rank+1] receiver expert offsets
   int32_t* my_counts = nullptr;     // [E]
-  int32_t* order = nullptr;         // [max_tokens*max_topk] assignment of each cb row
+  int32_t* order = nullptr;         // [max_tokens] tokens in the expert-ordered sending order
+  int32_t* token_key = nullptr;     // [max_tokens] sending key of each token
+  int32_t* key_count = nullptr;     // [E+1] tokens per sending key
+  int32_t* key_cursor = nullptr;    // [E+1] tokens placed per key
+  int32_t ordered_tokens[2] = {-1, -1};  // tokens of the slot's last ordered begin, else -1
   int32_t* expected[2] = {};        // [per_rank] rows of each local expert (before alignment)
   unsigned int* done_ctr = nullptr; // blocks finished in the current scatter
   uint64_t* epoch_ctr = nullptr;    // device-side epoch counter (epoch 0 = use it)
@@ -154,7 +158,10 @@ struct Params {
   int32_t* cb_pos;
   int32_t* offsets_out;
   int32_t* my_counts;
-  int32_t* order;        // expert-ordered dispatch: assignment of each of this rank's cb rows
+  int32_t* order;        // expert-ordered dispatch: this rank's tokens in sending order
+  int32_t* token_key;    // expert-ordered dispatch: sending key of each token
+  int32_t* key_count;    // [E + 1] tokens per key, then
+  int32_t* key_cursor;   // [E + 1] tokens placed per key
   int32_t* expected_out; // expert-ordered dispatch: rows of each local expert, for the GEMM
   int ordered;           // count phase: also build `order` and clear the arrival counters
   unsigned int* done_ctr;
@@ -287,6 +294,10 @@ __global__ void count_kernel(Params p) {
     // from zero, before any peer can see the count flag raised below.
     uint32_t* arrived = at<uint32_t>(p.peers[p.rank], p.lay.arrived) + p.slot * p.per_rank;
     for (int le = threadIdx.x; le < p.per_rank; le += blockDim.x) arrived[le] = 0;
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+      p.key_count[i] = 0;
+      p.key_cursor[i] = 0;
+    }
   }
   for (int d = 0; d < p.world; ++d) {
     int32_t* dst = at<int32_t>(p.peers[d], slot_of(p).counts) + p.rank * E;
@@ -300,19 +311,44 @@ __global__ void count_kernel(Params p) {
   }
 }
 
-// Expert-ordered dispatch: the assignment behind each of this rank's cb rows
-// (global expert order, then (token, slot) order), so that the scatter can walk
-// its rows expert by expert.  One thread per assignment; each block first forms
-// the exclusive prefix of this rank's per-expert counts (one warp scan).
-__global__ void __launch_bounds__(256) order_kernel(Params p) {
-  __shared__ int base_sh[kMaxExperts];
-  const int E = p.num_experts;
+// Expert-ordered dispatch, sending order.  A token's key is the earliest position,
+// in the walk (local expert index first, then owner: e -> (e % per_rank) * W + e / per_rank),
+// of the experts it was routed to; the scatter sends tokens by increasing key, so
+// every token of the walk's first expert goes first, and an expert's rows are all
+// sent once the tokens of its key (and of the keys before it) are.  Tokens with no
+// expert get key E.  One thread per token; the per-key counts are atomics into
+// arrays the count phase zeroed.
+__device__ __forceinline__ int walk_key(const Params& p, int t) {
+  int key = p.num_experts;
+  for (int j = 0; j < p.topk; ++j) {
+    const int64_t v = p.topk_idx[static_cast<int64_t>(t) * p.topk + j];
+    if (v < 0 || v >= p.num_experts) continue;
+    const int e = static_cast<int>(v);
+    key = min(key, (e % p.per_rank) * p.world + e / p.per_rank);
+  }
+  return key;
+}
+
+__global__ void __launch_bounds__(256) token_key_kernel(Params p) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.num_tokens) return;
+  const int key = walk_key(p, t);
+  p.token_key[t] = key;
+  atomicAdd(p.key_count + key, 1);
+}
+
+// Places each token at (first position of its key) + (its arrival among the key's
+// tokens); the order within a key is free (it changes only when rows are sent, not
+// where they land).  Each block forms the exclusive prefix of the E + 1 key counts.
+__global__ void __launch_bounds__(256) token_order_kernel(Params p) {
+  __shared__ int base_sh[kMaxExperts + 1];
+  const int n = p.num_experts + 1;
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
-    const int per = (E + 31) / 32;
-    const int beg = min(E, lane * per), end = min(E, beg + per);
+    const int per = (n + 31) / 32;
+    const int beg = min(n, lane * per), end = min(n, beg + per);
     int local = 0;
-    for (int e = beg; e < end; ++e) local += p.my_counts[e];
+    for (int i = beg; i < end; ++i) local += p.key_count[i];
     int incl = local;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -320,19 +356,16 @@ __global__ void __launch_bounds__(256) order_kernel(Params p) {
       if (lane >= d) incl += v;
     }
     int run = incl - local;
-    for (int e = beg; e < end; ++e) {
-      base_sh[e] = run;
-      run += p.my_counts[e];
+    for (int i = beg; i < end; ++i) {
+      base_sh[i] = run;
+      run += p.key_count[i];
     }
   }
   __syncthreads();
-  const int a = blockIdx.x * blockDim.x + threadIdx.x;
-  if (a >= p.num_tokens * p.topk) return;
-  const int64_t v = p.topk_idx[a];
-  if (v < 0 || v >= E) return;
-  const int e = static_cast<int>(v);
-  const int blk = a / kAssignPerLayoutBlock;
-  p.order[base_sh[e] + p.block_hist[blk * E + e] + p.rank_in_block[a]] = a;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.num_tokens) return;
+  const int key = p.token_key[t];
+  p.order[base_sh[key] + atomicAdd(p.key_cursor + key, 1)] = t;
 }
 
 __device__ __forceinline__ uint4 scale_bf16x8(const uint4& v, float s) {
@@ -567,48 +600,34 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_kernel(P
 }
 
 // ------------------------------------------------------ expert-ordered scatter --
-// The same rows, receive layout and metadata as scatter_kernel, pushed expert by
-// expert so that an owner can start multiplying an expert's rows as soon as they
-// have all landed, while later experts are still in flight.  Each rank walks its
-// rows (the cb order: global expert, then (token, slot)) with its experts visited
-// in (local expert, owner) order, so every owner's first expert goes first.  A
-// block copies a contiguous range of that walk in batches of up to 64 rows, then
-// fences and adds, per expert among them, the number of rows it delivered to the
-// owner's arrival counter of that local expert (a system-scope atomic over NVLink).  The owner's GEMM waits until a
+// The same rows, receive layout and metadata as scatter_kernel, sent in an order
+// that finishes experts early, so that an owner can start multiplying an expert's
+// rows as soon as they have all landed while later experts are still in flight.
+// Tokens go by increasing walk key (token_key_kernel), in batches of up to 64
+// tokens dealt round-robin to the blocks; a warp pushes one token's rows to all its
+// owners from one load of the row, as the token-order scatter does; after each
+// batch the block fences once and adds, per expert, the rows it delivered to the
+// owner's arrival counter of that local expert (system-scope atomics over NVLink).  The owner's GEMM waits until a
 // counter reaches that expert's row count (moe_ep_expert_gemm).
-constexpr int kOrderedBatch = 64;  // rows per lookup / fence batch of a block
+constexpr int kOrderedBatch = 64;  // tokens per lookup / fence batch of a block
 
 __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_kernel(Params p) {
   __shared__ CountView cv;
-  __shared__ int vbase[kMaxExperts + 1];  // first walk position of each (local expert, owner) segment
-  __shared__ int vexp[kMaxExperts];       // global expert of each segment
-  __shared__ int batch_seg[kOrderedBatch], batch_off[kOrderedBatch], batch_a[kOrderedBatch];
-  __shared__ float batch_w[kOrderedBatch];
+  __shared__ int batch_tok[kOrderedBatch];
+  __shared__ int batch_cnt[kMaxExperts];  // rows of each expert sent in this batch
   if (threadIdx.x == 0) {
     cv.overflow = 0;
     cv.fail = 0;
     cv.recv_total = 0;
   }
+  const int E = p.num_experts;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) batch_cnt[e] = 0;
   __syncthreads();
   if (!wait_all_flags(p, p.lay.count_flag, &cv.fail)) {
     if (threadIdx.x == 0) record_status(p.status, MOE_ERR_TIMEOUT);
     return;
   }
   build_count_view(p, cv);
-  const int E = p.num_experts;
-  if (threadIdx.x == 0) {
-    const int32_t* mine = at<const int32_t>(p.peers[p.rank], slot_of(p).counts) + p.rank * E;
-    int run = 0, seg = 0;
-    for (int le = 0; le < p.per_rank; ++le)
-      for (int d = 0; d < p.world; ++d, ++seg) {
-        const int e = d * p.per_rank + le;
-        vbase[seg] = run;
-        vexp[seg] = e;
-        run += mine[e];
-      }
-    vbase[E] = run;
-  }
-  __syncthreads();
   const bool overflow = cv.overflow != 0;
   if (blockIdx.x == 0 && threadIdx.x == 0 && overflow) record_status(p.status, MOE_ERR_CAPACITY);
   if (blockIdx.x == 0) {
@@ -625,96 +644,86 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) scatter_ordered_
     }
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int warps_total = gridDim.x * (kCommThreads / 32);
   const int nvec = p.hidden / 8;
   const SlotLayout sl = slot_of(p);
-  const int total_rows = vbase[E];
   if (!overflow) {
-    // Each block walks one contiguous range of the walk, in batches of up to
-    // kOrderedBatch rows: the batch's lookups first (one thread per row), then the
-    // rows (one warp per row), then one fence and, per expert in the batch, one
-    // arrival add on the owner.  Low-numbered blocks hold the first experts.
-    const int per_block = (total_rows + gridDim.x - 1) / gridDim.x;
-    const int v_begin = min(total_rows, static_cast<int>(blockIdx.x) * per_block);
-    const int v_end = min(total_rows, v_begin + per_block);
-    for (int vb = v_begin; vb < v_end; vb += kOrderedBatch) {
-      const int n = min(kOrderedBatch, v_end - vb);
-      if (threadIdx.x < n) {
-        const int v = vb + threadIdx.x;
-        int lo = 0;
-        for (int hi = E; hi - lo > 1;) {  // vbase[lo] <= v < vbase[lo + 1]
-          const int mid = (lo + hi) >> 1;
-          if (vbase[mid] <= v) lo = mid; else hi = mid;
-        }
-        const int off = v - vbase[lo];
-        const int a = p.order[cv.my_base[vexp[lo]] + off];
-        batch_seg[threadIdx.x] = lo;
-        batch_off[threadIdx.x] = off;
-        batch_a[threadIdx.x] = a;
-        batch_w[threadIdx.x] = p.topk_w[a];
-      }
+    // Batches are dealt round-robin, so the grid as a whole sweeps the sending order
+    // front to back and the walk's first experts complete first.  A batch is a
+    // multiple of the block's warps, just large enough for every block to have one.
+    constexpr int kWarps = kCommThreads / 32;
+    const int per_warp = (p.num_tokens + gridDim.x * kWarps - 1) / (gridDim.x * kWarps);
+    const int batch = min(kOrderedBatch, kWarps * max(1, per_warp));
+    for (int tb = blockIdx.x * batch; tb < p.num_tokens; tb += gridDim.x * batch) {
+      const int n = min(batch, p.num_tokens - tb);
+      if (threadIdx.x < n) batch_tok[threadIdx.x] = p.order[tb + threadIdx.x];
       __syncthreads();
-      for (int r = warp; r < n; r += kCommThreads / 32) {
-        const int e = vexp[batch_seg[r]];
-        const int off = batch_off[r];
-        const int a = batch_a[r];
-        const int cb_row = cv.my_base[e] + off;
-        const int t = a / p.topk, j = a - t * p.topk;
-        const int d = e / p.per_rank;
-        const int row = cv.exp_base[e] + cv.my_prefix[e] + off;
-        uint8_t* peer = p.peers[d];
-        if (lane < p.topk) {
-          at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
-              (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
-          at<float>(peer, sl.topk_w)[static_cast<int64_t>(row) * p.max_topk + lane] =
-              (lane == j) ? batch_w[r] : 0.0f;
-        }
-        if (lane == 0) {
-          at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
-          at<int32_t>(peer, sl.dst)[row] = cb_row;
-          p.send_pos[a] = row;
-          p.cb_pos[a] = cb_row;
-        }
+      for (int r = warp; r < n; r += kWarps) {
+        const int t = batch_tok[r];
+        if (t < 0 || t >= p.num_tokens) continue;  // the order array is the begin's, for these tokens
         const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(t) * p.hidden);
-        uint4* dst = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
-        constexpr int U = 8;  // a 4 KB row in one pass
-        for (int base = 0; base < nvec; base += 32 * U) {
-          uint4 vv[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int i = base + u * 32 + lane;
-            if (i < nvec) vv[u] = __ldg(src + i);
+        uint4* dst[8];
+        int nd = 0;
+        for (int j = 0; j < p.topk; ++j) {
+          const int a = t * p.topk + j;
+          const int64_t ev = p.topk_idx[a];
+          if (ev < 0 || ev >= E) {
+            if (lane == 0) p.send_pos[a] = -1;
+            continue;
           }
+          const int e = static_cast<int>(ev);
+          const int d = e / p.per_rank;
+          const int blk = a / kAssignPerLayoutBlock;
+          const int row = cv.exp_base[e] + cv.my_prefix[e] + p.block_hist[blk * E + e] +
+                          p.rank_in_block[a];
+          uint8_t* peer = p.peers[d];
+          dst[nd++] = at<uint4>(peer, sl.recv_x) + static_cast<int64_t>(row) * nvec;
+          if (lane < p.topk) {
+            at<int64_t>(peer, sl.topk_idx)[static_cast<int64_t>(row) * p.max_topk + lane] =
+                (lane == j) ? static_cast<int64_t>(e - d * p.per_rank) : -1;
+            at<float>(peer, sl.topk_w)[static_cast<int64_t>(row) * p.max_topk + lane] =
+                (lane == j) ? p.topk_w[a] : 0.0f;
+          }
+          if (lane == 0) {
+            const int cb_row = cv.my_base[e] + p.block_hist[blk * E + e] + p.rank_in_block[a];
+            at<int2>(peer, sl.src)[row] = make_int2(p.rank, t);
+            at<int32_t>(peer, sl.dst)[row] = cb_row;
+            p.send_pos[a] = row;
+            p.cb_pos[a] = cb_row;
+            atomicAdd_block(batch_cnt + e, 1);
+          }
+        }
+        constexpr int U = 4;
+        for (int base = 0; base < nvec; base += 32 * U) {
+          uint4 v[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int i = base + u * 32 + lane;
-            if (i < nvec) dst[i] = vv[u];
+            if (i < nvec) v[u] = __ldg(src + i);
+          }
+          for (int q = 0; q < nd; ++q) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int i = base + u * 32 + lane;
+              if (i < nvec) dst[q][i] = v[u];
+            }
           }
         }
       }
       // The batch's rows are visible everywhere before their owners count them.
       __threadfence_system();
       __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence_system();
-        for (int r = 0; r < n;) {
-          int m = 1;
-          while (r + m < n && batch_seg[r + m] == batch_seg[r]) ++m;
-          const int e = vexp[batch_seg[r]];
+      for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int c = batch_cnt[e];
+        if (c > 0) {
           const int d = e / p.per_rank;
+          __threadfence_system();
           atomicAdd_system(at<unsigned int>(p.peers[d], p.lay.arrived) + p.slot * p.per_rank +
                                (e - d * p.per_rank),
-                           static_cast<unsigned int>(m));
-          r += m;
+                           static_cast<unsigned int>(c));
+          batch_cnt[e] = 0;
         }
       }
-      __syncthreads();  // the next batch reuses the batch arrays
-    }
-    // (token, slot) pairs with no expert: no receive row.
-    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < p.num_tokens * p.topk;
-         a += gridDim.x * blockDim.x) {
-      const int64_t ev = p.topk_idx[a];
-      if (ev < 0 || ev >= E) p.send_pos[a] = -1;
+      __syncthreads();  // the next batch reuses batch_tok and batch_cnt
     }
     if (p.pad_rows) {
       uint8_t* me = p.peers[p.rank];
@@ -1164,6 +1173,10 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   off = align_up(off + uint64_t(num_experts) * 4, 256);
   const uint64_t o_order = off;
   off = align_up(off + uint64_t(assigns) * 4, 256);
+  const uint64_t o_tkey = off;
+  off = align_up(off + uint64_t(std::max(1, max_tokens)) * 4, 256);
+  const uint64_t o_kcount = off;
+  off = align_up(off + uint64_t(num_experts + 1) * 8, 256);  // counts, then cursors
   uint64_t o_expected[2];
   for (int s = 0; s < 2; ++s) {
     o_expected[s] = off;
@@ -1203,6 +1216,9 @@ extern "C" int32_t moe_ep_create(int32_t rank, int32_t world, int32_t num_expert
   }
   ep->my_counts = reinterpret_cast<int32_t*>(ep->scratch + o_cnt);
   ep->order = reinterpret_cast<int32_t*>(ep->scratch + o_order);
+  ep->token_key = reinterpret_cast<int32_t*>(ep->scratch + o_tkey);
+  ep->key_count = reinterpret_cast<int32_t*>(ep->scratch + o_kcount);
+  ep->key_cursor = ep->key_count + (num_experts + 1);
   for (int s = 0; s < 2; ++s) ep->expected[s] = reinterpret_cast<int32_t*>(ep->scratch + o_expected[s]);
   ep->done_ctr = reinterpret_cast<unsigned int*>(ep->scratch + o_done);
   ep->epoch_ctr = reinterpret_cast<uint64_t*>(ep->scratch + o_done + 8);
@@ -1313,7 +1329,11 @@ static int32_t dispatch_begin_impl(moe_ep_t ep, const void* x, const int64_t* to
   p.rank_in_block = ep->rank_in_block;
   p.my_counts = ep->my_counts;
   p.order = ep->order;
+  p.token_key = ep->token_key;
+  p.key_count = ep->key_count;
+  p.key_cursor = ep->key_cursor;
   p.ordered = ordered ? 1 : 0;
+  ep->ordered_tokens[slot] = ordered ? num_tokens : -1;
   const int64_t assigns = int64_t(num_tokens) * topk;
   p.num_layout_blocks = static_cast<int>((assigns + kAssignPerLayoutBlock - 1) / kAssignPerLayoutBlock);
   if (p.num_layout_blocks > 0) {
@@ -1322,7 +1342,11 @@ static int32_t dispatch_begin_impl(moe_ep_t ep, const void* x, const int64_t* to
   }
   count_kernel<<<1, 256, 0, stream>>>(p);
   if (int rc = check_launch(); rc != MOE_OK || !ordered || assigns == 0) return rc;
-  order_kernel<<<static_cast<int>((assigns + 255) / 256), 256, 0, stream>>>(p);
+  const int tok_blocks = static_cast<int>((int64_t(num_tokens) + 255) / 256);
+  if (tok_blocks == 0) return MOE_OK;
+  token_key_kernel<<<tok_blocks, 256, 0, stream>>>(p);
+  if (int rc = check_launch(); rc != MOE_OK) return rc;
+  token_order_kernel<<<tok_blocks, 256, 0, stream>>>(p);
   return check_launch();
 }
 
@@ -1353,6 +1377,8 @@ extern "C" int32_t moe_ep_dispatch_ordered_scatter(moe_ep_t ep, const void* x, c
       (num_tokens > 0 && (x == nullptr || topk_idx == nullptr || topk_weights == nullptr)) ||
       !moe::aligned16(x))
     return MOE_ERR_INVALID_ARG;
+  // The sending order is the one the slot's ordered begin built for these tokens.
+  if (ep->ordered_tokens[slot] != num_tokens) return MOE_ERR_INVALID_ARG;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   Params p = base_params(ep, slot, epoch, wait_ns, status);
   p.x = static_cast<const __nv_bfloat16*>(x);
@@ -1360,6 +1386,8 @@ extern "C" int32_t moe_ep_dispatch_ordered_scatter(moe_ep_t ep, const void* x, c
   p.topk_w = topk_weights;
   p.num_tokens = num_tokens;
   p.topk = topk;
+  p.block_hist = ep->block_hist;
+  p.rank_in_block = ep->rank_in_block;
   p.send_pos = ep->send_pos[slot];
   p.cb_pos = ep->cb_pos[slot];
   p.offsets_out = ep->offsets[slot];

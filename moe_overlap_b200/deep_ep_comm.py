@@ -225,8 +225,9 @@ class DeepEPDispatcher:
                  timeline: Optional[list] = None, ordered: bool = False) -> DispatchResult:
         """Sends each token's row to the ranks owning its top-k experts.
 
-        With ``ordered`` the rows travel expert by expert and each owner counts,
-        per local expert, the rows that have landed; ``extra["scatter_event"]`` of
+        With ``ordered`` the tokens travel sorted by the earliest of their experts
+        (local expert index first, then owner), so experts complete in that order,
+        and each owner counts, per local expert, the rows that have landed; ``extra["scatter_event"]`` of
         the result marks the end of this rank's sending, and ``expert_gemm`` enqueued
         behind it starts each expert's tiles as soon as that expert's rows are all
         here (``event`` still marks every row landed).  Same rows, layout and

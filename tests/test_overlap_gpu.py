@@ -129,6 +129,28 @@ def test_expert_gemm_wait_that_nobody_satisfies_times_out(cuda_device, monkeypat
         grp.close()
 
 
+def test_ordered_scatter_requires_the_slots_ordered_begin(cuda_device):
+    """The ordered scatter sends the order its begin built: after a plain begin on the
+    slot, or with another token count, it is refused on the host before any launch."""
+    world, tokens, topk, num_experts, hidden = 1, 128, 2, 8, 128
+    xs, idxs, ws = _routing(world, tokens, num_experts, topk, 4, hidden)
+    grp = LocalGroup(world, num_experts, hidden, tokens, topk, tokens * topk, num_blocks=4)
+    try:
+        ep = grp.eps[0]
+        x, i, w = xs[0].to(cuda_device), idxs[0].to(cuda_device), ws[0].to(cuda_device)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        ep.dispatch_begin(x, i, w, 0, 1, status)
+        with pytest.raises(_lib.MoeError):
+            ep.dispatch_ordered_scatter(x, i, w, 0, 1, 4, False, grp.wait_ns, status)
+        ep.dispatch_ordered_begin(x, i, w, 1, 1, status)
+        with pytest.raises(_lib.MoeError):
+            ep.dispatch_ordered_scatter(x[:64], i[:64], w[:64], 1, 1, 4, False, grp.wait_ns, status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+    finally:
+        grp.close()
+
+
 def test_layer_with_tile_overlap_equals_layer_without(cuda_device):
     from moe_overlap_b200.layer import MoELayer
 
