@@ -112,6 +112,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--solo-blocks", type=int, default=0,
                     help="layer workloads: blocks of the exchange phases that run alone (default "
                          "four per SM)")
+    ap.add_argument("--gemm-streams", type=int, choices=[1, 2], default=2,
+                    help="layer workloads: compute streams the forward's chunks alternate over")
     ap.add_argument("--micro-batch", type=int, default=4096,
                     help="layer workloads: tokens per pipelined chunk")
     ap.add_argument("--no-graph", action="store_true",
@@ -525,6 +527,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                        dispatch_fp8=args.dispatch_fp8,
                        solo_comm_blocks=args.solo_blocks or None,
                        expert_placement=placement,
+                       gemm_streams=args.gemm_streams,
                        **({} if args.overlap_tiles == "auto"
                           else {"overlap_tiles": args.overlap_tiles == "on"}),
                        ).init_random(std=0.02, seed=0)
@@ -701,7 +704,8 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                    else "pull",
                    "expert_placement": placement_name if placement_name != "balanced"
                    else {"balanced": placement},
-                   "overlap_tiles": layer.overlap_tiles, "dispatch_payload":
+                   "overlap_tiles": layer.overlap_tiles,
+                   "gemm_streams": len(layer.compute_streams), "dispatch_payload":
                        "fp8 e4m3 + per-128 scales" if layer.dispatch_fp8 else "bf16",
                    "comm_sms": args.comm_sms, "gate_bias": bias_info,
                    "realised_expert_share": [round(v, 4) for v in realised_share],

@@ -137,7 +137,7 @@ class MoELayer:
                  taper_chunks: bool = False, fused_combine: Optional[bool] = None,
                  enable_nvtx: bool = False, dispatch_fp8: bool = False,
                  overlap_tiles: bool = False, solo_comm_blocks: Optional[int] = None,
-                 expert_placement="contiguous"):
+                 expert_placement="contiguous", gemm_streams: int = 2):
         self.hidden, self.ffn, self.num_experts, self.top_k = hidden_size, ffn_size, num_experts, top_k
         # NVTX ranges named as the reference's (deepep_dispatch_chunk_i,
         # expert_compute_chunk_i, deepep_combine_chunk_i; train_moe_baseline.py:364-413)
@@ -197,13 +197,23 @@ class MoELayer:
         self.dispatcher = DeepEPDispatcher(group, hidden_size, num_experts, num_sms=num_comm_sms,
                                            max_tokens_per_rank=self.micro, max_top_k=top_k,
                                            max_recv_rows=max_recv_rows, exact_size=False)
-        self.compute_stream = torch.cuda.Stream(dev)
+        # The forward's chunks alternate over ``gemm_streams`` compute streams (1 or 2),
+        # each with its own GEMM1 output and work counter, so the next chunk's GEMM1
+        # can take the SMs that the last wave of this chunk's GEMM2 leaves idle.
+        if gemm_streams not in (1, 2):
+            raise ValueError("gemm_streams must be 1 or 2")
+        if training:
+            gemm_streams = 1  # the training step is one chunk
+        self.compute_streams = [torch.cuda.Stream(dev) for _ in range(gemm_streams)]
+        self.compute_stream = self.compute_streams[0]
         self.gemm_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         # Exchange blocks when nothing runs beside them (the training path waits for
         # each exchange phase): four 128-thread blocks per SM.
         self.solo_comm_blocks = int(solo_comm_blocks) if solo_comm_blocks else 4 * self.gemm_sms
-        self.h = torch.empty(self.dispatcher.max_recv_rows, ffn_size, dtype=bf16, device=dev)
-        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.hs = [torch.empty(self.dispatcher.max_recv_rows, ffn_size, dtype=bf16, device=dev)
+                   for _ in range(gemm_streams)]
+        self.counters = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(gemm_streams)]
+        self.h, self.counter = self.hs[0], self.counters[0]
         # When a list, the training path appends (phase, event) pairs recorded on
         # the compute stream at each phase boundary (for per-phase device times).
         self.trace: Optional[list] = None
@@ -253,30 +263,32 @@ class MoELayer:
         kw.pop("timeline", None)
         return self.dispatcher.dispatch_fp8(quantize_fp8(xs), idx, w, **kw)
 
-    def _experts(self, res) -> Optional[torch.Tensor]:
-        """GEMM1 (+GELU) and GEMM2 on the current stream.
+    def _experts(self, res, buf: int = 0) -> Optional[torch.Tensor]:
+        """GEMM1 (+GELU) and GEMM2 on the current stream, through GEMM1 output and
+        work counter ``buf`` (the compute stream's own).
 
         With ``fused_combine`` GEMM2's epilogue pushes each row straight to its
         source rank (DeepEPDispatcher.expert_gemm_push) and None is returned;
         otherwise the expert-output rows are written locally and returned.
         An FP8 receive payload is first dequantised into the slot's expert-output
         rows, which GEMM1 reads before GEMM2 overwrites them."""
-        kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counter)
+        h = self.hs[buf]
+        kw = dict(num_sms=self.gemm_sms, use_atomic_queue=self.use_atomic, work_counter=self.counters[buf])
         a = res.recv_x
         if isinstance(a, tuple):
             buf = self.dispatcher.expert_out_buffer(res.handle)
             a = dequantize_fp8(a[0], a[1], out=buf[:a[0].shape[0]], rows=res.expert_offsets[-1:])
         if getattr(res.handle, "ordered", False):
-            self.dispatcher.expert_gemm(res.handle, self.w1.transpose(1, 2), self.h,
+            self.dispatcher.expert_gemm(res.handle, self.w1.transpose(1, 2), h,
                                         activation="gelu", **kw)
         else:
-            grouped_gemm(a, self.w1.transpose(1, 2), res.expert_offsets, out=self.h,
+            grouped_gemm(a, self.w1.transpose(1, 2), res.expert_offsets, out=h,
                          activation="gelu", **kw)
         if self.fused_combine:
-            self.dispatcher.expert_gemm_push(self.h, self.w2.transpose(1, 2), res.handle, **kw)
+            self.dispatcher.expert_gemm_push(h, self.w2.transpose(1, 2), res.handle, **kw)
             return None
         y = self.dispatcher.expert_out_buffer(res.handle)
-        grouped_gemm(self.h, self.w2.transpose(1, 2), res.expert_offsets, out=y, **kw)
+        grouped_gemm(h, self.w2.transpose(1, 2), res.expert_offsets, out=y, **kw)
         return y
 
     def _combine(self, y, handle, **kw):
@@ -340,14 +352,16 @@ class MoELayer:
             # Enqueue this chunk's GEMMs before the next chunk's dispatch: the GPU
             # starts them as soon as this chunk's rows have landed, and the host
             # time spent enqueuing the next dispatch overlaps them.
-            with torch.cuda.stream(self.compute_stream), nvtx_range(f"expert_compute_chunk_{i}", nv):
+            buf = i % len(self.compute_streams)
+            cs = self.compute_streams[buf]
+            with torch.cuda.stream(cs), nvtx_range(f"expert_compute_chunk_{i}", nv):
                 # An ordered dispatch's GEMM may start once this rank's rows are sent.
                 cur.extra.get("scatter_event", cur.event).current_stream_wait()
-                self._timeline_mark(timeline, f"gemm{i}_start", self.compute_stream)
-                y = self._experts(cur)
-                self._timeline_mark(timeline, f"gemm{i}_end", self.compute_stream)
+                self._timeline_mark(timeline, f"gemm{i}_start", cs)
+                y = self._experts(cur, buf)
+                self._timeline_mark(timeline, f"gemm{i}_end", cs)
                 done = torch.cuda.Event()
-                done.record(self.compute_stream)
+                done.record(cs)
             nxt = None
             if i + 1 < len(chunks):
                 ns, ne = chunks[i + 1]

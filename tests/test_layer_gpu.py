@@ -181,3 +181,29 @@ def test_permuted_expert_placement_gives_the_same_output(cuda_device):
     finally:
         base.close()
         perm.close()
+
+
+def test_one_and_two_gemm_streams_give_the_same_output(cuda_device):
+    """The forward's chunks on one compute stream or alternating over two (each with
+    its own GEMM1 output and work counter): same bits, over several forwards so that
+    chunks reuse both streams' buffers and both dispatch slots."""
+    from moe_overlap_b200.layer import MoELayer
+
+    tokens, hidden, ffn, experts, topk = 1300, 256, 512, 8, 2
+    g = torch.Generator().manual_seed(61)
+    x = torch.randn(tokens, hidden, generator=g).to(torch.bfloat16).to(cuda_device)
+    one = MoELayer(hidden, ffn, experts, topk, micro_batch_size=256, num_comm_sms=8,
+                   gemm_streams=1).init_random(0.05, 9)
+    two = MoELayer(hidden, ffn, experts, topk, micro_batch_size=256, num_comm_sms=8,
+                   gemm_streams=2).init_random(0.05, 9)
+    try:
+        assert len(two.compute_streams) == 2 and two.hs[0].data_ptr() != two.hs[1].data_ptr()
+        routing = one.route(x)
+        want, _ = one(x, routing=routing)
+        for _ in range(3):
+            got, _ = two(x, routing=routing)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want)
+    finally:
+        one.close()
+        two.close()
