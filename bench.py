@@ -628,6 +628,10 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     step_ms, median_ms = float(t[0].item()), float(t[1].item())
     graph_used = graph is not None
+    # Kernels launched in the timed region: one replay launches the captured graph's
+    # kernel nodes (counted by name after capture); eager steps are not counted.
+    kernels_per_step = graph.kernel_counts if graph is not None else None
+    gpu_launches = kernels_per_step["ours"] * steps if kernels_per_step else None
     del graph
 
     marks_by_rank = None
@@ -700,6 +704,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                    "chunks": [e - s for s, e in layer.chunk_plan(T)],
                    "cuda_graph": graph_used,
                    "cuda_graph_note": graph_note,
+                   "kernels_per_step": kernels_per_step,
                    "combine": "push (fused into the down-projection GEMM)" if layer.fused_combine
                    else "pull",
                    "expert_placement": placement_name if placement_name != "balanced"
@@ -723,6 +728,7 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
                                                   / PEER_COPY_GBPS / 1e6, 4) if world > 1 else None,
         },
         "clocks": clocks,
+        "gpu_launches": gpu_launches,
     }
     if marks_by_rank is not None:
         result["timeline_ms"] = {f"rank{r}": m for r, m in enumerate(marks_by_rank)}
@@ -754,7 +760,7 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> None:
     if rank == 0:
         line = {**res, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
-                "warmup": args.warmup, "gpu_launches_per_step": None}
+                "warmup": args.warmup}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -931,7 +937,11 @@ def run_layer_train(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": args.workload, "description": cfg["desc"], "tokens_per_rank": T,
                        "comm_sms": args.comm_sms, "l2": "working set (weights 1 GiB, activations) > L2",
                        "cuda_graph": graph is not None, "cuda_graph_note": graph_note,
+                       "kernels_per_step": graph.kernel_counts if graph is not None else None,
                        "parallelism": "replicas" if world > 1 else "single"},
+            # kernels of this library in the timed region (graph replays only)
+            "gpu_launches": (graph.kernel_counts["ours"] * args.steps
+                             if graph is not None and graph.kernel_counts else None),
             "expert_load_cv": round(stats.load_cv, 4),
             "router_entropy": round(stats.entropy, 4),
             "roofline": {"bound": "tensor", "scope": "whole step, expert GEMM FLOPs only",
@@ -1250,10 +1260,10 @@ def main() -> None:
             extras["ep_layer_balanced_placement"] = {
                 k: bal[k] for k in ("value", "unit", "ms_per_step", "ms_per_step_median",
                                     "communication_hidden_ratio", "serial_phase_ms",
-                                    "expert_gemm_tflops")}
+                                    "expert_gemm_tflops", "gpu_launches")}
             extras["ep_layer_balanced_placement"]["config"] = {
                 k: bal["config"][k] for k in ("expert_placement", "rows_received_per_rank",
-                                              "cuda_graph", "parallelism")}
+                                              "cuda_graph", "kernels_per_step", "parallelism")}
             torch.cuda.empty_cache()
 
     cpu = None

@@ -613,6 +613,43 @@ class RoutedExperts(torch.autograd.Function):
         return dx, dw, dw1, dw2, None, None
 
 
+def graph_kernel_counts(graph: "torch.cuda.CUDAGraph") -> Optional[dict]:
+    """Kernel nodes of a captured graph (made with ``keep_graph=True`` and not yet
+    instantiated): ``total``, and ``ours``, those of this library (kernels named in
+    namespace ``moe``).  One replay launches exactly these.  None when the driver
+    bindings cannot tell (nothing is guessed)."""
+    try:
+        from cuda.bindings import driver as cu
+
+        ok = cu.CUresult.CUDA_SUCCESS
+        g = cu.CUgraph(graph.raw_cuda_graph())
+        err, _, n = cu.cuGraphGetNodes(g, 0)
+        if err != ok:
+            return None
+        err, nodes, n = cu.cuGraphGetNodes(g, n)
+        if err != ok:
+            return None
+        total = ours = 0
+        for node in nodes[:n]:
+            err, kind = cu.cuGraphNodeGetType(node)
+            if err != ok:
+                return None
+            if kind != cu.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+                continue
+            total += 1
+            err, prm = cu.cuGraphKernelNodeGetParams(node)
+            if err != ok or int(prm.func) == 0:
+                return None
+            err, name = cu.cuFuncGetName(prm.func)
+            if err != ok:
+                return None
+            if bytes(name).startswith(b"_ZN3moe"):
+                ours += 1
+        return {"total": total, "ours": ours}
+    except Exception:  # bindings absent or a different API shape: no count
+        return None
+
+
 class TrainStepGraph:
     """One training step of ``layer`` (forward_autograd + backward) as a CUDA graph.
 
@@ -648,12 +685,14 @@ class TrainStepGraph:
         torch.cuda.synchronize(layer.device)
         self._clear_grads()
         e0 = disp.last_epoch
-        self.graph = torch.cuda.CUDAGraph()
+        self.graph = torch.cuda.CUDAGraph(keep_graph=True)
         with torch.cuda.graph(self.graph):
             self.out, self.probs, self.topk_idx = layer.forward_autograd(x)
             self.out.backward(dout)
         if (disp.last_epoch - e0) % 2 != 0:
             raise RuntimeError("a captured training step must hold an even number of dispatches")
+        self.kernel_counts = graph_kernel_counts(self.graph)  # kernels per replay
+        self.graph.instantiate()
 
     def _clear_grads(self) -> None:
         for p in self.params:
@@ -691,9 +730,11 @@ class ForwardGraph:
                 layer(x, routing=routing)
         cur.wait_stream(side)
         torch.cuda.synchronize(layer.device)
-        self.graph = torch.cuda.CUDAGraph()
+        self.graph = torch.cuda.CUDAGraph(keep_graph=True)
         with torch.cuda.graph(self.graph):
             self.out, _ = layer(x, routing=routing)
+        self.kernel_counts = graph_kernel_counts(self.graph)  # kernels per replay
+        self.graph.instantiate()
 
     def replay(self) -> None:
         self.graph.replay()

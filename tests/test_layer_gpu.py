@@ -134,6 +134,11 @@ def test_forward_graph_replays_the_eager_forward(cuda_device):
         fg.replay()
         torch.cuda.synchronize()
         assert torch.equal(fg.out, want[i]), rep
+    # The captured graph's kernels, counted by name: four chunks, each with at least
+    # its two GEMMs and its exchange kernels from this library, beside torch's own.
+    kc = fg.kernel_counts
+    assert kc is not None
+    assert 4 * 2 <= kc["ours"] <= kc["total"]
     layer.close()
 
 
