@@ -134,18 +134,25 @@ __device__ __forceinline__ bool issue_tile(Ctrl* ctrl, uint8_t* sA, uint8_t* sB,
                                            const volatile int* abort_flag, bool& issued_any) {
   constexpr uint32_t idesc = SWAPPED ? idesc_f16(BF16, BM, BM_CTA, B_MN_MAJOR, false)
                                      : idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
+  // This thread's loop is on the critical path and shares its SM sub-partition with
+  // two epilogue warps, so every per-stage quantity is formed once per tile and
+  // advanced by constants: the descriptors of stage s differ from stage 0's only in
+  // the start address (bits 0-13, in 16-byte units), the stage barriers are 8 bytes
+  // apart, and mapa keeps offsets within the peer CTA's shared window.  The four
+  // 16-deep steps of a stage add +32 bytes along a K-major row, or +16 rows of 128
+  // bytes down an MN-major slab.  Shared memory ends below 2^18 bytes, so the
+  // start-address field never carries into the next one.
+  const uint64_t adesc_s0 = smem_desc_sw128(smem_u32(sA), 16, 1024);
+  const uint64_t bdesc_s0 = B_MN_MAJOR ? smem_desc_sw128(smem_u32(sB), B_SLAB_BYTES, 1024)
+                                       : smem_desc_sw128(smem_u32(sB), 16, 1024);
+  const uint32_t full_s0 = smem_u32(&ctrl->full[0]);
+  const uint32_t empty_s0 = smem_u32(&ctrl->empty[0]);
+  const uint32_t empty_peer_s0 = mapa_shared(empty_s0, 1);
   for (int kb = 0; kb < num_kb; ++kb) {
-    if (!mbar_wait_cluster(smem_u32(&ctrl->full[stage]), phase, abort_flag)) return false;
+    if (!mbar_wait_cluster(full_s0 + 8u * uint32_t(stage), phase, abort_flag)) return false;
     tc_fence_after();
-    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
-    const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
-    // The descriptors of the four 16-deep steps differ only in the start address
-    // (bits 0-13, in 16-byte units): +32 bytes per step along a K-major row, +16
-    // rows of 128 bytes per step down an MN-major slab.  Stage buffers end well
-    // below 2^18 bytes, so the field never carries into the next one.
-    const uint64_t adesc0 = smem_desc_sw128(a_base, 16, 1024);
-    const uint64_t bdesc0 = B_MN_MAJOR ? smem_desc_sw128(b_base, B_SLAB_BYTES, 1024)
-                                       : smem_desc_sw128(b_base, 16, 1024);
+    const uint64_t adesc0 = adesc_s0 + uint64_t(uint32_t(stage) * (A_STAGE_BYTES >> 4));
+    const uint64_t bdesc0 = bdesc_s0 + uint64_t(uint32_t(stage) * (B_STAGE_BYTES >> 4));
 #pragma unroll
     for (int kk = 0; kk < BK / UMMA_K; ++kk) {
       const uint64_t adesc = adesc0 + uint64_t(kk * (UMMA_K * 2 / 16));
@@ -156,9 +163,8 @@ __device__ __forceinline__ bool issue_tile(Ctrl* ctrl, uint8_t* sA, uint8_t* sB,
         umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
     }
     issued_any = true;
-    const uint32_t e_local = smem_u32(&ctrl->empty[stage]);
-    umma_commit_pair(e_local);
-    umma_commit_pair(mapa_shared(e_local, 1));
+    umma_commit_pair(empty_s0 + 8u * uint32_t(stage));
+    umma_commit_pair(empty_peer_s0 + 8u * uint32_t(stage));
     if (++stage == STAGES) {
       stage = 0;
       phase ^= 1;
