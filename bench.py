@@ -1090,6 +1090,59 @@ def cublas_same_shape(run: GemmRun, steps: int, warmup: int) -> dict:
     return {"form": form, "tflops": round(run.flops / (ms / 1e3) / 1e12, 2), "ms_per_launch": round(ms, 5)}
 
 
+# The reference checkout installed unmodified (git-ignored; it travels to the GPU box).
+REF_DIR = REPO / "baseline" / "_ref"
+
+
+def triton_reference(run: GemmRun, steps: int, warmup: int) -> dict:
+    """The reference's own GPU kernel on this workload, timed like the grouped GEMM:
+    ``persistent_grouped_gemm`` of src/triton_grouped_gemm.py:326-443 (Triton, JIT-built
+    on the box), with num_sms = the SM count, this workload's schedule (striped for
+    config 2, the atomic queue for config 3) and the reference's default 128x128x32
+    tiles.  Its output is checked against ours first.  A same-box comparison point,
+    not the product path; when the module is absent or fails, the reason is reported."""
+    import torch
+
+    if not (REF_DIR / "triton_grouped_gemm.py").exists():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    try:
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        import triton_grouped_gemm as ref
+
+        ctr = torch.zeros(1, dtype=torch.int32, device=run.device)
+
+        def fn():
+            return ref.persistent_grouped_gemm(run.a, run.b, run.off, num_sms=run.sm_count,
+                                               use_atomic_queue=run.wl["atomic"], work_counter=ctr)
+
+        out = None
+        for _ in range(max(3, warmup)):  # the first call JIT-compiles the kernel
+            out = fn()
+            run.flush.fill_(1)
+        ours = run.step()
+        torch.cuda.synchronize(run.device)
+        diff = float((out.float() - ours.float()).abs().max().item())
+        del ours
+        evs = []
+        for i in range(steps):
+            run.flush.fill_(i & 0xFF)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(run.stream)
+            fn()
+            s1.record(run.stream)
+            evs.append((s0, s1))
+        torch.cuda.synchronize(run.device)
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        return {"kernel": "reference persistent_grouped_gemm (Triton), "
+                          f"{'atomic' if run.wl['atomic'] else 'striped'} schedule, "
+                          f"num_sms={run.sm_count}, 128x128x32 tiles",
+                "tflops": round(run.flops / (ms / 1e3) / 1e12, 2), "ms_per_launch": round(ms, 5),
+                "max_abs_diff_vs_ours": diff}
+    except Exception as exc:  # reported, never timed
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:240]}
+
+
 def measure_e2e(run: GemmRun, steps: int, warmup: int, world: int) -> dict:
     """The headline metric end to end through ``persistent_grouped_gemm``.
 
@@ -1221,6 +1274,11 @@ def main() -> None:
     lib_ref = cublas_same_shape(run, args.steps, args.warmup)
     lib_ref["ours_over_cublas"] = round(roofline["achieved"] / lib_ref["tflops"], 4)
     roofline["cublas_same_shape"] = lib_ref
+    if not args.no_extras:
+        tri = triton_reference(run, args.steps, args.warmup)
+        if "tflops" in tri:
+            tri["ours_over_triton"] = round(roofline["achieved"] / tri["tflops"], 4)
+        roofline["triton_reference"] = tri
     run.release()
     torch.cuda.empty_cache()
 
@@ -1241,6 +1299,10 @@ def main() -> None:
         lib3 = cublas_same_shape(r3, args.steps, args.warmup)
         lib3["ours_over_cublas"] = round(extras["gemm_cfg3"]["roofline"]["achieved"] / lib3["tflops"], 4)
         extras["gemm_cfg3"]["roofline"]["cublas_same_shape"] = lib3
+        tri3 = triton_reference(r3, args.steps, args.warmup)
+        if "tflops" in tri3:
+            tri3["ours_over_triton"] = round(extras["gemm_cfg3"]["roofline"]["achieved"] / tri3["tflops"], 4)
+        extras["gemm_cfg3"]["roofline"]["triton_reference"] = tri3
         r3.release()
         del r3
         torch.cuda.empty_cache()

@@ -140,3 +140,11 @@ def test_torch_loop_restatement_matches_the_numpy_oracle():
     assert loop_flops(a.shape, b.shape, off.tolist()) == 2 * sum(counts) * 256 * 192
     assert loop_flops(a.shape, b.shape, off.tolist(), [2]) == 2 * 129 * 256 * 192
     del torch
+
+
+def test_triton_reference_leg_reports_an_absent_install(monkeypatch, tmp_path):
+    """Without the reference installed under baseline/_ref the Triton comparison is
+    reported unavailable with its reason, never timed."""
+    monkeypatch.setattr(bench, "REF_DIR", tmp_path / "absent")
+    got = bench.triton_reference(run=None, steps=1, warmup=1)
+    assert set(got) == {"unavailable"} and "baseline/_ref" in got["unavailable"]
