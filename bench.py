@@ -1274,7 +1274,9 @@ def main() -> None:
     lib_ref = cublas_same_shape(run, args.steps, args.warmup)
     lib_ref["ours_over_cublas"] = round(roofline["achieved"] / lib_ref["tflops"], 4)
     roofline["cublas_same_shape"] = lib_ref
-    if not args.no_extras:
+    # The reference's Triton kernel beside ours on one GPU (a per-GPU comparison; at N > 1
+    # every rank would JIT-build it into the same cache at once).
+    if not args.no_extras and world == 1:
         tri = triton_reference(run, args.steps, args.warmup)
         if "tflops" in tri:
             tri["ours_over_triton"] = round(roofline["achieved"] / tri["tflops"], 4)
@@ -1299,10 +1301,12 @@ def main() -> None:
         lib3 = cublas_same_shape(r3, args.steps, args.warmup)
         lib3["ours_over_cublas"] = round(extras["gemm_cfg3"]["roofline"]["achieved"] / lib3["tflops"], 4)
         extras["gemm_cfg3"]["roofline"]["cublas_same_shape"] = lib3
-        tri3 = triton_reference(r3, args.steps, args.warmup)
-        if "tflops" in tri3:
-            tri3["ours_over_triton"] = round(extras["gemm_cfg3"]["roofline"]["achieved"] / tri3["tflops"], 4)
-        extras["gemm_cfg3"]["roofline"]["triton_reference"] = tri3
+        if world == 1:
+            tri3 = triton_reference(r3, args.steps, args.warmup)
+            if "tflops" in tri3:
+                tri3["ours_over_triton"] = round(extras["gemm_cfg3"]["roofline"]["achieved"]
+                                                 / tri3["tflops"], 4)
+            extras["gemm_cfg3"]["roofline"]["triton_reference"] = tri3
         r3.release()
         del r3
         torch.cuda.empty_cache()
