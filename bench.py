@@ -732,6 +732,11 @@ def measure_layer(args, name: str, rank: int, world: int, device, group, steps: 
     }
     if marks_by_rank is not None:
         result["timeline_ms"] = {f"rank{r}": m for r, m in enumerate(marks_by_rank)}
+    if world == 1 and not getattr(args, "no_extras", False):
+        ref = reference_layer(layer, x, device)
+        if "ms_per_step" in ref:
+            ref["ours_over_reference"] = round(ref["ms_per_step"] / step_ms, 2)
+        result["reference_layer"] = ref
     layer.close()
     return result
 
@@ -1092,6 +1097,61 @@ def cublas_same_shape(run: GemmRun, steps: int, warmup: int) -> dict:
 
 # The reference checkout installed unmodified (git-ignored; it travels to the GPU box).
 REF_DIR = REPO / "baseline" / "_ref"
+
+
+def reference_layer(layer, x, device, steps: int = 5) -> dict:
+    """The reference's own MoE layer forward on the same tokens and GPU: ``SimpleMoE``
+    (src/train_moe_baseline.py:112-441) on its single-GPU path, with no exchange and
+    the Triton grouped GEMMs of src/triton_grouped_gemm.py, under torch.inference_mode
+    as the reference runs it.  The harness fixes what the reference leaves to its
+    command line or to an A100: no shared experts, the device's SM count for the GEMMs
+    (the reference derives 108 - deepep_num_sms), and this layer's gate weights and
+    bias copied in so that both route alike.  Each forward is timed with CUDA events
+    around the whole call, host synchronisations included, as a user of the reference
+    sees it.  Context for the layer line, not the product path."""
+    import torch
+
+    if not (REF_DIR / "train_moe_baseline.py").exists():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    ref = None
+    try:
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        import train_moe_baseline as tmb
+
+        H, E = layer.hidden, layer.num_experts
+        ref = tmb.SimpleMoE(H, layer.ffn, E, 0, layer.top_k, ep_group=None, comm_backend="local",
+                            micro_batch_size=layer.micro, expert_kernel="triton")
+        ref = ref.to(device=device, dtype=torch.bfloat16)
+        ref.triton_num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+        with torch.no_grad():
+            gate = torch.nn.Linear(H, E, bias=layer.router_b is not None).to(device=device,
+                                                                           dtype=torch.bfloat16)
+            gate.weight.copy_(layer.router_w)
+            if layer.router_b is not None:
+                gate.bias.copy_(layer.router_b.to(torch.bfloat16))
+            ref.router = gate
+        with torch.inference_mode():
+            for _ in range(2):
+                ref(x)
+            torch.cuda.synchronize(device)
+            evs = []
+            for _ in range(steps):
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                ref(x)
+                s1.record()
+                evs.append((s0, s1))
+            torch.cuda.synchronize(device)
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        return {"impl": "reference SimpleMoE forward, single-GPU path, Triton grouped GEMMs",
+                "tokens_per_s": round(x.shape[0] / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+                "steps": steps}
+    except Exception as exc:  # reported, never timed
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:240]}
+    finally:
+        del ref
+        torch.cuda.empty_cache()
 
 
 def triton_reference(run: GemmRun, steps: int, warmup: int) -> dict:

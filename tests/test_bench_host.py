@@ -148,3 +148,9 @@ def test_triton_reference_leg_reports_an_absent_install(monkeypatch, tmp_path):
     monkeypatch.setattr(bench, "REF_DIR", tmp_path / "absent")
     got = bench.triton_reference(run=None, steps=1, warmup=1)
     assert set(got) == {"unavailable"} and "baseline/_ref" in got["unavailable"]
+
+
+def test_reference_layer_leg_reports_an_absent_install(monkeypatch, tmp_path):
+    monkeypatch.setattr(bench, "REF_DIR", tmp_path / "absent")
+    got = bench.reference_layer(layer=None, x=None, device=None)
+    assert set(got) == {"unavailable"} and "baseline/_ref" in got["unavailable"]
