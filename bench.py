@@ -203,13 +203,14 @@ def rows_computed(counts) -> int:
     """Rows the CTA-pair GEMM multiplies for these expert counts (tensor work incl. padding).
 
     Every expert's rows are cut into 256-row pair tiles; a last tile of at most
-    128 rows runs swapped (the weights take the MMA's 256-row side and the tile's
-    rows a 128-wide N), so it costs 128 rows; a longer last tile costs 256.
+    224 rows runs swapped (the weights take the MMA's 256-row side and the tile's
+    rows its N side, rounded up to 16), so it costs its rows rounded up to 16; a
+    longer last tile costs 256.
     """
     total = 0
     for c in counts:
         full, tail = divmod(int(c), 256)
-        total += 256 * full + (0 if tail == 0 else (128 if tail <= 128 else 256))
+        total += 256 * full + (0 if tail == 0 else ((tail + 15) // 16 * 16 if tail <= 224 else 256))
     return total
 
 

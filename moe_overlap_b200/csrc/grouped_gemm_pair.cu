@@ -23,14 +23,14 @@
 //            quadrant and every SM sub-partition runs two epilogue warps.  Each
 //            warp stages 32x32 bf16 chunks in its own 2 KiB of shared memory and
 //            writes them with TMA bulk stores (rows inside the tile's expert only).
-// Swapped tails: a tile of at most 128 rows (an expert's last rows) would leave
-// the second CTA's 128 rows of a 256-row MMA empty.  With swap_tails such a tile
-// is computed transposed instead: the 256 weight columns take the MMA's M side
-// (128 per CTA, the same B stage as usual, now the MMA's A operand) and the tile's
-// rows its N side (N = 128: 64 rows from each CTA, loaded through a 64-row map), so
-// the tensor work of the tile halves and its A traffic too.  Each CTA's TMEM then holds its 128 output columns in its
-// lanes and the tile's rows in 128 accumulator columns; the epilogue stores
-// them transposed (plain or GELU epilogues only).
+// Swapped tails: a tile of at most 224 rows (an expert's last rows) would leave part
+// of a 256-row MMA empty.  With swap_tails such a tile is computed transposed
+// instead: the 256 weight columns take the MMA's M side (128 per CTA, the same B
+// stage as usual, now the MMA's A operand) and the tile's rows its N side, N the
+// rows rounded up to 16 (N/2 rows from each CTA, through a 64-row map when N <= 128),
+// so the tensor work follows the rows.  Each CTA's TMEM then holds its 128 output
+// columns in its lanes and the tile's rows in N accumulator columns; the epilogue
+// stores them transposed (plain or GELU epilogues only).
 // No load uses cluster multicast; the pair exchanges only barrier arrivals and
 // the tile ring entries through shared::cluster addresses.
 #include <algorithm>
@@ -60,8 +60,11 @@ constexpr int A_STAGE_BYTES = BM_CTA * BK * 2;  // 16 KiB
 constexpr int B_STAGE_BYTES = BK * BN_CTA * 2;  // 16 KiB
 constexpr int B_SLAB_BYTES = BK * 64 * 2;       // one 64-column slab of an N-major B stage
 constexpr uint32_t PAIR_TX_BYTES = 2 * (A_STAGE_BYTES + B_STAGE_BYTES);
-// A swapped tile loads only the 64 rows per CTA that its MMA reads.
+// A swapped tile of at most 128 rows loads only the 64 rows per CTA that its MMA can read.
 constexpr uint32_t PAIR_TX_BYTES_SWAPPED = 2 * (A_STAGE_BYTES / 2 + B_STAGE_BYTES);
+// Tiles of at most this many rows run swapped (above it the N side would be within 32
+// rows of a full tile's tensor work and its epilogue is the slower one).
+constexpr int SWAP_MAX_ROWS = 224;
 constexpr int EPI_STAGE_BYTES = 32 * 32 * 2;  // one 32x32 bf16 chunk per epilogue warp
 constexpr uint32_t TMEM_COLS = 2 * BN;
 
@@ -83,14 +86,23 @@ __host__ __device__ constexpr size_t smem_bytes(int num_experts) {
          ((sizeof(Ctrl) + 15) / 16) * 16 + size_t(3) * 4 * (num_experts + 1);
 }
 
+// A tile of at most SWAP_MAX_ROWS rows (an expert's last rows) is computed swapped:
+// the 256 weight columns take the MMA's M side and the tile's rows its N side, N the
+// rows rounded up to 16 (the N granularity with M = 256), so the tensor work follows
+// the rows.  Returns that N, or 0 for a tile computed the usual way.
+__device__ __forceinline__ int swapped_n(const Params& p, int rows) {
+  return (p.swap_tails && rows <= SWAP_MAX_ROWS) ? (rows + 15) & ~15 : 0;
+}
+
 // Epilogue of a swapped tile: TMEM lane (32*quad + lane) of this CTA holds output
 // column n_cta + 32*quad + lane, accumulator column j the tile's row j.  The warp
-// covers rows [r_first, r_first + 64) in two 32-row chunks; lane pairs swap values
+// covers rows [r_first, r_end) in 32-row chunks; lane pairs swap values
 // so that each thread stores two adjacent columns of one row (4 bytes), and the
 // 32 lanes of a warp store 64 contiguous bytes of a row per instruction.
 template <bool BF16>
 __device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, int quad, int row0,
-                                              int rows, int r_first, int n_cta, const Params& p) {
+                                              int rows, int r_first, int r_end, int n_cta,
+                                              const Params& p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int col = n_cta + quad * 32 + lane;
   const bool odd = (lane & 1) != 0;
@@ -98,9 +110,7 @@ __device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, in
   const bool col_ok = pair_col < p.n;        // n is a multiple of 8: col + 1 < n as well
   const bool gelu = p.activation == MOE_ACT_GELU;
 #pragma unroll 1
-  for (int ch = 0; ch < 2; ++ch) {
-    const int rbase = r_first + 32 * ch;
-    if (rbase >= rows) break;  // warp-uniform
+  for (int rbase = r_first; rbase < r_end && rbase < rows; rbase += 32) {  // warp-uniform
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_lane_base + uint32_t(rbase), r);
     tmem_wait_ld();
@@ -126,14 +136,15 @@ __device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, in
 // The MMA issuer's k-block loop for one tile (leader CTA, one thread): waits for
 // each stage's data, issues its four 16-deep MMAs into the accumulator at d_tmem
 // and commits the stage back to both CTAs' producers.  SWAPPED issues the swapped
-// form (B stage as the MMA's A operand with M = 256, the A stage's first 64 rows
-// as its B operand with N = 128).  Returns false when a wait gave up.
+// form (B stage as the MMA's A operand with M = 256, the A stage's first N/2 rows
+// as its B operand, N and the operand layouts in idesc_sw).  Returns false when a
+// wait gave up.
 template <bool BF16, bool B_MN_MAJOR, bool SWAPPED>
 __device__ __forceinline__ bool issue_tile(Ctrl* ctrl, uint8_t* sA, uint8_t* sB, uint32_t d_tmem,
                                            int num_kb, int& stage, uint32_t& phase,
-                                           const volatile int* abort_flag, bool& issued_any) {
-  constexpr uint32_t idesc = SWAPPED ? idesc_f16(BF16, BM, BM_CTA, B_MN_MAJOR, false)
-                                     : idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
+                                           const volatile int* abort_flag, bool& issued_any,
+                                           uint32_t idesc_sw) {
+  const uint32_t idesc = SWAPPED ? idesc_sw : idesc_f16(BF16, BM, BN, false, B_MN_MAJOR);
   // This thread's loop is on the critical path and shares its SM sub-partition with
   // two epilogue warps, so every per-stage quantity is formed once per tile and
   // advanced by constants: the descriptors of stage s differ from stage 0's only in
@@ -296,12 +307,15 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
           }
           ready_expert = s.w;
         }
-        // A swapped tile takes 64 rows from each CTA (the MMA's N side), loaded
-        // through the 64-row map into the first half of the A stage.
-        const bool swapped = p.swap_tails && s.y <= BM_CTA;
-        const int row_a = s.x + static_cast<int>(crank) * (swapped ? BM_CTA / 2 : BM_CTA);
-        const CUtensorMap* map_a = swapped ? &tmap_a_half : &tmap_a;
-        const uint32_t stage_tx = swapped ? PAIR_TX_BYTES_SWAPPED : PAIR_TX_BYTES;
+        // A swapped tile of N rows takes N/2 of them from each CTA (the MMA's N side),
+        // CTA c from row c*N/2, through the 64-row map into the first half of the A
+        // stage when N/2 <= 64, else through the usual 128-row map; the MMA reads only
+        // the first N/2 rows of each stage.
+        const int n_sw = swapped_n(p, s.y);
+        const bool half_box = n_sw > 0 && n_sw <= BM_CTA;
+        const int row_a = s.x + static_cast<int>(crank) * (n_sw > 0 ? n_sw / 2 : BM_CTA);
+        const CUtensorMap* map_a = half_box ? &tmap_a_half : &tmap_a;
+        const uint32_t stage_tx = half_box ? PAIR_TX_BYTES_SWAPPED : PAIR_TX_BYTES;
         const int n_b = s.z + static_cast<int>(crank) * BN_CTA;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(smem_u32(&ctrl->empty[stage]), phase ^ 1, abort_flag)) {
@@ -366,13 +380,15 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        const bool swapped = p.swap_tails && s.y <= BM_CTA;
+        const int n_sw = swapped_n(p, s.y);
         // Two instantiations of the k-block loop, so that the usual tile's loop
         // carries no per-MMA choice between the two operand arrangements.
-        const bool ok = swapped ? issue_tile<BF16, B_MN_MAJOR, true>(ctrl, sA, sB, d_tmem, num_kb, stage,
-                                                                   phase, abort_flag, issued_any)
-                                : issue_tile<BF16, B_MN_MAJOR, false>(ctrl, sA, sB, d_tmem, num_kb, stage,
-                                                                    phase, abort_flag, issued_any);
+        const bool ok =
+            n_sw > 0 ? issue_tile<BF16, B_MN_MAJOR, true>(ctrl, sA, sB, d_tmem, num_kb, stage, phase,
+                                                          abort_flag, issued_any,
+                                                          idesc_f16(BF16, BM, n_sw, B_MN_MAJOR, false))
+                     : issue_tile<BF16, B_MN_MAJOR, false>(ctrl, sA, sB, d_tmem, num_kb, stage, phase,
+                                                           abort_flag, issued_any, 0u);
         if (!ok) failed = true;
         if (failed) break;
         const uint32_t tf_local = smem_u32(&ctrl->tfull[acc]);
@@ -421,9 +437,13 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kMaxRegs)
         break;
       }
       tc_fence_after();
-      if (!PUSH && p.swap_tails && s.y <= BM_CTA) {
+      const int n_sw = PUSH ? 0 : swapped_n(p, s.y);
+      if (n_sw > 0) {
+        // The two warps of a lane quadrant split the tile's rows in 32-row chunks.
+        const int half = ((n_sw / 2) + 31) & ~31;
         store_swapped<BF16>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), lane, quad,
-                            s.x, s.y, col_half * 64, s.z + static_cast<int>(crank) * BN_CTA, p);
+                            s.x, s.y, col_half * half, col_half * half + half,
+                            s.z + static_cast<int>(crank) * BN_CTA, p);
       } else {
       const int rows_here = min(int(BM_CTA), max(0, s.y - static_cast<int>(crank) * int(BM_CTA)));
       store_accumulator<BF16, PUSH>(tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN), quad,

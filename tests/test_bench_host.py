@@ -115,9 +115,10 @@ def test_both_arms_print_the_same_gemm_config():
 
 def test_rows_computed_counts_pair_tiles():
     assert bench.rows_computed([512] * 16) == 8192
-    assert bench.rows_computed([1, 0, 257]) == 128 + 256 + 128
-    assert bench.rows_computed([129, 384]) == 256 + 384
-    assert bench.rows_computed(bench.workload_counts("gemm_cfg3")) == 17280
+    assert bench.rows_computed([1, 0, 257]) == 16 + 256 + 16
+    assert bench.rows_computed([129, 384]) == 144 + 256 + 128
+    assert bench.rows_computed([224, 225]) == 224 + 256
+    assert bench.rows_computed(bench.workload_counts("gemm_cfg3")) == 16544
 
 
 def test_torch_loop_restatement_matches_the_numpy_oracle():

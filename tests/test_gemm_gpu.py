@@ -55,6 +55,10 @@ CASES = [
     ("one_expert_bf16", [1000], 256, 264, "bf16", 148, True),
     ("k_pad_70", [10, 20, 0, 33], 70, 24, "bf16", 148, False),
     ("n_pad_30", [10, 20], 64, 30, "f16", 148, True),
+    # last tiles on both sides of every swap boundary: N = rows rounded up to 16 from
+    # 1 to 224 rows (64-row A box up to 128 rows, the full box above), full tiles above
+    ("swap_boundaries", [16, 17, 112, 113, 127, 128, 129, 143, 144, 145, 200, 223, 224, 225,
+                         240, 255, 256, 257, 481], 128, 264, "bf16", 148, True),
 ]
 
 
@@ -102,7 +106,7 @@ def test_rows_past_last_offset_untouched_and_int64_offsets(cuda_device):
 
 
 def test_fused_gelu_matches_oracle(cuda_device):
-    counts = [100, 0, 257, 31]
+    counts = [100, 0, 257, 31, 150, 224, 473]
     a, b, off = gemm_inputs(counts, 512, 384, "bf16", seed=5, w_std=0.05)
     c = mo.grouped_gemm(a.to(cuda_device), b.to(cuda_device), off.to(cuda_device),
                         activation="gelu")
