@@ -54,7 +54,7 @@ struct Params {
   void* aux_out;           // aux_out[row, col] = v (before the activation)
   int64_t ld_aux;
   int c_tma;               // the CTA-pair kernel may store C through its TMA store map
-  int swap_tails;          // the CTA-pair kernel computes tiles of <= 128 rows swapped
+  int swap_tails;          // the CTA-pair kernel computes tiles of <= 224 rows swapped
   PushTarget push;         // combine push instead of C (push.src != null)
   ArrivalWait arrival;     // arrival.arrived != null: wait for each expert's rows
 };
@@ -314,7 +314,7 @@ int grouped_gemm_launch(const void* a, int64_t lda, const void* b, int64_t b_str
                         const PushTarget* push, const ArrivalWait* arrival = nullptr);
 
 // Launches the 2-SM (CTA pair) kernel; grid must be even.  `ta_half` is A's map with
-// 64-row boxes (the rows a swapped tile reads per CTA); `tc` is the 2-D {N, m_total}
+// 64-row boxes (the rows a swapped tile of N <= 128 reads per CTA); `tc` is the 2-D {N, m_total}
 // store map of C (32x32 boxes, 64-byte swizzle), used when p.c_tma is set.
 // Returns a MOE_* code.
 int launch_pair_kernel(bool bf16, bool b_mn, const CUtensorMap& ta, const CUtensorMap& ta_half,

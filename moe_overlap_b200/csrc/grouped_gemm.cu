@@ -355,7 +355,7 @@ static bool gemm_tma_store() {
 }
 
 // MOE_B200_GEMM_SWAP=0 computes every tile of the CTA-pair kernel as 256 rows
-// (default 1: tiles of at most 128 rows run swapped, see grouped_gemm_pair.cu).
+// (default 1: tiles of at most 224 rows run swapped, see grouped_gemm_pair.cu).
 static bool gemm_swap_tails() {
   static const bool v = [] {
     const char* e = std::getenv("MOE_B200_GEMM_SWAP");
@@ -467,7 +467,7 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
     const uint64_t strides[1] = {uint64_t(lda) * 2};
     const uint32_t box[2] = {BK, BM};
     if (int rc = encode_tiled(&ta, dt, 2, a, dims, strides, box); rc != MOE_OK) return rc;
-    const uint32_t box_half[2] = {BK, BM / 2};  // the 64 rows a swapped pair tile reads per CTA
+    const uint32_t box_half[2] = {BK, BM / 2};  // the <= 64 rows a swapped tile of N <= 128 reads per CTA
     if (int rc = encode_tiled(&ta_half, dt, 2, a, dims, strides, box_half); rc != MOE_OK) return rc;
   }
   {
@@ -505,7 +505,7 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
   p.ld_aux = ld_aux;
   p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0, nullptr};
   p.arrival = arrival != nullptr ? *arrival : ArrivalWait{nullptr, nullptr, 0};
-  // Tiles of at most 128 rows (an expert's tail) run swapped on the CTA pair when
+  // Tiles of at most 224 rows (an expert's tail) run swapped on the CTA pair when
   // the epilogue is elementwise on the product alone (no row scale, auxiliary
   // operands or combine push).
   p.swap_tails = use_pair && gemm_swap_tails() && !pushing && row_scale == nullptr &&
