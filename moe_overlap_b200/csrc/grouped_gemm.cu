@@ -505,12 +505,9 @@ int moe::gg::grouped_gemm_launch(const void* a, int64_t lda, const void* b, int6
   p.ld_aux = ld_aux;
   p.push = pushing ? *push : PushTarget{nullptr, nullptr, nullptr, 0, nullptr};
   p.arrival = arrival != nullptr ? *arrival : ArrivalWait{nullptr, nullptr, 0};
-  // Tiles of at most 224 rows (an expert's tail) run swapped on the CTA pair when
-  // the epilogue is elementwise on the product alone (no row scale, auxiliary
-  // operands or combine push).
-  p.swap_tails = use_pair && gemm_swap_tails() && !pushing && row_scale == nullptr &&
-                 aux_in == nullptr && aux_out == nullptr &&
-                 (activation == MOE_ACT_NONE || activation == MOE_ACT_GELU);
+  // Tiles of at most 224 rows (an expert's tail) run swapped on the CTA pair with
+  // every epilogue but the combine push, whose rows go to their source ranks.
+  p.swap_tails = use_pair && gemm_swap_tails() && !pushing;
 
   // The pair kernel stores C through a {N, m_total} map in 32x32 boxes (64-byte swizzle).
   CUtensorMap tc;

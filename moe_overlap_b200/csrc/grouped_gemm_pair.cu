@@ -96,9 +96,12 @@ __device__ __forceinline__ int swapped_n(const Params& p, int rows) {
 
 // Epilogue of a swapped tile: TMEM lane (32*quad + lane) of this CTA holds output
 // column n_cta + 32*quad + lane, accumulator column j the tile's row j.  The warp
-// covers rows [r_first, r_end) in 32-row chunks; lane pairs swap values
-// so that each thread stores two adjacent columns of one row (4 bytes), and the
-// 32 lanes of a warp store 64 contiguous bytes of a row per instruction.
+// covers rows [r_first, r_end) in 32-row chunks and applies, per element, the same
+// float operations in the same order as store_accumulator (row scale, derivative or
+// pre-activation to aux_out, GELU or the multiply by aux_in), so a swapped tile's
+// outputs equal an unswapped one's bit for bit.  Lane pairs swap values so that each
+// thread stores two adjacent columns of one row (4 bytes) of C and of aux_out, and
+// the 32 lanes of a warp store 64 contiguous bytes of a row per instruction.
 template <bool BF16>
 __device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, int quad, int row0,
                                               int rows, int r_first, int r_end, int n_cta,
@@ -108,27 +111,66 @@ __device__ __forceinline__ void store_swapped(uint32_t t_lane_base, int lane, in
   const bool odd = (lane & 1) != 0;
   const int pair_col = col - (odd ? 1 : 0);  // first column of the pair this thread stores
   const bool col_ok = pair_col < p.n;        // n is a multiple of 8: col + 1 < n as well
-  const bool gelu = p.activation == MOE_ACT_GELU;
+  const int act = p.activation;
+  const bool save_grad = act == MOE_ACT_GELU_SAVE_GRAD;
+  const bool pre_out = !save_grad && p.aux_out != nullptr;  // aux_out = pre-activation
+  const bool with_aux_out = save_grad || pre_out;
+  const bool dgelu = act == MOE_ACT_DGELU || act == MOE_ACT_MUL_AUX;
+  const bool aux_is_grad = act == MOE_ACT_MUL_AUX;
 #pragma unroll 1
   for (int rbase = r_first; rbase < r_end && rbase < rows; rbase += 32) {  // warp-uniform
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_lane_base + uint32_t(rbase), r);
+    // This chunk's row scales, one row per lane, broadcast to every lane below.
+    const float rs_lane = (p.row_scale != nullptr && rbase + lane < rows)
+                              ? p.row_scale[int64_t(row0) + rbase + lane]
+                              : 1.0f;
     tmem_wait_ld();
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-      float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
-      if (gelu) {
-        v0 = gelu_erf(v0);
-        v1 = gelu_erf(v1);
+      float v[2], g[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int rr_u = rbase + j + u;
+        float x = __uint_as_float(r[j + u]) * __shfl_sync(0xffffffffu, rs_lane, j + u);
+        g[u] = 0.0f;
+        if (save_grad) {
+          const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+          g[u] = cdf + x * (0.39894228040143267794f * expf(-0.5f * x * x));
+          x = x * cdf;
+        } else if (pre_out) {
+          g[u] = x;
+        }
+        if (act == MOE_ACT_GELU) {
+          x = gelu_erf(x);
+        } else if (dgelu) {
+          float f = 0.0f;
+          if (col < p.n && rr_u < rows) {
+            const T h = reinterpret_cast<const T*>(p.aux_in)[(int64_t(row0) + rr_u) * p.ld_aux + col];
+            if constexpr (BF16)
+              f = __bfloat162float(h);
+            else
+              f = __half2float(h);
+          }
+          x *= aux_is_grad ? f : gelu_erf_grad(f);
+        }
+        v[u] = x;
       }
       // even lane: row j, columns (col, col+1); odd lane: row j+1, columns (col-1, col)
-      const float mine_other = odd ? v0 : v1;
-      const float theirs = __shfl_xor_sync(0xffffffffu, mine_other, 1);
       const int rr = rbase + j + (odd ? 1 : 0);
-      const uint32_t packed = odd ? pack2<BF16>(theirs, v1) : pack2<BF16>(v0, theirs);
-      if (col_ok && rr < rows)
+      const bool store = col_ok && rr < rows;
+      const float theirs = __shfl_xor_sync(0xffffffffu, odd ? v[0] : v[1], 1);
+      const uint32_t packed = odd ? pack2<BF16>(theirs, v[1]) : pack2<BF16>(v[0], theirs);
+      if (store)
         *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.c) + (int64_t(row0) + rr) * p.ldc +
                                      pair_col) = packed;
+      if (with_aux_out) {  // warp-uniform
+        const float gtheirs = __shfl_xor_sync(0xffffffffu, odd ? g[0] : g[1], 1);
+        const uint32_t gpacked = odd ? pack2<BF16>(gtheirs, g[1]) : pack2<BF16>(g[0], gtheirs);
+        if (store)
+          *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.aux_out) + (int64_t(row0) + rr) * p.ld_aux +
+                                       pair_col) = gpacked;
+      }
     }
   }
 }
